@@ -1,0 +1,68 @@
+"""Acceptance + KMP re-alignment (host side of subsystem 3).
+
+One kernel launch per verification step handles every packed block with one
+warp each: the reference's per-block Python loop body
+(hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py D:1103-1336) at the default
+exact-match thresholds.  Block state lives in an int32 tensor with the field
+order of ``hsd_block_t``; results come back as ``hsd_block_result_t`` rows.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _native as N
+
+BLOCK_FIELDS = [f for f, _ in N.Block._fields_]
+RESULT_FIELDS = [f for f, _ in N.BlockResult._fields_]
+F = {name: i for i, name in enumerate(BLOCK_FIELDS)}
+R = {name: i for i, name in enumerate(RESULT_FIELDS)}
+
+DOTS_SENTINEL = 20993     # D:1306
+HUNYUAN_SENTINEL = 41153  # H:1873
+
+
+def make_config(n_blocks, kv_len, q_len, words_stride, eos_ids, match_window_size=3,
+                match_window_size_upper_bound=10, max_spec_len=0,
+                repeat_sentinel=DOTS_SENTINEL):
+    cfg = N.AcceptConfig()
+    cfg.n_blocks = n_blocks
+    cfg.kv_len = kv_len
+    cfg.kv_base = kv_len - q_len
+    cfg.kv_words_stride = words_stride
+    cfg.match_window_size = match_window_size
+    cfg.match_window_size_upper_bound = match_window_size_upper_bound
+    cfg.max_spec_len = max_spec_len
+    cfg.repeat_sentinel = repeat_sentinel
+    eos = list(eos_ids)
+    if len(eos) > 8:
+        raise ValueError("at most 8 EOS ids")
+    cfg.n_eos = len(eos)
+    for i, e in enumerate(eos):
+        cfg.eos_ids[i] = int(e)
+    return cfg
+
+
+def accept_kmp(cfg, blocks, next_ids, input_ids, gen_pool, draft_pool, seg_kv_bits,
+               out_kv_bits, filter_bits, tree_tokens=None, tree_parents=None, results=None,
+               status=None, stream=None):
+    """Launch the acceptance kernel; all tensors are device int32 / int64.
+
+    ``blocks``: int32 ``[n_blocks, 16]`` (updated in place);
+    returns ``results`` int32 ``[n_blocks, 8]``.
+    """
+    lib = N.load()
+    if results is None:
+        results = torch.empty((blocks.shape[0], len(RESULT_FIELDS)), dtype=torch.int32,
+                              device=blocks.device)
+    dummy = None
+    if tree_tokens is None or tree_parents is None:
+        dummy = torch.zeros(1, dtype=torch.int32, device=blocks.device)
+    N.check(lib.hsd_accept_kmp(
+        C.byref(cfg), N.ptr(blocks), N.ptr(results), N.ptr(next_ids), N.ptr(input_ids),
+        N.ptr(gen_pool), N.ptr(draft_pool), N.ptr(tree_tokens if tree_tokens is not None else dummy),
+        N.ptr(tree_parents if tree_parents is not None else dummy), N.ptr(seg_kv_bits),
+        N.ptr(out_kv_bits), N.ptr(filter_bits), N.ptr(status), N.stream_handle(stream)),
+        "hsd_accept_kmp")
+    return results

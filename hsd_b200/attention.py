@@ -1,0 +1,102 @@
+"""Verification attention: the drop-in for the reference's attention hook.
+
+``flex_attention_forward`` keeps the signature and return convention of the
+reference's hook (hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py D:72-135,
+hsd/hunyuan_ocr_pipeline/modeling_hunyuan_vl_hsd.py H:103-180), which the
+patched Qwen2 / HunYuan attention calls per decoder layer (D:378-381,
+H:1039-1042).  It accepts the same dense float mask (converted once per step
+and cached by identity, as D:83-106 caches its BlockMask), a
+:class:`~hsd_b200.plan.PackedMask`, or a prebuilt
+:class:`~hsd_b200.plan.TilePlan`.  Grouped KV heads are consumed directly;
+nothing is expanded the way ``repeat_kv`` (D:137-146) does.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _native as N
+from .plan import PackedMask, TilePlan, plan_from_dense
+
+_cache = {"src": None, "plan": None}
+
+
+def _as_heads(x, name):
+    """[1, H, S, D] or [H, S, D] -> [H, S, D] view (strides kept)."""
+    if x.dim() == 4:
+        if x.shape[0] != 1:
+            raise ValueError(f"{name}: batch must be 1 (packed verification)")
+        x = x[0]
+    if x.dim() != 3:
+        raise ValueError(f"{name}: expected [1, H, S, D] or [H, S, D], got {tuple(x.shape)}")
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"{name}: bf16 required, got {x.dtype}")
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    return x
+
+
+def verify_attention(q, k, v, plan: TilePlan, scale=None, out=None, lse=None,
+                     need_lse=True, stream=None):
+    """Masked GQA attention over a tile plan.
+
+    q: ``[Hq, Q, 128]`` (or ``[1, Hq, Q, 128]``) bf16, any row/head strides;
+    k, v: ``[Hkv, KV, 128]`` likewise.  Returns ``(out [Q, Hq, 128] bf16,
+    lse [Hq, Q] fp32 natural log or None)``.
+    """
+    lib = N.load()
+    q = _as_heads(q, "query")
+    k = _as_heads(k, "key")
+    v = _as_heads(v, "value")
+    hq, q_len, d = q.shape
+    hkv, kv_len = k.shape[0], k.shape[1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    if out is None:
+        out = torch.empty((q_len, hq, d), dtype=torch.bfloat16, device=q.device)
+    if need_lse and lse is None:
+        lse = torch.empty((hq, q_len), dtype=torch.float32, device=q.device)
+    N.check(lib.hsd_verify_attention(
+        N.ptr(q), q.stride(1), q.stride(0), N.ptr(k), k.stride(1), k.stride(0),
+        N.ptr(v), v.stride(1), v.stride(0), N.ptr(out), N.ptr(lse) if need_lse else None,
+        q_len, kv_len, hq, hkv, d, float(scale), C_byref(plan), N.ptr(plan.status),
+        N.stream_handle(stream)), "hsd_verify_attention")
+    return out, lse
+
+
+def C_byref(plan):
+    import ctypes
+    return ctypes.byref(plan.struct)
+
+
+def plan_for(attention_mask, q_len, kv_len):
+    """Tile plan for whatever mask object the caller passed."""
+    if isinstance(attention_mask, TilePlan):
+        return attention_mask
+    if isinstance(attention_mask, PackedMask):
+        return attention_mask.plan()
+    if isinstance(attention_mask, torch.Tensor):
+        if _cache["src"] is attention_mask and _cache["plan"] is not None \
+                and _cache["plan"].kv_len == kv_len:
+            return _cache["plan"]
+        plan = plan_from_dense(attention_mask[..., :kv_len], kv_len)
+        _cache["src"], _cache["plan"] = attention_mask, plan
+        return plan
+    raise TypeError(f"unsupported attention_mask type {type(attention_mask)!r}")
+
+
+def flex_attention_forward(module, query, key, value, attention_mask, scaling=None,
+                           softcap=None, head_mask=None, **kwargs):
+    """Drop-in for the reference's ``flex_attention_forward``.
+
+    Returns ``(attn_output [1, Q, Hq, D] contiguous, lse [1, Hq, Q] in the
+    value dtype)`` like D:131-135.  ``softcap`` and ``head_mask`` are not used
+    by the reference's FlexAttention call either (D:118-130).
+    """
+    if attention_mask is None:
+        raise ValueError("packed verification needs a mask (dense, PackedMask or TilePlan)")
+    q_len, kv_len = query.shape[-2], key.shape[-2]
+    plan = plan_for(attention_mask, q_len, kv_len)
+    out, lse = verify_attention(query, key, value, plan, scale=scaling)
+    return out.unsqueeze(0), lse.to(value.dtype).unsqueeze(0)

@@ -1,0 +1,246 @@
+// (2) KV-cache compaction on the device.
+//
+// The reference compacts with one index_select(-2, keep_indices) per layer
+// and per K/V (D:1705-1722, H:2262-2269), which allocates a new cache and
+// copies every kept row.  Here the cache is compacted in place and only rows
+// that actually move (i >= first_moved) are read and written.
+//
+// In place is safe because keep_idx is ascending, so keep_idx[i] >= i: a
+// "wave" of destination rows [w0, w1) reads sources >= w0 and earlier waves
+// only wrote rows < w0.  Within a wave every source is read into registers
+// before any destination is written, and the CTAs that share one plane form a
+// thread-block cluster whose hardware barrier separates the read and write
+// phases -- no global spin-waits.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace hsd {
+namespace compact {
+
+constexpr int kThreads = 256;
+constexpr int kVec = 8;  // 16-byte vectors staged per thread per wave
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_nrank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// grid = n_planes * cluster, one cluster per plane.
+__global__ void __launch_bounds__(kThreads) compact_planes_kernel(
+    const uint64_t* __restrict__ plane_ptrs, int n_planes, int row_bytes,
+    const int32_t* __restrict__ keep_idx, int n_keep_host, const int32_t* counts,
+    int32_t* status) {
+  const int cs = int(cluster_nrank());
+  const int crank = int(cluster_rank());
+  const int plane = blockIdx.x / cs;
+  const int n_keep = counts ? counts[0] : n_keep_host;
+  const int first = counts ? counts[1] : 0;
+  if (plane >= n_planes) return;  // whole cluster exits together (same plane)
+  char* base = reinterpret_cast<char*>(plane_ptrs[plane]);
+  const int vpr = row_bytes >> 4;                 // 16-byte vectors per row
+  const int cta_vecs = kThreads * kVec;           // vectors staged per CTA per wave
+  const int rows_per_cta = cta_vecs / vpr;        // rows per CTA per wave (>= 1)
+  const int rows_per_wave = rows_per_cta * cs;
+  for (int w0 = first; w0 < n_keep; w0 += rows_per_wave) {
+    const int r0 = w0 + crank * rows_per_cta;
+    int4 stage[kVec];
+    int dst_row[kVec];
+#pragma unroll
+    for (int k = 0; k < kVec; ++k) {
+      const int v = threadIdx.x + k * kThreads;
+      const int r = r0 + v / vpr;
+      dst_row[k] = -1;
+      if (v < rows_per_cta * vpr && r < n_keep) {
+        const int src = keep_idx[r];
+        if (src != r) {
+          if (src < r) report(status, HSD_DEV_BAD_INDEX | 2);  // not ascending
+          const int c = v % vpr;
+          stage[k] = *reinterpret_cast<const int4*>(base + size_t(src) * row_bytes + size_t(c) * 16);
+          dst_row[k] = r;
+        }
+      }
+    }
+    cluster_sync_all();
+#pragma unroll
+    for (int k = 0; k < kVec; ++k) {
+      if (dst_row[k] >= 0) {
+        const int v = threadIdx.x + k * kThreads;
+        const int c = v % vpr;
+        *reinterpret_cast<int4*>(base + size_t(dst_row[k]) * row_bytes + size_t(c) * 16) = stage[k];
+      }
+    }
+    cluster_sync_all();
+  }
+}
+
+// keep = OR(live rows) & ~filter; ascending indices of set bits; n_keep and
+// the first index i with keep_idx[i] != i.  One CTA of 1024 threads.
+__global__ void __launch_bounds__(1024) keep_kernel(const uint64_t* live, int n_live,
+                                                    int live_stride, const uint64_t* filter,
+                                                    int kv_len, uint64_t* keep_bits,
+                                                    int32_t* keep_idx, int32_t* counts) {
+  __shared__ int warp_sums[32];
+  __shared__ int carry;
+  __shared__ int first_moved;
+  const int nw = (kv_len + 63) / 64;
+  if (threadIdx.x == 0) {
+    carry = 0;
+    first_moved = 0x7fffffff;
+  }
+  __syncthreads();
+  for (int base = 0; base < nw; base += blockDim.x) {
+    const int t = base + threadIdx.x;
+    uint64_t w = 0;
+    if (t < nw) {
+      for (int r = 0; r < n_live; ++r) w |= live[size_t(r) * live_stride + t];
+      if (filter) w &= ~filter[t];
+      const int rem = kv_len - 64 * t;
+      if (rem < 64) w &= (1ull << rem) - 1ull;
+      keep_bits[t] = w;
+    }
+    const int c = __popcll(w);
+    // block-wide exclusive scan of c
+    int x = c;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane_id() >= o) x += y;
+    }
+    if (lane_id() == 31) warp_sums[warp_id()] = x;
+    __syncthreads();
+    if (warp_id() == 0) {
+      int s = lane_id() < (blockDim.x >> 5) ? warp_sums[lane_id()] : 0;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, s, o);
+        if (lane_id() >= o) s += y;
+      }
+      warp_sums[lane_id()] = s;  // inclusive
+    }
+    __syncthreads();
+    const int excl = carry + (warp_id() ? warp_sums[warp_id() - 1] : 0) + x - c;
+    int pos = excl;
+    uint64_t m = w;
+    while (m) {
+      const int b = __ffsll(static_cast<long long>(m)) - 1;
+      const int col = 64 * t + b;
+      keep_idx[pos] = col;
+      if (col != pos) atomicMin(&first_moved, pos);
+      ++pos;
+      m &= m - 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = excl + c;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    counts[0] = carry;
+    counts[1] = first_moved == 0x7fffffff ? carry : first_moved;
+  }
+}
+
+// out[r] bit i = in[r] bit keep_idx[i], i < n_keep; words past n_keep cleared.
+__global__ void compact_bits_kernel(const uint64_t* in, uint64_t* out, int n_rows, int stride,
+                                    const int32_t* keep_idx, const int32_t* counts,
+                                    int out_words) {
+  const int n_keep = counts[0];
+  const int total = n_rows * out_words;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += gridDim.x * blockDim.x) {
+    const int r = idx / out_words, t = idx % out_words;
+    const uint64_t* row = in + size_t(r) * stride;
+    uint64_t w = 0;
+    for (int b = 0; b < 64; ++b) {
+      const int i = 64 * t + b;
+      if (i >= n_keep) break;
+      const int src = keep_idx[i];
+      w |= ((row[src >> 6] >> (src & 63)) & 1ull) << b;
+    }
+    out[size_t(r) * stride + t] = w;
+  }
+}
+
+}  // namespace compact
+}  // namespace hsd
+
+using namespace hsd;
+
+extern "C" {
+
+int hsd_compact_kv(const uint64_t* plane_ptrs, int32_t n_planes, int32_t row_bytes,
+                   const int32_t* keep_idx, int32_t n_keep, const int32_t* counts,
+                   int32_t* status, hsd_stream_t stream) {
+  if (!plane_ptrs || n_planes <= 0 || !keep_idx || row_bytes <= 0 || (row_bytes & 15) ||
+      row_bytes > compact::kThreads * compact::kVec * 16) {
+    hsd_host::set_error("hsd_compact_kv: bad arguments (n_planes=%d row_bytes=%d)", n_planes,
+                        row_bytes);
+    return HSD_ERR_INVALID_ARG;
+  }
+  if (!counts && n_keep < 0) {
+    hsd_host::set_error("hsd_compact_kv: n_keep < 0 needs the device counts");
+    return HSD_ERR_INVALID_ARG;
+  }
+  // Enough CTAs per plane to cover the SMs a few times over, at most 8
+  // (portable cluster size).
+  int cs = 1;
+  while (cs < 8 && n_planes * cs < 148 * 4) cs <<= 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(n_planes * cs));
+  cfg.blockDim = dim3(compact::kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return hsd_host::cuda_check(
+      cudaLaunchKernelEx(&cfg, compact::compact_planes_kernel, plane_ptrs, int(n_planes),
+                         int(row_bytes), keep_idx, int(n_keep), counts, status),
+      "compact_planes_kernel launch");
+}
+
+int hsd_keep_indices(const uint64_t* live_bits, int32_t n_live, int32_t live_stride,
+                     const uint64_t* filter_bits, int32_t kv_len, uint64_t* keep_bits,
+                     int32_t* keep_idx, int32_t* counts, hsd_stream_t stream) {
+  if (!live_bits || n_live < 0 || kv_len <= 0 || !keep_bits || !keep_idx || !counts ||
+      live_stride < (kv_len + 63) / 64) {
+    hsd_host::set_error("hsd_keep_indices: bad arguments");
+    return HSD_ERR_INVALID_ARG;
+  }
+  compact::keep_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      live_bits, n_live, live_stride, filter_bits, kv_len, keep_bits, keep_idx, counts);
+  return hsd_host::cuda_check(cudaGetLastError(), "keep_kernel launch");
+}
+
+int hsd_compact_bits(const uint64_t* in_bits, uint64_t* out_bits, int32_t n_rows, int32_t stride,
+                     const int32_t* keep_idx, const int32_t* counts, int32_t out_words,
+                     hsd_stream_t stream) {
+  if (!in_bits || !out_bits || in_bits == out_bits || n_rows <= 0 || out_words > stride ||
+      !keep_idx || !counts) {
+    hsd_host::set_error("hsd_compact_bits: bad arguments (in-place remap is not supported)");
+    return HSD_ERR_INVALID_ARG;
+  }
+  const int total = n_rows * out_words;
+  const int grid = (total + 255) / 256 < 1184 ? (total + 255) / 256 : 1184;
+  compact::compact_bits_kernel<<<grid > 0 ? grid : 1, 256, 0,
+                                  reinterpret_cast<cudaStream_t>(stream)>>>(
+      in_bits, out_bits, n_rows, stride, keep_idx, counts, out_words);
+  return hsd_host::cuda_check(cudaGetLastError(), "compact_bits_kernel launch");
+}
+
+}  // extern "C"

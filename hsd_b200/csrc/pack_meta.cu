@@ -1,0 +1,308 @@
+// (4) Packing metadata on the device.
+//
+// Replaces the reference's per-step dense mask build + create_block_mask
+// (D:94-106 with make_mask_mod D:148-153; H:1213-1221): from segment
+// descriptors (or, for drop-in use, from the dense float mask) it writes
+//   * the 64-bit row masks of every 128x64 tile (tile-major, 1 KB per tile),
+//   * the tile classes (empty / partial / full) and FlexAttention-style
+//     ascending partial / full index lists per 128-row query tile,
+//   * the list of 128-column KV blocks the attention kernel visits, with a
+//     present/partial flag per 64-column half,
+//   * a query-tile order, most blocks first, for the attention grid.
+// Padding rows (>= q_len) and padding columns (>= kv_len) are never allowed,
+// exactly as create_block_mask pads its tiles.
+#include "common.cuh"
+
+namespace hsd {
+namespace meta {
+
+struct SegSource {
+  const hsd_segment_t* segs;
+  const int32_t* row_seg;
+  const uint64_t* seg_kv_bits;
+  const uint64_t* tree_bits;
+  int32_t stride;  // words per seg_kv_bits row
+  int32_t q_len, kv_len, kv_base, n_segs;
+  int32_t* status;
+};
+
+// Bits of columns [lo, hi] (inclusive) that fall into word t.
+__device__ __forceinline__ uint64_t range_bits(int t, int lo, int hi) {
+  const int a = max(lo, 64 * t), b = min(hi, 64 * t + 63);
+  if (a > b) return 0;
+  const int n = b - a + 1;
+  const uint64_t m = (n >= 64) ? ~0ull : ((1ull << n) - 1ull);
+  return m << (a - 64 * t);
+}
+
+// 64 bits of a packed bit row starting at bit `off` (may be negative).
+__device__ __forceinline__ uint64_t extract64(const uint64_t* row, int nwords, int off) {
+  if (off <= -64) return 0;
+  if (off < 0) return nwords > 0 ? (row[0] << (-off)) : 0;
+  const int wi = off >> 6, sh = off & 63;
+  const uint64_t lo = wi < nwords ? row[wi] : 0;
+  if (sh == 0) return lo;
+  const uint64_t hi = wi + 1 < nwords ? row[wi + 1] : 0;
+  return (lo >> sh) | (hi << (64 - sh));
+}
+
+__device__ __forceinline__ uint64_t clip_word(uint64_t w, int t, int kv_len) {
+  const int rem = kv_len - 64 * t;
+  if (rem <= 0) return 0;
+  if (rem < 64) w &= (1ull << rem) - 1ull;
+  return w;
+}
+
+__device__ __forceinline__ uint64_t seg_row_word(const SegSource& S, int q, int t) {
+  if (q >= S.q_len) return 0;
+  const int s = S.row_seg[q];
+  if (s < 0) return 0;
+  if (s >= S.n_segs) {
+    report(S.status, HSD_DEV_BAD_INDEX | 1);
+    return 0;
+  }
+  const hsd_segment_t seg = S.segs[s];
+  uint64_t w = S.seg_kv_bits[size_t(s) * S.stride + t];
+  const int i = q - seg.q_start;
+  const int lo = S.kv_base + seg.q_start;
+  if (seg.kind == HSD_SEG_CAUSAL) {
+    w |= range_bits(t, lo, lo + i);
+  } else if (seg.kind == HSD_SEG_SINGLE) {
+    if (i == 0) w |= range_bits(t, lo, lo);
+  } else if (seg.kind == HSD_SEG_TREE) {
+    const int off = 64 * t - lo;
+    if (off > -64 && off < seg.q_len && i >= 0 && i < seg.q_len) {
+      const uint64_t* row = S.tree_bits + seg.tree_off + size_t(i) * seg.tree_words;
+      uint64_t a = extract64(row, seg.tree_words, off);
+      // nodes beyond the segment are not its columns
+      const int span = seg.q_len - off;  // nodes available from bit 0 of this word
+      if (span < 64) a &= (span <= 0) ? 0ull : ((1ull << span) - 1ull);
+      w |= a;
+    }
+  }
+  return clip_word(w, t, S.kv_len);
+}
+
+__device__ __forceinline__ uint64_t warp_and64(uint64_t v) {
+  uint32_t lo = __reduce_and_sync(0xffffffffu, uint32_t(v));
+  uint32_t hi = __reduce_and_sync(0xffffffffu, uint32_t(v >> 32));
+  return (uint64_t(hi) << 32) | lo;
+}
+__device__ __forceinline__ uint64_t warp_or64(uint64_t v) {
+  uint32_t lo = __reduce_or_sync(0xffffffffu, uint32_t(v));
+  uint32_t hi = __reduce_or_sync(0xffffffffu, uint32_t(v >> 32));
+  return (uint64_t(hi) << 32) | lo;
+}
+
+// One CTA (8 warps) per 128-row query tile.  kFromSegments: compute row words
+// from segment descriptors and store them; otherwise read the words the dense
+// kernel stored.
+template <bool kFromSegments>
+__global__ void __launch_bounds__(256) classify_kernel(SegSource S, hsd_plan_t P) {
+  extern __shared__ uint8_t cls[];  // [n_kv64]
+  const int qt = blockIdx.x;
+  const int warp = warp_id(), lane = lane_id();
+  const int n64 = P.n_kv64;
+  uint64_t* words = P.mask_words + size_t(qt) * n64 * 128;
+  for (int t = warp; t < n64; t += 8) {
+    uint64_t acc_and = ~0ull, acc_or = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int r = lane + 32 * k;
+      const int q = qt * 128 + r;
+      uint64_t w;
+      if (kFromSegments) {
+        w = seg_row_word(S, q, t);
+        words[size_t(t) * 128 + r] = w;
+      } else {
+        w = (q < P.q_len) ? words[size_t(t) * 128 + r] : 0ull;
+      }
+      acc_and &= w;
+      acc_or |= w;
+    }
+    acc_and = warp_and64(acc_and);
+    acc_or = warp_or64(acc_or);
+    if (lane == 0) cls[t] = acc_or == 0 ? 0 : (acc_and == ~0ull ? 2 : 1);
+  }
+  __syncthreads();
+  uint8_t* gcls = P.tile_class + size_t(qt) * n64;
+  for (int t = threadIdx.x; t < n64; t += blockDim.x) gcls[t] = cls[t];
+  if (warp == 0) {
+    // FlexAttention-style ascending lists.
+    int n_part = 0, n_full = 0;
+    int32_t* kvi = P.kv_indices + size_t(qt) * n64;
+    int32_t* fvi = P.full_kv_indices + size_t(qt) * n64;
+    for (int base = 0; base < n64; base += 32) {
+      const int t = base + lane;
+      const int c = t < n64 ? cls[t] : 0;
+      const uint32_t bp = __ballot_sync(0xffffffffu, c == 1);
+      const uint32_t bf = __ballot_sync(0xffffffffu, c == 2);
+      const uint32_t below = (1u << lane) - 1u;
+      if (c == 1) kvi[n_part + __popc(bp & below)] = t;
+      if (c == 2) fvi[n_full + __popc(bf & below)] = t;
+      n_part += __popc(bp);
+      n_full += __popc(bf);
+    }
+    // 128-column blocks for the attention kernel.
+    int n_blk = 0;
+    uint32_t* bl = P.blk_list + size_t(qt) * P.n_kv128;
+    for (int base = 0; base < P.n_kv128; base += 32) {
+      const int b = base + lane;
+      int c0 = 0, c1 = 0;
+      if (b < P.n_kv128) {
+        c0 = cls[2 * b];
+        c1 = (2 * b + 1 < n64) ? cls[2 * b + 1] : 0;
+      }
+      const bool present = (c0 | c1) != 0;
+      const uint32_t bb = __ballot_sync(0xffffffffu, present);
+      if (present) {
+        const uint32_t e = uint32_t(b) | (uint32_t(c0 != 0) << 24) | (uint32_t(c0 == 1) << 25) |
+                           (uint32_t(c1 != 0) << 26) | (uint32_t(c1 == 1) << 27);
+        bl[n_blk + __popc(bb & ((1u << lane) - 1u))] = e;
+      }
+      n_blk += __popc(bb);
+    }
+    if (lane == 0) {
+      P.kv_num_blocks[qt] = n_part;
+      P.full_kv_num_blocks[qt] = n_full;
+      P.blk_count[qt] = n_blk;
+    }
+  }
+}
+
+// Query tiles ranked by descending block count (ties: lower tile first), so
+// the attention grid starts the longest tiles first.
+__global__ void order_kernel(hsd_plan_t P) {
+  const int n = P.n_qtiles;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int ci = P.blk_count[i];
+    int rank = 0;
+    for (int j = 0; j < n; ++j) {
+      const int cj = P.blk_count[j];
+      rank += (cj > ci) || (cj == ci && j < i);
+    }
+    P.tile_order[rank] = i;
+  }
+}
+
+// Dense float mask -> row words.  One warp per (row, 64-column word); the two
+// 32-column halves are read as coalesced 128-byte lines.
+__global__ void __launch_bounds__(256) dense_words_kernel(const float* mask, int64_t row_stride,
+                                                          hsd_plan_t P) {
+  const int n64 = P.n_kv64;
+  const int64_t total = int64_t(P.n_qtiles) * 128 * n64;
+  const int lane = lane_id();
+  for (int64_t w = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < total;
+       w += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+    const int q = int(w / n64);
+    const int t = int(w % n64);
+    bool a = false, b = false;
+    if (q < P.q_len) {
+      const float* row = mask + int64_t(q) * row_stride;
+      const int c0 = 64 * t + lane, c1 = c0 + 32;
+      if (c0 < P.kv_len) a = row[c0] > -0.1f;
+      if (c1 < P.kv_len) b = row[c1] > -0.1f;
+    }
+    const uint32_t lo = __ballot_sync(0xffffffffu, a);
+    const uint32_t hi = __ballot_sync(0xffffffffu, b);
+    if (lane == 0) {
+      const int qt = q >> 7, r = q & 127;
+      P.mask_words[(size_t(qt) * n64 + t) * 128 + r] = (uint64_t(hi) << 32) | lo;
+    }
+  }
+}
+
+}  // namespace meta
+}  // namespace hsd
+
+using namespace hsd;
+
+static int check_plan(const hsd_plan_t* p) {
+  if (!p || !p->mask_words || !p->tile_class || !p->blk_list || p->q_len <= 0 ||
+      p->kv_len <= 0) {
+    hsd_host::set_error("plan is not initialised (hsd_plan_init)");
+    return HSD_ERR_INVALID_ARG;
+  }
+  return HSD_OK;
+}
+
+static int launch_classify(bool from_segments, const meta::SegSource& S, const hsd_plan_t& P,
+                           cudaStream_t st) {
+  const size_t smem = size_t(P.n_kv64);
+  if (smem > 200 * 1024) {
+    hsd_host::set_error("kv_len %d too large for the metadata kernel", P.kv_len);
+    return HSD_ERR_TOO_LARGE;
+  }
+  if (from_segments) {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(meta::classify_kernel<true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    meta::classify_kernel<true><<<P.n_qtiles, 256, smem, st>>>(S, P);
+  } else {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(meta::classify_kernel<false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    meta::classify_kernel<false><<<P.n_qtiles, 256, smem, st>>>(S, P);
+  }
+  int rc = hsd_host::cuda_check(cudaGetLastError(), "classify_kernel launch");
+  if (rc) return rc;
+  meta::order_kernel<<<1, 1024, 0, st>>>(P);
+  return hsd_host::cuda_check(cudaGetLastError(), "order_kernel launch");
+}
+
+extern "C" {
+
+int hsd_build_plan_segments(const hsd_segment_t* segs, int32_t n_segs, const int32_t* row_seg,
+                            const uint64_t* seg_kv_bits, int32_t kv_words_stride,
+                            const uint64_t* tree_bits, hsd_plan_t* plan, int32_t* status,
+                            hsd_stream_t stream) {
+  int rc = check_plan(plan);
+  if (rc) return rc;
+  if (!segs || n_segs <= 0 || !row_seg || !seg_kv_bits ||
+      kv_words_stride < plan->n_kv64) {
+    hsd_host::set_error("hsd_build_plan_segments: bad segment arguments (n_segs=%d stride=%d "
+                        "n_kv64=%d)",
+                        n_segs, kv_words_stride, plan->n_kv64);
+    return HSD_ERR_INVALID_ARG;
+  }
+  if (plan->kv_len < plan->q_len) {
+    hsd_host::set_error("kv_len (%d) must include the %d new columns", plan->kv_len,
+                        plan->q_len);
+    return HSD_ERR_INVALID_ARG;
+  }
+  meta::SegSource S;
+  S.segs = segs;
+  S.row_seg = row_seg;
+  S.seg_kv_bits = seg_kv_bits;
+  S.tree_bits = tree_bits;
+  S.stride = kv_words_stride;
+  S.q_len = plan->q_len;
+  S.kv_len = plan->kv_len;
+  S.kv_base = plan->kv_len - plan->q_len;
+  S.n_segs = n_segs;
+  S.status = status;
+  return launch_classify(true, S, *plan, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int hsd_build_plan_dense(const float* mask, int64_t row_stride, hsd_plan_t* plan,
+                         int32_t* status, hsd_stream_t stream) {
+  int rc = check_plan(plan);
+  if (rc) return rc;
+  if (!mask || row_stride < plan->kv_len) {
+    hsd_host::set_error("hsd_build_plan_dense: row_stride %lld < kv_len %d",
+                        (long long)row_stride, plan->kv_len);
+    return HSD_ERR_INVALID_ARG;
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t warps = int64_t(plan->n_qtiles) * 128 * plan->n_kv64;
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  const int grid = int(blocks < 148 * 16 ? blocks : 148 * 16);
+  meta::dense_words_kernel<<<grid, 256, 0, st>>>(mask, row_stride, *plan);
+  rc = hsd_host::cuda_check(cudaGetLastError(), "dense_words_kernel launch");
+  if (rc) return rc;
+  meta::SegSource S{};
+  S.status = status;
+  return launch_classify(false, S, *plan, st);
+}
+
+}  // extern "C"

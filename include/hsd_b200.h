@@ -1,0 +1,227 @@
+/*
+ * hsd_b200 -- C ABI of the B200 (sm_100a) verification hot path of HSD.
+ *
+ * Plain pointers and sizes only.  Every entry point is asynchronous on the
+ * stream it is given, never synchronises, and returns an HSD_* status code
+ * for host-side argument errors (hsd_last_error() holds the message).
+ * Problems found on the device (a bounded wait that ran out, an index out of
+ * range) are written with atomicCAS into the caller's int32 `status` word in
+ * device memory (first error wins; NULL disables reporting); the host reads
+ * it after its next synchronisation.  Every device pointer is caller-owned.
+ *
+ * Reference interfaces replaced (paths inside whlscut/HSD):
+ *   D  = hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py
+ *   H  = hsd/hunyuan_ocr_pipeline/modeling_hunyuan_vl_hsd.py
+ */
+#ifndef HSD_B200_H
+#define HSD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *hsd_stream_t;
+
+/* host status codes */
+#define HSD_OK 0
+#define HSD_ERR_INVALID_ARG 1
+#define HSD_ERR_UNSUPPORTED 2
+#define HSD_ERR_CUDA 3
+#define HSD_ERR_TOO_LARGE 4
+
+/* device status codes (low 16 bits: where; high bits: what) */
+#define HSD_DEV_TIMEOUT 0x10000
+#define HSD_DEV_BAD_INDEX 0x20000
+#define HSD_DEV_CAPACITY 0x40000
+
+/* segment kinds: the intra-segment pattern over the segment's new columns */
+#define HSD_SEG_CAUSAL 0 /* speculative / prefill block: tril (D:1442-1447, RD:234-245) */
+#define HSD_SEG_TREE 1   /* tree block: ancestor sets (D:1519-1533) */
+#define HSD_SEG_SINGLE 2 /* normal block: only its first row sees its first column (D:1021-1025) */
+#define HSD_SEG_NONE 3   /* no new columns (e.g. HunYuan tight-pack tail rows, H:2290-2293) */
+
+/* block modes of the verification loop (D:979, `decode_modes`) */
+#define HSD_MODE_NORMAL 0
+#define HSD_MODE_SPEC 1
+#define HSD_MODE_TREE 2
+#define HSD_MODE_FINISHED 3
+
+/* One segment of the packed query.  Every row q in [q_start, q_start+q_len)
+ * sees the columns set in the segment's row of `seg_kv_bits`, plus the
+ * pattern `kind` over the segment's own new columns, which start at column
+ * kv_len - q_len_total + q_start.  Replaces the dense float mask the
+ * reference rebuilds each step (D:1634-1667, D:1737-1748). */
+typedef struct {
+  int32_t q_start;
+  int32_t q_len;
+  int32_t kind;
+  int32_t tree_off;   /* HSD_SEG_TREE: offset (in uint64 words) of q_len ancestor rows */
+  int32_t tree_words; /* HSD_SEG_TREE: words per ancestor row, >= ceil(q_len / 64) */
+  int32_t reserved;
+} hsd_segment_t;
+
+/* Tile plan of one packed mask: the same information as FlexAttention's
+ * BlockMask at BLOCK_SIZE (128, 64) (D:94-106, H:1213-1221) plus the per-row
+ * 64-bit masks of every tile and the list of 128-column blocks the attention
+ * kernel visits.  All pointers are device memory carved from one workspace by
+ * hsd_plan_init(). */
+typedef struct {
+  int32_t q_len, kv_len;
+  int32_t n_qtiles;   /* ceil(q_len / 128) */
+  int32_t n_kv64;     /* ceil(kv_len / 64) */
+  int32_t n_kv128;    /* ceil(kv_len / 128) */
+  int32_t reserved;
+  uint64_t *mask_words;      /* [n_qtiles][n_kv64][128] bit c of row r = column 64t+c allowed */
+  uint8_t *tile_class;       /* [n_qtiles][n_kv64] 0 empty, 1 partial, 2 full */
+  int32_t *kv_num_blocks;    /* [n_qtiles]  BlockMask.kv_num_blocks (partial tiles) */
+  int32_t *kv_indices;       /* [n_qtiles][n_kv64] ascending */
+  int32_t *full_kv_num_blocks; /* [n_qtiles] */
+  int32_t *full_kv_indices;  /* [n_qtiles][n_kv64] ascending */
+  int32_t *blk_count;        /* [n_qtiles] 128-column blocks visited */
+  uint32_t *blk_list;        /* [n_qtiles][n_kv128] block | flags << 24 */
+  int32_t *tile_order;       /* [n_qtiles] query tiles, most blocks first */
+} hsd_plan_t;
+
+/* Per-block state and inputs of the acceptance / re-alignment kernel.  Mirrors
+ * the per-block Python lists of `batch_generate` (D:979-992). */
+typedef struct {
+  int32_t mode;        /* HSD_MODE_* this step ran in */
+  int32_t q_start;     /* block_start in the packed query (D:1101) */
+  int32_t q_len;       /* block_end - block_start */
+  int32_t valid_count; /* block_valid_counts[b] (D:992) */
+  int32_t gen_off;     /* generated tokens live at gen_pool[gen_off, gen_off + gen_cap) */
+  int32_t gen_len;     /* in: tokens so far; out: after this step */
+  int32_t gen_cap;
+  int32_t draft_off;   /* tokenized draft at draft_pool[draft_off, + draft_len) */
+  int32_t draft_len;
+  int32_t mws;         /* match_window_sizes[b] (in/out) */
+  int32_t matches_len; /* matches_length[b] (in/out) */
+  int32_t tree_off;    /* HSD_MODE_TREE: packed BFS nodes at tree_tokens/parents[tree_off..] */
+  int32_t tree_nodes;
+  int32_t seg;         /* row of seg_kv_bits holding this block's KV visibility */
+  int32_t flags;       /* bit 0: page block (no repetition stop, no token KMP) */
+  int32_t reserved;
+} hsd_block_t;
+
+typedef struct {
+  int32_t finished;    /* 0 running, 1 EOS (D:1299-1305), 2 repetition stop (D:1306-1319), 3 was finished */
+  int32_t increment;   /* generated_tokens_increment[b] */
+  int32_t pointer;     /* packed row of the last accepted token */
+  int32_t next_token;  /* next_token_int */
+  int32_t match_count; /* len(matches) of the re-alignment (D:1419) */
+  int32_t match_start; /* draft index of the first match, -1 if none */
+  int32_t slice_begin; /* unique match: next speculative input is draft[slice_begin, slice_end) */
+  int32_t slice_end;
+} hsd_block_result_t;
+
+typedef struct {
+  int32_t n_blocks;
+  int32_t kv_len;          /* columns of the current mask */
+  int32_t kv_base;         /* first new column: kv_len - q_len (D:1089) */
+  int32_t kv_words_stride; /* uint64 words per row of seg_kv_bits / out_kv_bits */
+  int32_t match_window_size;            /* default 3 */
+  int32_t match_window_size_upper_bound;/* default 10 */
+  int32_t max_spec_len;    /* HSD_MAX_SPEC_LEN, 0 = unlimited */
+  int32_t repeat_sentinel; /* 20993 (dots) / 41153 (HunYuan) */
+  int32_t n_eos;
+  int32_t eos_ids[8];
+} hsd_accept_config_t;
+
+/* ---- library ---------------------------------------------------------- */
+const char *hsd_version(void);
+const char *hsd_last_error(void);
+
+/* ---- (4) packing metadata ---------------------------------------------- */
+
+/* Bytes of device workspace a plan for (q_len, kv_len) needs. */
+size_t hsd_plan_workspace_bytes(int32_t q_len, int32_t kv_len);
+
+/* Carve `plan` out of `workspace` (device memory, 256-byte aligned). */
+int hsd_plan_init(void *workspace, size_t bytes, int32_t q_len, int32_t kv_len,
+                  hsd_plan_t *plan);
+
+/* Tile plan from segment descriptors; replaces create_block_mask(make_mask_mod(
+ * dense mask), BLOCK_SIZE=(128,64)) (D:94-106, D:148-153, H:1213-1221) without
+ * ever materialising the dense mask.  row_seg[q] is the segment of row q
+ * (-1: no segment, row fully masked).  seg_kv_bits has kv_words_stride words
+ * per segment. */
+int hsd_build_plan_segments(const hsd_segment_t *segs, int32_t n_segs,
+                            const int32_t *row_seg,
+                            const uint64_t *seg_kv_bits, int32_t kv_words_stride,
+                            const uint64_t *tree_bits, hsd_plan_t *plan,
+                            int32_t *status, hsd_stream_t stream);
+
+/* Tile plan from the reference's dense float mask [.., q_len, >=kv_len]
+ * (allowed <=> value > -0.1, make_mask_mod D:148-153). */
+int hsd_build_plan_dense(const float *mask, int64_t row_stride, hsd_plan_t *plan,
+                         int32_t *status, hsd_stream_t stream);
+
+/* ---- (1) packed verification attention ---------------------------------- */
+
+/* out = softmax(q k^T * scale + mask) v per query head with grouped KV heads,
+ * lse = natural log-sum-exp; replaces flex_attention_forward (D:72-135,
+ * H:103-180) including repeat_kv (D:137-146).  q: bf16 [num_q_heads][q_len]
+ * [128] at the given element strides (row, head); k, v likewise with
+ * num_kv_heads; out: bf16 [q_len][num_q_heads][128] contiguous (the
+ * reference's transposed output, D:134); lse: fp32 [num_q_heads][q_len] or
+ * NULL.  Fully masked rows give 0 and -inf.  head_dim must be 128. */
+int hsd_verify_attention(const void *q, int64_t q_row_stride, int64_t q_head_stride,
+                         const void *k, int64_t k_row_stride, int64_t k_head_stride,
+                         const void *v, int64_t v_row_stride, int64_t v_head_stride,
+                         void *out, float *lse, int32_t q_len, int32_t kv_len,
+                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                         float scale, const hsd_plan_t *plan, int32_t *status,
+                         hsd_stream_t stream);
+
+/* ---- (2) KV-cache compaction -------------------------------------------- */
+
+/* In place, for every plane p (one layer's K or V of one KV head, rows of
+ * row_bytes contiguous bytes): row i <- row keep_idx[i] for i < n_keep.
+ * keep_idx is ascending (so keep_idx[i] >= i); rows already in place are not
+ * touched.  Replaces the per-layer index_select(-2, keep_indices) of
+ * D:1705-1722 / H:2262-2269.  plane_ptrs: device array of n_planes addresses.
+ * counts: device {n_keep, first_moved} as written by hsd_keep_indices (then
+ * n_keep is ignored), or NULL to use the host n_keep from row 0. */
+int hsd_compact_kv(const uint64_t *plane_ptrs, int32_t n_planes, int32_t row_bytes,
+                   const int32_t *keep_idx, int32_t n_keep,
+                   const int32_t *counts, int32_t *status, hsd_stream_t stream);
+
+/* keep = (OR of live_bits rows [0, n_live)) & ~filter_bits, then the ascending
+ * indices of set bits (keep_idx), their count and the first index that moves
+ * (D:1679-1707).  Counts land in counts[0] = n_keep, counts[1] = first_moved. */
+int hsd_keep_indices(const uint64_t *live_bits, int32_t n_live, int32_t live_stride,
+                     const uint64_t *filter_bits, int32_t kv_len,
+                     uint64_t *keep_bits, int32_t *keep_idx, int32_t *counts,
+                     hsd_stream_t stream);
+
+/* Remap visibility rows after compaction: out[r] bit i = in[r] bit keep_idx[i]
+ * (the mask's index_select(-1, keep) of D:1723), rows of `stride` words. */
+int hsd_compact_bits(const uint64_t *in_bits, uint64_t *out_bits, int32_t n_rows,
+                     int32_t stride, const int32_t *keep_idx, const int32_t *counts,
+                     int32_t out_words, hsd_stream_t stream);
+
+/* ---- (3) acceptance + KMP re-alignment ----------------------------------- */
+
+/* One warp per block: acceptance by mode (D:1107-1293, H:1633-1858 at
+ * threshold >= 1), EOS / repetition stop (D:1299-1319), KMP re-alignment of
+ * region blocks (compute_lps / kmp_search / find_all_matches_kmp, D:543-618,
+ * call site D:1326-1336) and the window update.  next_ids = argmax of the
+ * target model per packed row; input_ids = the packed input.  Appends the
+ * accepted tokens to gen_pool, ORs rejected columns into filter_bits and
+ * writes each block's new visibility (segment row | accepted path) to
+ * out_kv_bits[b]. */
+int hsd_accept_kmp(const hsd_accept_config_t *cfg, hsd_block_t *blocks,
+                   hsd_block_result_t *results, const int32_t *next_ids,
+                   const int32_t *input_ids, int32_t *gen_pool,
+                   const int32_t *draft_pool, const int32_t *tree_tokens,
+                   const int32_t *tree_parents, const uint64_t *seg_kv_bits,
+                   uint64_t *out_kv_bits, uint64_t *filter_bits, int32_t *status,
+                   hsd_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HSD_B200_H */

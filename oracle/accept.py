@@ -1,0 +1,232 @@
+"""Per-block acceptance and re-alignment (test infrastructure only).
+
+Restates the token-level parts of one iteration of the reference's
+``batch_generate`` loop (hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py):
+
+* normal mode 1-token step (D:1107-1124)
+* speculative exact-match acceptance at ``HSD_SPEC_THRESH >= 1`` (D:1126-1213)
+* tree-walk acceptance at ``HSD_TREE_THRESH >= 1`` (D:1215-1293)
+* EOS and repetition stop (D:1299-1319)
+* KMP re-alignment of non-page blocks (D:1321-1336, D:1417-1419)
+* next block input: speculative slice, BFS tree, or normal (D:1421-1567)
+
+The page block's text/select/bbox parser modes need the tokenizer and stay
+on the host in both implementations; they are not restated here.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from .kmp import compute_lps, find_all_matches_kmp, trie_bfs
+
+NORMAL, SPEC, TREE, FINISHED = 0, 1, 2, 3
+
+
+@dataclass
+class BlockState:
+    """Host bookkeeping of one packed block (D:979-992)."""
+
+    mode: int = NORMAL
+    gen: list = field(default_factory=list)      # generated_tokens[b]
+    draft: list = field(default_factory=list)    # tokenized_draft[b]
+    mws: int = 3                                 # match_window_sizes[b]
+    matches_len: int = 0                         # matches_length[b]
+    valid_count: int | None = None               # block_valid_counts[b]
+    tree_tokens: list | None = None              # packed BFS tree (tree mode)
+    tree_parents: list | None = None
+
+
+@dataclass
+class StepConfig:
+    pad_token_id: int = 0
+    eos_token_ids: tuple = (151643,)
+    match_window_size: int = 3
+    match_window_size_upper_bound: int = 10
+    max_tree_depth: int = 15
+    max_tree_len: int = 256
+    min_input_length: int = 128
+    max_spec_len: int = 0          # HSD_MAX_SPEC_LEN (D:61)
+    tight_pack: bool = False       # HSD_TIGHT_PACK (D:52)
+    enable_tree_decode: bool = False
+    repeat_sentinel: int = 20993   # dots (D:1306); HunYuan uses 41153 (H:1873)
+
+
+def _valid_length(st, input_list, bs, be, pad):
+    if st.valid_count is not None:
+        return st.valid_count
+    return sum(1 for t in input_list[bs:be] if t != pad)
+
+
+def _window_update(st, cfg, increment):
+    if st.matches_len in (0, 1):
+        st.mws = cfg.match_window_size
+    else:
+        st.mws += increment
+
+
+def accept_block(st, bs, be, next_list, input_list, cfg, filt, kv_base,
+                 allowed_row_fn, is_page_block):
+    """Acceptance for one block; mutates ``st`` and ``filt``.
+
+    Returns ``(pointer, next_token, increment, finished_reason)`` where
+    ``pointer`` is the absolute row (in the current packed query) of the
+    block's last accepted token, ``finished_reason`` is 0 (running),
+    1 (EOS) or 2 (repetition stop).  ``filt`` is the step's bool filter over
+    KV columns; ``allowed_row_fn(row)`` gives the bool visibility of a query
+    row (the mask row the EOS rule ORs in, D:1300-1302).
+    """
+    pad = cfg.pad_token_id
+    mode = st.mode
+    if mode == NORMAL:                                         # D:1107-1124
+        valid = _valid_length(st, input_list, bs, be, pad)
+        ptr = bs + valid - 1
+        nxt = next_list[ptr]
+        st.gen.append(nxt)
+        inc = 1
+        _window_update(st, cfg, 1)
+    elif mode == SPEC:                                         # D:1126-1213
+        valid = _valid_length(st, input_list, bs, be, pad)
+        ptr = bs + valid - 1
+        group = next_list[bs:be]
+        ref = input_list[bs:be]
+        blen = be - bs
+        acc = [group[i] == ref[i + 1] for i in range(blen - 1)]
+        diff = len(acc)
+        for i, ok in enumerate(acc):
+            if not ok:
+                diff = i
+                break
+        accepted = list(group[:diff + 1])
+        for i in range(diff):
+            accepted[i] = ref[i + 1]
+        st.gen.extend(accepted)
+        inc = diff + 1
+        nxt = group[diff]
+        _window_update(st, cfg, diff + 1)
+        if diff != blen - 1:
+            ptr = bs + diff
+            filt[kv_base + bs + diff + 1: kv_base + be] = True
+    elif mode == TREE:                                         # D:1215-1293
+        group = next_list[bs:be]
+        tokens, parents = st.tree_tokens, st.tree_parents
+        n_nodes = len(tokens)
+        consumed = [False] * n_nodes
+        decode = group[0]
+        st.gen.append(decode)
+        inc = 1
+        filt[kv_base + bs] = True
+        node = 0
+        new_index = 0
+        walked = 0
+        while True:
+            child = -1
+            for c in range(node + 1, n_nodes):
+                if parents[c] == node and tokens[c] == decode:
+                    child = c
+                    break
+            if child < 0 or consumed[child]:
+                break
+            node = child
+            new_index = child
+            consumed[child] = True
+            decode = group[new_index]
+            st.gen.append(decode)
+            inc += 1
+            walked += 1
+            filt[kv_base + bs + new_index] = True
+        ptr = bs + new_index
+        seg = filt[kv_base + bs: kv_base + be]
+        filt[kv_base + bs: kv_base + be] = ~seg
+        nxt = group[new_index]
+        _window_update(st, cfg, 1 + walked)
+    else:
+        return None, None, 0, 0
+
+    if st.gen[-1] in cfg.eos_token_ids:                       # D:1299-1305
+        filt |= allowed_row_fn(ptr)
+        st.mode = FINISHED
+        st.gen = st.gen[:-1]
+        return ptr, nxt, inc, 1
+    if not is_page_block:                                       # D:1306-1319
+        tail = st.gen[-10:]
+        reps = find_all_matches_kmp([st.gen], tail, compute_lps(tail), 1)[1]
+        if len(reps) > 10 and cfg.repeat_sentinel not in st.gen:
+            filt |= allowed_row_fn(ptr)
+            st.gen = list(st.draft)
+            st.mode = FINISHED
+            return ptr, nxt, inc, 2
+    return ptr, nxt, inc, 0
+
+
+def realign_block(st, cfg):
+    """KMP re-alignment of a region block (D:1321-1336, D:1417-1419).
+
+    Returns ``(window, matches, trie)``.
+    """
+    w = min(cfg.match_window_size_upper_bound, st.mws)
+    window = st.gen[-w:]
+    trie, matches = find_all_matches_kmp([st.draft], window,
+                                         compute_lps(window),
+                                         cfg.max_tree_depth)
+    st.matches_len = len(matches)
+    return window, matches, trie
+
+
+def next_block_input(st, cfg, window, matches, trie, next_token, pos_base):
+    """Next input of a region block (D:1421-1567).
+
+    Returns ``(input_ids, position_ids, intra_kind, new_len)`` and updates
+    ``st.mode`` / ``st.valid_count`` / the packed tree.
+    """
+    pad = cfg.pad_token_id
+    mil = cfg.min_input_length
+    if len(matches) == 1:                                       # D:1421-1436
+        _, start, end = matches[0]
+        start += len(window) - 1
+        ids = list(st.draft[start:end])
+        if cfg.max_spec_len > 0 and len(ids) > cfg.max_spec_len:
+            ids = ids[:cfg.max_spec_len]
+        if not cfg.tight_pack:
+            ids += [pad] * (math.ceil(len(ids) / mil) * mil - len(ids))
+        pos = list(range(pos_base, pos_base + len(ids)))
+        st.valid_count = len(ids) - (ids.count(pad) if not cfg.tight_pack else 0)
+        st.mode = SPEC
+        st.tree_tokens = st.tree_parents = None
+        return ids, pos, "causal", len(ids)
+    if cfg.enable_tree_decode and len(trie.children) > 0:       # D:1488-1543
+        cap = (min(cfg.max_tree_len, cfg.max_spec_len) if cfg.max_spec_len > 0
+               else cfg.max_tree_len)
+        tokens, depths, parents = trie_bfs(trie, cap)
+        ids = list(tokens)
+        pos = [d + pos_base for d in depths]
+        if not cfg.tight_pack:
+            ids += [pad] * (math.ceil(len(ids) / mil) * mil - len(ids))
+            pos += [0] * (len(ids) - len(pos))
+        st.valid_count = len(tokens)
+        st.mode = TREE
+        st.tree_tokens, st.tree_parents = tokens, parents
+        return ids, pos, "tree", len(ids)
+    if cfg.tight_pack:                                           # D:1544-1565
+        ids, pos = [next_token], [pos_base]
+    else:
+        ids = [next_token] + [pad] * (mil - 1)
+        pos = [pos_base] + [0] * (mil - 1)
+    st.valid_count = 1
+    st.mode = NORMAL
+    st.tree_tokens = st.tree_parents = None
+    return ids, pos, "single", len(ids)
+
+
+def kmp_match_summary(draft, window):
+    """(count, first start) of the matches ``find_all_matches_kmp`` keeps."""
+    _, matches = find_all_matches_kmp([draft], window, compute_lps(window), 1)
+    if not matches:
+        return 0, -1
+    return len(matches), matches[0][1]
+
+
+def as_int_array(x):
+    return np.asarray(x, dtype=np.int64)

@@ -1,0 +1,90 @@
+"""C-ABI library: loads, exports every declared entry point, validates arguments.
+
+No compute call is made here: every call below is rejected on the host before
+any CUDA work, so this runs without a GPU.
+"""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from hsd_b200 import _native as N
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "include", "hsd_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(hsd_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = N.load()
+    names = declared_functions()
+    assert len(names) >= 10
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == {s[0] for s in N.SIGNATURES}
+
+
+def test_version_and_error_strings():
+    lib = N.load()
+    assert b"sm_100a" in lib.hsd_version()
+    assert isinstance(lib.hsd_last_error(), bytes)
+
+
+def test_struct_sizes_match_header():
+    assert C.sizeof(N.Segment) == 24
+    assert C.sizeof(N.Block) == 64
+    assert C.sizeof(N.BlockResult) == 32
+    assert C.sizeof(N.AcceptConfig) == 4 * 17
+    assert C.sizeof(N.Plan) == 24 + 9 * 8
+
+
+def test_plan_layout_host_only():
+    lib = N.load()
+    assert lib.hsd_plan_workspace_bytes(0, 10) == 0
+    n = lib.hsd_plan_workspace_bytes(1512, 1512)
+    # mask words dominate: 12 q tiles x 24 kv tiles x 128 rows x 8 bytes
+    assert n >= 12 * 24 * 128 * 8
+    buf = C.create_string_buffer(n + 512)
+    base = (C.addressof(buf) + 255) & ~255
+    plan = N.Plan()
+    assert lib.hsd_plan_init(C.c_void_p(base), n, 1512, 1512, C.byref(plan)) == 0
+    assert (plan.n_qtiles, plan.n_kv64, plan.n_kv128) == (12, 24, 12)
+    ptrs = [plan.mask_words, plan.tile_class, plan.kv_num_blocks, plan.kv_indices,
+            plan.full_kv_num_blocks, plan.full_kv_indices, plan.blk_count, plan.blk_list,
+            plan.tile_order]
+    assert all(p % 256 == 0 for p in ptrs)
+    assert ptrs == sorted(ptrs) and ptrs[-1] < base + n
+    # too small / misaligned workspaces are rejected
+    assert lib.hsd_plan_init(C.c_void_p(base), n - 1, 1512, 1512, C.byref(plan)) != 0
+    assert lib.hsd_plan_init(C.c_void_p(base + 8), n, 1512, 1512, C.byref(plan)) != 0
+    assert b"aligned" in lib.hsd_last_error()
+
+
+def test_attention_rejects_bad_head_dim_on_host():
+    lib = N.load()
+    plan = N.Plan()
+    plan.q_len, plan.kv_len = 128, 128
+    rc = lib.hsd_verify_attention(None, 64, 64, None, 64, 64, None, 64, 64, None, None,
+                                  128, 128, 2, 1, 64, 0.1, C.byref(plan), None, None)
+    assert rc == N.HSD_OK + 2  # HSD_ERR_UNSUPPORTED
+    assert b"head_dim" in lib.hsd_last_error()
+
+
+def test_other_entry_points_reject_null_arguments():
+    lib = N.load()
+    assert lib.hsd_compact_kv(None, 0, 256, None, 0, None, None, None) != 0
+    assert lib.hsd_keep_indices(None, 0, 0, None, 0, None, None, None, None) != 0
+    assert lib.hsd_compact_bits(None, None, 0, 0, None, None, 0, None) != 0
+    cfg = N.AcceptConfig()
+    assert lib.hsd_accept_kmp(C.byref(cfg), None, None, None, None, None, None, None,
+                              None, None, None, None, None, None) != 0
+    plan = N.Plan()
+    assert lib.hsd_build_plan_segments(None, 0, None, None, 0, None, C.byref(plan),
+                                       None, None) != 0
+    assert lib.hsd_build_plan_dense(None, 0, C.byref(plan), None, None) != 0
