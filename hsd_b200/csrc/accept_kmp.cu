@@ -33,7 +33,6 @@ struct Params {
   int32_t* status;
 };
 
-constexpr int kMaxTreeNodes = 1024;  // 32 lanes x 32 bits of "visited"
 
 __device__ __forceinline__ uint64_t word_range(int w, int lo, int hi) {  // [lo, hi]
   const int a = max(lo, 64 * w), b = min(hi, 64 * w + 63);
@@ -85,206 +84,251 @@ __device__ void count_matches(const int32_t* text, int n, const int32_t* pat, in
   }
 }
 
-__global__ void __launch_bounds__(128) accept_kmp_kernel(Params p) {
+// Filter-bit operation a block applies, replayed in block order by phase 2
+// (the reference mutates one shared filter mask block after block; a tree
+// block *inverts* its column range, so order matters when ranges overlap).
+constexpr int kMaxPath = 64;
+struct FilterOp {
+  int32_t kind;  // 0 none, 1 OR [lo, hi], 2 tree: set path, then invert [lo, hi]
+  int32_t lo, hi;
+  int32_t finished;  // OR the block's visibility row afterwards
+  int32_t n_path;
+  int16_t path[kMaxPath];
+};
+
+// One CTA.  Phase 1: warp w handles blocks w, w + nwarps, ... in parallel.
+// Phase 2: warp 0 applies every block's filter operation in block order.
+__global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  FilterOp* ops = reinterpret_cast<FilterOp*>(smem_raw);
   const int lane = lane_id();
-  const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nwarps = blockDim.x >> 5;
   const hsd_accept_config_t& cfg = p.cfg;
-  if (b >= cfg.n_blocks) return;
-  hsd_block_t blk = p.blocks[b];
-  hsd_block_result_t res;
-  res.finished = 0;
-  res.increment = 0;
-  res.pointer = -1;
-  res.next_token = -1;
-  res.match_count = 0;
-  res.match_start = -1;
-  res.slice_begin = -1;
-  res.slice_end = -1;
-  if (blk.mode == HSD_MODE_FINISHED) {
-    res.finished = 3;
-    if (lane == 0) p.results[b] = res;
-    return;
-  }
   const int stride = cfg.kv_words_stride;
   const int nwords = (cfg.kv_len + 63) / 64;
   const int kvb = cfg.kv_base;
-  const int bs = blk.q_start, blen = blk.q_len;
-  int32_t* gen = p.gen_pool + blk.gen_off;
-  int glen = blk.gen_len;
-  uint64_t* vis = p.out_kv_bits + size_t(b) * stride;
-  const uint64_t* seg_row = p.seg_kv_bits + size_t(blk.seg) * stride;
-  for (int w = lane; w < nwords; w += 32) vis[w] = seg_row[w];
-  __syncwarp();
-
-  int ptr, nxt, inc;
-  uint32_t visited = 0;  // tree mode: bit k of lane l = node 32*l + k on the accepted path
-  if (blk.mode == HSD_MODE_NORMAL) {
-    ptr = bs + blk.valid_count - 1;
-    nxt = p.next_ids[ptr];
-    if (glen + 1 > blk.gen_cap) {
-      report(p.status, HSD_DEV_CAPACITY | 1);
-      return;
-    }
-    if (lane == 0) gen[glen] = nxt;
-    glen += 1;
-    inc = 1;
-    or_range(vis, kvb + bs, kvb + ptr, lane, false);
-  } else if (blk.mode == HSD_MODE_SPEC) {
-    ptr = bs + blk.valid_count - 1;
-    int diff = blen - 1;
-    for (int base = 0; base < blen - 1; base += 32) {
-      const int i = base + lane;
-      const bool bad = (i < blen - 1) && (p.next_ids[bs + i] != p.input_ids[bs + i + 1]);
-      const uint32_t bal = __ballot_sync(0xffffffffu, bad);
-      if (bal) {
-        diff = base + __ffs(bal) - 1;
-        break;
+  for (int b = warp_id(); b < cfg.n_blocks; b += nwarps) {
+    FilterOp op;
+    op.kind = 0;
+    op.lo = op.hi = 0;
+    op.finished = 0;
+    op.n_path = 0;
+    hsd_block_t blk = p.blocks[b];
+    hsd_block_result_t res;
+    res.finished = 0;
+    res.increment = 0;
+    res.pointer = -1;
+    res.next_token = -1;
+    res.match_count = 0;
+    res.match_start = -1;
+    res.slice_begin = -1;
+    res.slice_end = -1;
+    if (blk.mode == HSD_MODE_FINISHED) {
+      // a block finished in an earlier step sees nothing any more
+      uint64_t* dead = p.out_kv_bits + size_t(b) * stride;
+      for (int w = lane; w < nwords; w += 32) dead[w] = 0;
+      res.finished = 3;
+      if (lane == 0) {
+        p.results[b] = res;
+        ops[b] = op;
       }
+      continue;
     }
-    if (glen + diff + 1 > blk.gen_cap) {
-      report(p.status, HSD_DEV_CAPACITY | 2);
-      return;
-    }
-    nxt = p.next_ids[bs + diff];
-    for (int i = lane; i <= diff; i += 32)
-      gen[glen + i] = (i < diff) ? p.input_ids[bs + i + 1] : nxt;
-    glen += diff + 1;
-    inc = diff + 1;
-    if (diff != blen - 1) {
-      ptr = bs + diff;
-      or_range(p.filter_bits, kvb + bs + diff + 1, kvb + bs + blen - 1, lane, true);
-    }
-    or_range(vis, kvb + bs, kvb + ptr, lane, false);
-  } else if (blk.mode == HSD_MODE_TREE) {
-    const int32_t* tok = p.tree_tokens + blk.tree_off;
-    const int32_t* par = p.tree_parents + blk.tree_off;
-    const int n = min(blk.tree_nodes, min(blen, kMaxTreeNodes));
-    int decode = p.next_ids[bs];
-    int node = 0, new_index = 0, walked = 0;
-    if (lane == 0) visited |= 1u;
-    // the walk appends 1 + walked tokens; reserve capacity up front
-    if (glen + n > blk.gen_cap) {
-      report(p.status, HSD_DEV_CAPACITY | 3);
-      return;
-    }
-    if (lane == 0) gen[glen] = decode;
-    glen += 1;
-    for (int guard = 0; guard < n; ++guard) {
-      int child = -1;
-      for (int base = node + 1; base < n; base += 32) {
-        const int c = base + lane;
-        const bool hit = c < n && par[c] == node && tok[c] == decode;
-        const uint32_t bal = __ballot_sync(0xffffffffu, hit);
+    const int bs = blk.q_start, blen = blk.q_len;
+    int32_t* gen = p.gen_pool + blk.gen_off;
+    int glen = blk.gen_len;
+    uint64_t* vis = p.out_kv_bits + size_t(b) * stride;
+    const uint64_t* seg_row = p.seg_kv_bits + size_t(blk.seg) * stride;
+    for (int w = lane; w < nwords; w += 32) vis[w] = seg_row[w];
+    __syncwarp();
+
+    int ptr = bs, nxt = 0, inc = 0;
+    bool bad = false;
+    if (blk.mode == HSD_MODE_NORMAL) {
+      ptr = bs + blk.valid_count - 1;
+      nxt = p.next_ids[ptr];
+      if (glen + 1 > blk.gen_cap) {
+        bad = true;
+      } else {
+        if (lane == 0) gen[glen] = nxt;
+        glen += 1;
+        inc = 1;
+        or_range(vis, kvb + bs, kvb + ptr, lane, false);
+      }
+    } else if (blk.mode == HSD_MODE_SPEC) {
+      ptr = bs + blk.valid_count - 1;
+      int diff = blen - 1;
+      for (int base = 0; base < blen - 1; base += 32) {
+        const int i = base + lane;
+        const bool miss = (i < blen - 1) && (p.next_ids[bs + i] != p.input_ids[bs + i + 1]);
+        const uint32_t bal = __ballot_sync(0xffffffffu, miss);
         if (bal) {
-          child = base + __ffs(bal) - 1;
+          diff = base + __ffs(bal) - 1;
           break;
         }
       }
-      if (child < 0) break;
-      node = child;
-      new_index = child;
-      decode = p.next_ids[bs + child];
-      if (lane == 0) gen[glen] = decode;
-      glen += 1;
-      ++walked;
-      if (lane == (child >> 5)) visited |= 1u << (child & 31);
-    }
-    ptr = bs + new_index;
-    nxt = decode;
-    inc = 1 + walked;
-    // every column of the block off the accepted path is filtered (D:1271-1279)
-    for (int j0 = 0; j0 < blen; j0 += 64) {
-      // build the 64-column word for block columns [j0, j0+64) from the visited bits
-      const uint32_t lo = __shfl_sync(0xffffffffu, visited, (j0 >> 5) & 31);
-      const uint32_t hi = __shfl_sync(0xffffffffu, visited, ((j0 >> 5) + 1) & 31);
-      uint64_t v = (j0 < kMaxTreeNodes) ? ((uint64_t(j0 + 32 < kMaxTreeNodes ? hi : 0) << 32) | lo)
-                                        : 0ull;
-      const int rem = blen - j0;
-      const uint64_t span = rem >= 64 ? ~0ull : ((1ull << rem) - 1ull);
-      const uint64_t dead = ~v & span, keep = v & span;
-      if (lane == 0) {
-        // columns kvb + bs + j0 + k, k < 64: may straddle two words
-        const int c0 = kvb + bs + j0;
-        const int w = c0 >> 6, sh = c0 & 63;
-        if (dead) {
-          atomicOr(reinterpret_cast<unsigned long long*>(p.filter_bits + w), dead << sh);
-          if (sh && (dead >> (64 - sh)))
-            atomicOr(reinterpret_cast<unsigned long long*>(p.filter_bits + w + 1),
-                     dead >> (64 - sh));
+      if (glen + diff + 1 > blk.gen_cap) {
+        bad = true;
+      } else {
+        nxt = p.next_ids[bs + diff];
+        for (int i = lane; i <= diff; i += 32)
+          gen[glen + i] = (i < diff) ? p.input_ids[bs + i + 1] : nxt;
+        glen += diff + 1;
+        inc = diff + 1;
+        if (diff != blen - 1) {
+          ptr = bs + diff;
+          op.kind = 1;
+          op.lo = kvb + bs + diff + 1;
+          op.hi = kvb + bs + blen - 1;
         }
-        if (keep) {
-          vis[w] |= keep << sh;
-          if (sh && (keep >> (64 - sh))) vis[w + 1] |= keep >> (64 - sh);
+        or_range(vis, kvb + bs, kvb + ptr, lane, false);
+      }
+    } else if (blk.mode == HSD_MODE_TREE) {
+      const int32_t* tok = p.tree_tokens + blk.tree_off;
+      const int32_t* par = p.tree_parents + blk.tree_off;
+      const int n = min(blk.tree_nodes, blen);
+      int decode = p.next_ids[bs];
+      int node = 0, walked = 0;
+      if (glen + n > blk.gen_cap) {
+        bad = true;
+      } else {
+        if (lane == 0) gen[glen] = decode;
+        glen += 1;
+        op.kind = 2;
+        op.lo = kvb + bs;
+        op.hi = kvb + bs + blen - 1;
+        op.path[0] = 0;
+        op.n_path = 1;
+        for (int guard = 0; guard < n; ++guard) {
+          int child = -1;
+          for (int base = node + 1; base < n; base += 32) {
+            const int c = base + lane;
+            const bool hit = c < n && par[c] == node && tok[c] == decode;
+            const uint32_t bal = __ballot_sync(0xffffffffu, hit);
+            if (bal) {
+              child = base + __ffs(bal) - 1;
+              break;
+            }
+          }
+          if (child < 0) break;
+          if (op.n_path >= kMaxPath) {
+            bad = true;
+            break;
+          }
+          node = child;
+          decode = p.next_ids[bs + child];
+          if (lane == 0) gen[glen] = decode;
+          glen += 1;
+          ++walked;
+          op.path[op.n_path++] = int16_t(child);
+        }
+        ptr = bs + node;
+        nxt = decode;
+        inc = 1 + walked;
+        if (lane == 0)
+          for (int k = 0; k < op.n_path; ++k) {
+            const int c = kvb + bs + op.path[k];
+            vis[c >> 6] |= 1ull << (c & 63);
+          }
+      }
+    } else {
+      bad = true;
+    }
+    if (bad) {
+      report(p.status, HSD_DEV_CAPACITY | 1);
+      op.kind = 0;
+      if (lane == 0) ops[b] = op;
+      continue;
+    }
+    __syncwarp();
+
+    // window update (D:1121-1124, D:1201-1204, D:1288-1291)
+    const int mws = (blk.matches_len == 0 || blk.matches_len == 1) ? cfg.match_window_size
+                                                                   : blk.mws + inc;
+    res.increment = inc;
+    res.pointer = ptr;
+    res.next_token = nxt;
+
+    // EOS stop (D:1299-1305) and repetition stop (D:1306-1319); their
+    // filter update (the pointer row) is applied in phase 2.
+    const bool page_block = (blk.flags & 1) != 0;
+    int finished = 0;
+    if (is_eos(cfg, gen[glen - 1])) {
+      finished = 1;
+      glen -= 1;
+    } else if (!page_block) {
+      const int tl = min(10, glen);
+      int count, first;
+      count_matches(gen, glen, gen + glen - tl, tl, lane, count, first);
+      bool sentinel = false;
+      for (int i = lane; i < glen; i += 32) sentinel |= (gen[i] == cfg.repeat_sentinel);
+      sentinel = __any_sync(0xffffffffu, sentinel);
+      if (count > 10 && !sentinel) {
+        if (blk.draft_len > blk.gen_cap) {
+          report(p.status, HSD_DEV_CAPACITY | 4);
+        } else {
+          finished = 2;
+          __syncwarp();
+          for (int i = lane; i < blk.draft_len; i += 32) gen[i] = p.draft_pool[blk.draft_off + i];
+          glen = blk.draft_len;
         }
       }
     }
-  } else {
-    report(p.status, HSD_DEV_BAD_INDEX | 3);
-    return;
+    __syncwarp();
+    if (finished) {
+      op.finished = 1;
+      blk.mode = HSD_MODE_FINISHED;
+    } else if (!page_block) {
+      // KMP re-alignment (D:1321-1336)
+      const int w = min(cfg.match_window_size_upper_bound, mws);
+      const int wl = min(w, glen);
+      int count, first;
+      count_matches(p.draft_pool + blk.draft_off, blk.draft_len, gen + glen - wl, wl, lane,
+                    count, first);
+      res.match_count = count;
+      res.match_start = first;
+      blk.matches_len = count;
+      if (count == 1) {
+        res.slice_begin = first + wl - 1;
+        int end = blk.draft_len;
+        if (cfg.max_spec_len > 0 && end - res.slice_begin > cfg.max_spec_len)
+          end = res.slice_begin + cfg.max_spec_len;
+        res.slice_end = end;
+      }
+    }
+    res.finished = finished;
+    blk.gen_len = glen;
+    blk.mws = mws;
+    __syncwarp();
+    if (lane == 0) {
+      p.results[b] = res;
+      p.blocks[b] = blk;
+      ops[b] = op;
+    }
   }
-  __syncwarp();
-
-  // window update (D:1121-1124, D:1201-1204, D:1288-1291)
-  int mws = (blk.matches_len == 0 || blk.matches_len == 1) ? cfg.match_window_size
-                                                           : blk.mws + inc;
-  res.increment = inc;
-  res.pointer = ptr;
-  res.next_token = nxt;
-
-  // EOS stop (D:1299-1305): the pointer row's columns are filtered.
-  const bool page_block = (blk.flags & 1) != 0;
-  int finished = 0;
-  if (is_eos(cfg, gen[glen - 1])) {
-    finished = 1;
-    glen -= 1;
-  } else if (!page_block) {
-    // repetition stop (D:1306-1319)
-    const int tl = min(10, glen);
-    int count, first;
-    count_matches(gen, glen, gen + glen - tl, tl, lane, count, first);
-    bool sentinel = false;
-    for (int i = lane; i < glen; i += 32) sentinel |= (gen[i] == cfg.repeat_sentinel);
-    sentinel = __any_sync(0xffffffffu, sentinel);
-    if (count > 10 && !sentinel) {
-      finished = 2;
-      if (blk.draft_len > blk.gen_cap) {
-        report(p.status, HSD_DEV_CAPACITY | 4);
-        return;
-      }
+  __syncthreads();
+  if (warp_id() != 0) return;
+  // Phase 2: replay the filter operations in block order.
+  for (int b = 0; b < cfg.n_blocks; ++b) {
+    const FilterOp& op = ops[b];
+    if (op.kind == 1) {
+      or_range(p.filter_bits, op.lo, op.hi, lane, false);
+    } else if (op.kind == 2) {
+      if (lane == 0)
+        for (int k = 0; k < op.n_path; ++k) {
+          const int c = op.lo + op.path[k];
+          p.filter_bits[c >> 6] |= 1ull << (c & 63);
+        }
       __syncwarp();
-      for (int i = lane; i < blk.draft_len; i += 32) gen[i] = p.draft_pool[blk.draft_off + i];
-      glen = blk.draft_len;
+      for (int w = (op.lo >> 6) + lane; w <= (op.hi >> 6); w += 32)
+        p.filter_bits[w] ^= word_range(w, op.lo, op.hi);
     }
-  }
-  __syncwarp();
-  if (finished) {
-    for (int w = lane; w < nwords; w += 32)
-      atomicOr(reinterpret_cast<unsigned long long*>(p.filter_bits + w), vis[w]);
-    blk.mode = HSD_MODE_FINISHED;
-  } else if (!page_block) {
-    // KMP re-alignment (D:1321-1336)
-    const int w = min(cfg.match_window_size_upper_bound, mws);
-    const int wl = min(w, glen);
-    int count, first;
-    count_matches(p.draft_pool + blk.draft_off, blk.draft_len, gen + glen - wl, wl, lane, count,
-                  first);
-    res.match_count = count;
-    res.match_start = first;
-    blk.matches_len = count;
-    if (count == 1) {
-      res.slice_begin = first + wl - 1;
-      int end = blk.draft_len;
-      if (cfg.max_spec_len > 0 && end - res.slice_begin > cfg.max_spec_len)
-        end = res.slice_begin + cfg.max_spec_len;
-      res.slice_end = end;
+    __syncwarp();
+    if (op.finished) {
+      const uint64_t* vis = p.out_kv_bits + size_t(b) * stride;
+      for (int w = lane; w < nwords; w += 32) p.filter_bits[w] |= vis[w];
     }
-  }
-  res.finished = finished;
-  blk.gen_len = glen;
-  blk.mws = mws;
-  if (lane == 0) {
-    p.results[b] = res;
-    p.blocks[b] = blk;
+    __syncwarp();
   }
 }
 
@@ -292,6 +336,8 @@ __global__ void __launch_bounds__(128) accept_kmp_kernel(Params p) {
 }  // namespace hsd
 
 using namespace hsd;
+
+static constexpr int kMaxBlocks = 1024;
 
 extern "C" int hsd_accept_kmp(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
                               hsd_block_result_t* results, const int32_t* next_ids,
@@ -321,8 +367,18 @@ extern "C" int hsd_accept_kmp(const hsd_accept_config_t* cfg, hsd_block_t* block
   p.out_kv_bits = out_kv_bits;
   p.filter_bits = filter_bits;
   p.status = status;
-  const int threads = 128;
-  const int grid = (cfg->n_blocks * 32 + threads - 1) / threads;
-  acc::accept_kmp_kernel<<<grid, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  if (cfg->n_blocks > kMaxBlocks) {
+    hsd_host::set_error("hsd_accept_kmp: %d blocks > %d", cfg->n_blocks, kMaxBlocks);
+    return HSD_ERR_TOO_LARGE;
+  }
+  const int warps = cfg->n_blocks < 32 ? cfg->n_blocks : 32;
+  const size_t smem = size_t(cfg->n_blocks) * sizeof(acc::FilterOp);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(acc::accept_kmp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         int(kMaxBlocks * sizeof(acc::FilterOp)));
+    attr = true;
+  }
+  acc::accept_kmp_kernel<<<1, warps * 32, smem, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   return hsd_host::cuda_check(cudaGetLastError(), "accept_kmp_kernel launch");
 }

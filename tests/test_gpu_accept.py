@@ -1,0 +1,107 @@
+"""GPU parity: acceptance + KMP re-alignment kernel vs the oracle (bit-exact).
+
+Checks per block: result fields (finished, increment, pointer, next token,
+match count / first start / next slice), the updated state (generated
+tokens, window size, match count, mode), the step's filter bits, and the
+block's new visibility row (= the mask row at its pointer, which the next
+step inherits, D:1634-1667).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import accept as OA
+from tests import accept_cases as AC
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch.device("cuda:0")
+
+
+def run_kernel(sc, dev, page_block=None):
+    from hsd_b200 import accept as A
+    from hsd_b200.plan import pack_bits
+    nb = len(sc["blocks"])
+    kv_len = sc["kv_len"]
+    stride = (kv_len + 63) // 64 + 1
+    blocks = np.zeros((nb, 16), dtype=np.int32)
+    gen_pool = np.zeros(nb * AC.CAP, dtype=np.int32)
+    drafts, tree_tok, tree_par = [], [], []
+    seg_bits = np.zeros((nb, stride), dtype=np.uint64)
+    doff = toff = 0
+    for i, blk in enumerate(sc["blocks"]):
+        f = A.F
+        blocks[i, f["mode"]] = blk["mode"]
+        blocks[i, f["q_start"]] = blk["q_start"]
+        blocks[i, f["q_len"]] = blk["q_len"]
+        blocks[i, f["valid_count"]] = blk["valid"] or 0
+        blocks[i, f["gen_off"]] = i * AC.CAP
+        blocks[i, f["gen_len"]] = len(blk["gen"])
+        blocks[i, f["gen_cap"]] = AC.CAP
+        gen_pool[i * AC.CAP:i * AC.CAP + len(blk["gen"])] = blk["gen"]
+        blocks[i, f["draft_off"]] = doff
+        blocks[i, f["draft_len"]] = len(blk["draft"])
+        drafts += blk["draft"]
+        doff += len(blk["draft"])
+        blocks[i, f["mws"]] = blk["mws"]
+        blocks[i, f["matches_len"]] = blk["matches_len"]
+        if blk["tree"]:
+            toks, pars = blk["tree"]
+            blocks[i, f["tree_off"]] = toff
+            blocks[i, f["tree_nodes"]] = len(toks)
+            tree_tok += list(toks)
+            tree_par += list(pars)
+            toff += len(toks)
+        blocks[i, f["seg"]] = i
+        blocks[i, f["flags"]] = 1 if i == page_block else 0
+        seg_bits[i, :(kv_len + 63) // 64] = pack_bits(blk["kv"])
+    t = lambda a, dt=torch.int32: torch.as_tensor(np.asarray(a), dtype=dt).to(dev)
+    cfg = A.make_config(nb, kv_len, sc["q_len"], stride, sc["eos"])
+    d_blocks = t(blocks)
+    d_gen = t(gen_pool)
+    out_bits = torch.zeros((nb, stride), dtype=torch.int64, device=dev)
+    filt = torch.zeros(stride, dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    res = A.accept_kmp(cfg, d_blocks, t(sc["next_ids"]), t(sc["input_ids"]), d_gen,
+                       t(drafts or [0]), t(seg_bits.view(np.int64), torch.int64), out_bits, filt,
+                       tree_tokens=t(tree_tok or [0]), tree_parents=t(tree_par or [0]),
+                       status=status)
+    torch.cuda.synchronize()
+    assert status.item() == 0, hex(status.item())
+    return (res.cpu().numpy(), d_blocks.cpu().numpy(), d_gen.cpu().numpy(),
+            out_bits.cpu().numpy(), filt.cpu().numpy())
+
+
+def unpack(words, n):
+    return np.unpackbits(np.ascontiguousarray(words).view(np.uint8), bitorder="little")[:n].astype(bool)
+
+
+@pytest.mark.parametrize("seed", list(range(24)))
+@pytest.mark.parametrize("tight", [False, True])
+def test_accept_kmp_matches_oracle(dev, seed, tight):
+    from hsd_b200 import accept as A
+    sc = AC.make_scenario(seed, tight=tight)
+    page = len(sc["blocks"]) - 1 if seed % 3 == 0 else None
+    expect, filt = run_oracle_checked(sc, page)
+    res, blocks, gen, vis, kfilt = run_kernel(sc, dev, page_block=page)
+    for i, (r, st, row) in enumerate(expect):
+        got = {k: int(res[i, A.R[k]]) for k in A.RESULT_FIELDS}
+        assert got == r, (seed, i, got, r)
+        if r["finished"] == 3:
+            continue
+        glen = int(blocks[i, A.F["gen_len"]])
+        assert gen[i * AC.CAP:i * AC.CAP + glen].tolist() == st.gen, (seed, i)
+        assert int(blocks[i, A.F["mws"]]) == st.mws, (seed, i)
+        assert int(blocks[i, A.F["matches_len"]]) == st.matches_len, (seed, i)
+        assert (int(blocks[i, A.F["mode"]]) == OA.FINISHED) == (st.mode == OA.FINISHED)
+        np.testing.assert_array_equal(unpack(vis[i], sc["kv_len"]), row)
+    np.testing.assert_array_equal(unpack(kfilt, sc["kv_len"]), filt)
+
+
+def run_oracle_checked(sc, page):
+    out, filt = AC.run_oracle(sc, page_block=page)
+    return out, filt
