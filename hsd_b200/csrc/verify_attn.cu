@@ -10,18 +10,22 @@
 // empty 128x64 tiles never appear, partial 64-column halves carry per-row
 // 64-bit masks, absent halves are masked out).
 //
-//   warp 8      TMA producer: Q (once), then K_j and V_j into a 3-slot ring
-//   warp 9      MMA issuer (one thread): S = Q K^T and O += P V on tcgen05,
-//               accumulators in TMEM
+//   warp 8      TMA producer: Q (once), then K_j and V_j into a 5-slot ring
+//   warp 9      MMA issuer (one thread): S = Q K^T (A, B in smem) and
+//               O += P V (P from TMEM, V in smem) on tcgen05
+//   warps 10-11 idle (complete the third warpgroup for setmaxnreg)
 //   warps 0-3   softmax + epilogue of head slot 0 (thread = query row)
 //   warps 4-7   softmax + epilogue of head slot 1
 //
 // TMEM (512 columns): slot s holds S_s at columns [256 s, 256 s + 128) and
-// O_s at [256 s + 128, 256 s + 256), fp32, lane = query row.  P (bf16) goes
-// through shared memory in the 128-byte-swizzled K-major layout the MMA
-// reads.  Softmax keeps a running max in log2 units and rescales O only when
-// the max grows by more than kRescaleLog2 (exact: the final O / l and LSE use
-// the same stale max).
+// O_s at [256 s + 128, 256 s + 256), fp32, lane = query row.  The softmax
+// overwrites the first 64 columns of S_s with P_s (bf16 pairs), which the PV
+// MMA reads as its A operand.  Per slot the MMA thread issues
+// PV_s(j) before S_s(j+1); tcgen05 MMAs of one thread complete in order, so
+// when the softmax sees S_s(j) complete, PV_s(j-1) is complete too -- O can be
+// rescaled and the S/P columns reused without further waits.  Softmax keeps a
+// running max in log2 units and rescales O only when the max grows by more
+// than kRescaleLog2 (exact: the final O / l and LSE use the same stale max).
 #include "common.cuh"
 
 namespace hsd {
@@ -31,21 +35,19 @@ constexpr int BM = 128;  // query rows per tile
 constexpr int BN = 128;  // KV columns per block
 constexpr int HD = 128;  // head dim
 constexpr int NSLOT = 2;
-constexpr int NSTAGE = 3;
+constexpr int NSTAGE = 5;
 constexpr int TILE_BYTES = BN * HD * 2;  // 32 KB: a 128x128 bf16 tile
 constexpr int SUB_BYTES = 128 * 128;     // one 64-column swizzled sub-tile of 128 rows
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;  // 3 warpgroups: softmax slot 0, slot 1, producer + MMA
 constexpr float kRescaleLog2 = 8.0f;
 
 struct __align__(1024) Smem {
   uint8_t q[NSLOT][TILE_BYTES];
   uint8_t kv[NSTAGE][TILE_BYTES];
-  uint8_t p[NSLOT][TILE_BYTES];
   uint64_t bar_q;
   uint64_t bar_full[NSTAGE];
   uint64_t bar_empty[NSTAGE];
   uint64_t bar_s_full[NSLOT];
-  uint64_t bar_s_free[NSLOT];
   uint64_t bar_p_full[NSLOT];
   uint64_t bar_o_done[NSLOT];
   uint64_t bar_final;
@@ -96,7 +98,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < NSLOT; ++i) {
       mbar_init(&sm.bar_s_full[i], 1);
-      mbar_init(&sm.bar_s_free[i], 128);
       mbar_init(&sm.bar_p_full[i], 128);
       mbar_init(&sm.bar_o_done[i], 1);
     }
@@ -114,9 +115,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = sm.tmem_base;
   volatile int* abort = &sm.abort;
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0 && nblk > 0) {
+  // Register split across warpgroups (launch: 384 x 168 = 64512): the
+  // producer/MMA warpgroup keeps 56, each softmax warpgroup gets 224
+  // (2 x 128 x 224 + 128 x 56 = 64512).  Each role's code sits inside the
+  // branch of its own setmaxnreg.
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
+    if (warp == 8 && lane == 0 && nblk > 0) {
+      // ---------------------------------------------------------- producer
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
@@ -154,11 +160,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_wait(&sm.bar_full[i], uint32_t(uses - 1) & 1u, abort, p.status, 0x110 + i, false);
       }
       mbar_wait(&sm.bar_q, 0, abort, p.status, 0x120, false);
-    }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && nblk > 0) {
-      const uint32_t qa0 = smem_u32(sm.q[0]), pa0 = smem_u32(sm.p[0]);
+    } else if (warp == 9 && lane == 0 && nblk > 0) {
+      // ---------------------------------------------------------- MMA issuer
+      const uint32_t qa0 = smem_u32(sm.q[0]);
       bool ok = mbar_wait(&sm.bar_q, 0, abort, p.status, 0x200);
       tc_fence_after();
       int stage = 0;
@@ -169,36 +173,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           ph ^= 1u;
         }
       };
+      // Descriptors advance inside a 128-byte swizzle atom by adding the byte
+      // offset >> 4 to the start-address field; the loops stay rolled so the
+      // warpgroup's small register budget holds.
       auto issue_s = [&](int s, int kstage) {
-        const uint32_t ka = smem_u32(sm.kv[kstage]);
-#pragma unroll
+        const uint64_t a = sdesc_sw128(qa0 + s * TILE_BYTES, 16, 1024);
+        const uint64_t b = sdesc_sw128(smem_u32(sm.kv[kstage]), 16, 1024);
+        const uint32_t d = tmem + s * 256;
+#pragma unroll 1
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * SUB_BYTES + (kk & 3) * 32;
-          umma_bf16_ss(tmem + s * 256, sdesc_sw128(qa0 + s * TILE_BYTES + off, 16, 1024),
-                       sdesc_sw128(ka + off, 16, 1024), kIdescS, kk > 0);
+          const uint64_t off = uint64_t(((kk >> 2) * SUB_BYTES + (kk & 3) * 32) >> 4);
+          umma_bf16_ss(d, a + off, b + off, kIdescS, kk > 0);
         }
       };
       auto issue_pv = [&](int s, int vstage, bool acc) {
-        const uint32_t va = smem_u32(sm.kv[vstage]);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * SUB_BYTES + (kk & 3) * 32;
-          umma_bf16_ss(tmem + s * 256 + 128, sdesc_sw128(pa0 + s * TILE_BYTES + aoff, 16, 1024),
-                       sdesc_sw128(va + kk * 2048, SUB_BYTES, 1024), kIdescO,
+        const uint32_t a = tmem + s * 256;  // P: bf16 pairs in the S columns
+        const uint64_t b = sdesc_sw128(smem_u32(sm.kv[vstage]), SUB_BYTES, 1024);
+        const uint32_t d = tmem + s * 256 + 128;
+#pragma unroll 1
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_bf16_ts(d, a + kk * 8, b + uint64_t((kk * 2048) >> 4), kIdescO,
                        (acc || kk > 0) ? 1u : 0u);
-        }
       };
-      // prologue: S_s,0
-      int kstage = stage;
-      uint32_t kphase = phase;
-      if (ok) ok = mbar_wait(&sm.bar_full[kstage], kphase, abort, p.status, 0x201);
+      // prologue: S_s(0)
+      const int k0 = stage;
+      if (ok) ok = mbar_wait(&sm.bar_full[k0], phase, abort, p.status, 0x201);
       if (ok) {
         tc_fence_after();
         for (int s = 0; s < nslot; ++s) {
-          issue_s(s, kstage);
+          issue_s(s, k0);
           umma_commit(&sm.bar_s_full[s]);
         }
-        umma_commit(&sm.bar_empty[kstage]);
+        umma_commit(&sm.bar_empty[k0]);
       }
       next_stage(stage, phase);
       for (int j = 0; j < nblk && ok; ++j) {
@@ -206,37 +212,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t vphase = phase;
         next_stage(stage, phase);
         const bool more = j + 1 < nblk;
-        int nk = stage;
-        uint32_t nkph = phase;
+        const int nk = stage;
+        const uint32_t nkph = phase;
         if (more) next_stage(stage, phase);
         ok = mbar_wait(&sm.bar_full[vstage], vphase, abort, p.status, 0x202);
-        if (ok && more) ok = mbar_wait(&sm.bar_full[nk], nkph, abort, p.status, 0x203);
         if (!ok) break;
-        tc_fence_after();
         for (int s = 0; s < nslot && ok; ++s) {
-          if (more) {
-            ok = mbar_wait(&sm.bar_s_free[s], j & 1, abort, p.status, 0x204);
-            if (!ok) break;
-            tc_fence_after();
-            issue_s(s, nk);
-            umma_commit(&sm.bar_s_full[s]);
-          }
           ok = mbar_wait(&sm.bar_p_full[s], j & 1, abort, p.status, 0x205);
           if (!ok) break;
           tc_fence_after();
           issue_pv(s, vstage, j > 0);
           umma_commit(&sm.bar_o_done[s]);
+          if (more) {
+            if (s == 0) {
+              ok = mbar_wait(&sm.bar_full[nk], nkph, abort, p.status, 0x203);
+              if (!ok) break;
+              tc_fence_after();
+            }
+            issue_s(s, nk);
+            umma_commit(&sm.bar_s_full[s]);
+          }
         }
-        if (more) umma_commit(&sm.bar_empty[nk]);
+        if (!ok) break;
         umma_commit(&sm.bar_empty[vstage]);
+        if (more) umma_commit(&sm.bar_empty[nk]);
       }
       // every MMA this thread issued has completed once bar_final fires
       umma_commit(&sm.bar_final);
-      mbar_wait(&sm.bar_final, 0, abort, p.status, 0x206);
+      mbar_wait(&sm.bar_final, 0, abort, p.status, 0x206, false);
     }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;\n" ::: "memory");
     // ------------------------------------------------------------ softmax
-    const int s = warp >> 2;      // head slot
+    const int s = warp >> 2;       // head slot
     const int quarter = warp & 3;  // TMEM lane quarter
     const int r = quarter * 32 + lane;
     const int q = qt * BM + r;
@@ -244,89 +252,87 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
     const uint32_t t_s = tmem + lane_off + s * 256;
     const uint32_t t_o = t_s + 128;
-    const uint32_t p_row = smem_u32(sm.p[s]) + r * 128;
-    const uint32_t swz = uint32_t(r & 7);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     if (s < nslot) {
       for (int j = 0; j < nblk && ok; ++j) {
         const uint32_t e = list[j];
         const int kb = int(e & 0xFFFFFFu);
-        ok = __all_sync(0xffffffffu, mbar_wait(&sm.bar_s_full[s], j & 1, abort, p.status, 0x300 + s));
-        if (!ok) break;
-        tc_fence_after();
-        float x[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t u[32];
-          tmem_ld32(t_s + c * 32, u);
-          tmem_wait_ld(u);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(u[i]);
-        }
-        tc_fence_before();
-        mbar_arrive(&sm.bar_s_free[s]);
-        // mask: absent halves out, partial halves by their row word
+        // mask words: absent half = 0, full half = ~0, partial half = its row word
+        uint32_t mw[4];
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           const bool present = (e >> (24 + 2 * hf)) & 1u;
           const bool partial = (e >> (25 + 2 * hf)) & 1u;
-          if (!present) {
-#pragma unroll
-            for (int i = 0; i < 64; ++i) x[hf * 64 + i] = -INFINITY;
-          } else if (partial) {
-            const uint64_t w =
-                p.mask_words[(size_t(qt) * p.n_kv64 + 2 * kb + hf) * 128 + r];
-#pragma unroll
-            for (int i = 0; i < 64; ++i)
-              if (!((w >> i) & 1ull)) x[hf * 64 + i] = -INFINITY;
-          }
+          uint64_t w = present ? ~0ull : 0ull;
+          if (partial) w = p.mask_words[(size_t(qt) * p.n_kv64 + 2 * kb + hf) * 128 + r];
+          mw[2 * hf] = uint32_t(w);
+          mw[2 * hf + 1] = uint32_t(w >> 32);
         }
-        float mx = x[0];
+        ok = __all_sync(0xffffffffu, mbar_wait(&sm.bar_s_full[s], j & 1, abort, p.status,
+                                               0x300 + s));
+        if (!ok) break;
+        tc_fence_after();
+        // S row -> registers: four loads in flight, one wait
+        uint32_t u[4][32];
 #pragma unroll
-        for (int i = 1; i < 128; ++i) mx = fmaxf(mx, x[i]);
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, u[c]);
+        tmem_wait_ld(u[0]);
+        tmem_wait_ld(u[1]);
+        tmem_wait_ld(u[2]);
+        tmem_wait_ld(u[3]);
+        float x[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(u[c][i]);
+        if ((mw[0] & mw[1] & mw[2] & mw[3]) != 0xffffffffu) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            x[i] = ((mw[i >> 5] >> (i & 31)) & 1u) ? x[i] : -INFINITY;
+        }
+        // row max: eight independent chains, then a tree
+        float mx8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = x[k];
+#pragma unroll
+        for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], x[i]);
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         const float m_new = fmaxf(m, mx * p.scale_log2);
         const bool need = m_new > m + kRescaleLog2;  // also true for m = -inf, m_new finite
         const float alpha = need ? ex2_approx(m - m_new) : 1.f;
         if (need) m = m_new;
-        const float m_use = (m == -INFINITY) ? 0.f : m;
-        float sum = 0.f;
-        uint32_t pk[64];
+        const float nm = (m == -INFINITY) ? 0.f : -m;
+        // O holds sum_{i<j} P_i V_i (PV(j-1) completed before S(j)); rescale it
+        // when this block raised the max.
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const float a = ex2_approx(fmaf(x[2 * i], p.scale_log2, -m_use));
-          const float b = ex2_approx(fmaf(x[2 * i + 1], p.scale_log2, -m_use));
-          sum += a + b;
-          pk[i] = pack_bf16x2(a, b);
-        }
-        l = l * alpha + sum;
-        // PV_{j-1} must be done before O is rescaled or P is overwritten.
-        if (j > 0) {
-          ok = __all_sync(0xffffffffu,
-                          mbar_wait(&sm.bar_o_done[s], (j - 1) & 1, abort, p.status, 0x310 + s));
-          if (!ok) break;
-          tc_fence_after();
-          if (__any_sync(0xffffffffu, need)) {
+          for (int c = 0; c < 8; ++c) {
+            uint32_t o[16];
+            tmem_ld16(t_o + c * 16, o);
+            tmem_wait_ld16(o);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              uint32_t u[32];
-              tmem_ld32(t_o + c * 32, u);
-              tmem_wait_ld(u);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
-              tmem_st32(t_o + c * 32, u);
-            }
-            tmem_wait_st();
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st16(t_o + c * 16, o);
           }
         }
-        // P row -> swizzled K-major smem (two 64-column sub-tiles)
+        // P = exp2(s * scale - m) -> bf16 pairs -> TMEM columns [0, 64) of S
+        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c8 = 0; c8 < 16; ++c8) {
-          const uint32_t sub = c8 >> 3, chunk = c8 & 7;
-          const uint32_t addr = p_row + sub * SUB_BYTES + ((chunk ^ swz) << 4);
-          st_shared_v4(addr, pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float a = ex2_approx(fmaf(x[64 * c + 2 * i], p.scale_log2, nm));
+            const float b = ex2_approx(fmaf(x[64 * c + 2 * i + 1], p.scale_log2, nm));
+            sum4[i & 3] += a + b;
+            pk[i] = pack_bf16x2(a, b);
+          }
+          tmem_st32(t_s + c * 32, pk);
         }
-        fence_async_shared();
+        l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+        tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&sm.bar_p_full[s]);
       }

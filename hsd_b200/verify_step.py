@@ -1,0 +1,216 @@
+"""One verification step of a packed page, entirely on the device.
+
+This is the hot path of the reference's ``batch_generate`` iteration
+(hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py D:1053-1767) minus the dense
+decoder GEMMs, which stay in the model:
+
+1. KV append of the step's new rows into the layer caches (what
+   ``DynamicCache.update`` does with ``torch.cat``, D:356-359),
+2. tile plan from the segment descriptors (replaces the dense mask build and
+   ``create_block_mask``, D:94-106, D:1634-1667),
+3. packed verification attention on every layer (D:72-135),
+4. acceptance + KMP re-alignment of every block (D:1103-1336),
+5. keep indices and in-place compaction of every layer's K and V
+   (D:1669-1735), plus the remap of each block's visibility row.
+
+``VerifyStep.run()`` launches all of it on one stream without a host sync.
+``VerifyStep.run_from_host()`` is the end-to-end form: the step's inputs come
+from pinned host buffers and the per-block results go back to the host.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import _native as N
+from .accept import F as BF
+from .accept import make_config
+from .plan import PackedMask, TilePlan, pack_bits
+
+
+class VerifyStep:
+    def __init__(self, page, device="cuda", seed=0, period=1):
+        self.page = page
+        self.device = torch.device(device)
+        dev = self.device
+        L, hq, hkv, d = page.layers, page.hq, page.hkv, page.head_dim
+        self.L, self.hq, self.hkv, self.d = L, hq, hkv, d
+        self.q_len, self.kv_len, self.prefix = page.q_len, page.kv_len, page.prefix
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        s = 1.0 / np.sqrt(d)
+
+        def rnd(*shape):
+            return (torch.randn(*shape, generator=g) * s).to(torch.bfloat16)
+
+        # step inputs (device-resident for run(); mirrored in pinned host memory
+        # for run_from_host())
+        self.q = rnd(L, hq, self.q_len, d).to(dev)
+        self.new_kv = rnd(L, 2, hkv, self.q_len, d).to(dev)
+        # layer caches [L][K/V][Hkv][kv_len][D]; the prefix rows are resident state
+        self.cache = torch.empty(L, 2, hkv, self.kv_len, d, dtype=torch.bfloat16, device=dev)
+        self.cache[:, :, :, :self.prefix] = rnd(L, 2, hkv, self.prefix, d).to(dev)
+        self.out = torch.empty(L, self.q_len, hq, d, dtype=torch.bfloat16, device=dev)
+        self.lse = torch.empty(L, hq, self.q_len, dtype=torch.float32, device=dev)
+
+        from .workloads import segment_dicts
+        self.mask = PackedMask(self.q_len, self.kv_len, segment_dicts(page), device=dev)
+        self.plan = TilePlan(self.q_len, self.kv_len, dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+        # acceptance inputs
+        segs = page.segments
+        nb = len(segs)
+        self.n_blocks = nb
+        self.stride = self.mask.stride
+        cap = max(len(sg.gen) + sg.q_len + 8 for sg in segs)
+        cap = max(cap, max(len(sg.draft) for sg in segs))
+        blocks = np.zeros((nb, 16), dtype=np.int32)
+        gen_pool = np.zeros(nb * cap, dtype=np.int32)
+        drafts = []
+        doff = 0
+        for i, sg in enumerate(segs):
+            blocks[i, BF["mode"]] = N.HSD_MODE_SPEC
+            blocks[i, BF["q_start"]] = sg.q_start
+            blocks[i, BF["q_len"]] = sg.q_len
+            blocks[i, BF["valid_count"]] = sg.q_len
+            blocks[i, BF["gen_off"]] = i * cap
+            blocks[i, BF["gen_len"]] = len(sg.gen)
+            blocks[i, BF["gen_cap"]] = cap
+            gen_pool[i * cap:i * cap + len(sg.gen)] = sg.gen
+            blocks[i, BF["draft_off"]] = doff
+            blocks[i, BF["draft_len"]] = len(sg.draft)
+            drafts += sg.draft
+            doff += len(sg.draft)
+            blocks[i, BF["mws"]] = 3
+            blocks[i, BF["matches_len"]] = 1
+            blocks[i, BF["seg"]] = i
+        self.blocks0 = torch.from_numpy(blocks).to(dev)
+        self.blocks = self.blocks0.clone()
+        self.gen_pool = torch.from_numpy(gen_pool).to(dev)
+        self.draft_pool = torch.from_numpy(np.asarray(drafts, dtype=np.int32)).to(dev)
+        self.input_ids = torch.from_numpy(page.input_ids).to(dev)
+        self.next_ids = torch.from_numpy(page.next_ids).to(dev)
+        self.results = torch.zeros(nb, 8, dtype=torch.int32, device=dev)
+        self.vis = torch.zeros(nb, self.stride, dtype=torch.int64, device=dev)
+        self.vis_next = torch.zeros_like(self.vis)
+        self.filter = torch.zeros(self.stride, dtype=torch.int64, device=dev)
+        self.keep_bits = torch.zeros(self.stride, dtype=torch.int64, device=dev)
+        self.keep_idx = torch.zeros(self.kv_len, dtype=torch.int32, device=dev)
+        self.counts = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.tree_dummy = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.cfg = make_config(nb, self.kv_len, self.q_len, self.stride, [2**31 - 1])
+        planes = []
+        for l in range(L):
+            for kv in range(2):
+                for h in range(hkv):
+                    planes.append(self.cache[l, kv, h].data_ptr())
+        self.planes = torch.tensor(planes, dtype=torch.int64, device=dev)
+        self.row_bytes = d * 2
+        self.period = period
+        self._host = None
+        self.attn_launches_per_step = L
+        self.kernel_launches_per_step = 2 + L + 1 + 1 + 1 + 1
+
+    # ------------------------------------------------------------------
+    def _ptr(self, t):
+        return C.c_void_p(t.data_ptr())
+
+    def run(self, stream=None, attn_events=None):
+        """Launch one verification step on ``stream`` (no host sync)."""
+        lib = N.load()
+        st = N.stream_handle(stream)
+        p = self._ptr
+        # 1. KV append (the model's cache update)
+        self.cache[:, :, :, self.prefix:self.prefix + self.q_len].copy_(self.new_kv)
+        self.filter.zero_()
+        self.blocks.copy_(self.blocks0)
+        # 2. tile plan
+        m = self.mask
+        N.check(lib.hsd_build_plan_segments(
+            p(m.segs), m.n_segs, p(m.row_seg), p(m.kv_bits), m.stride, p(m.tree_bits),
+            C.byref(self.plan.struct), p(self.status), st), "hsd_build_plan_segments")
+        # 3. attention, every layer
+        scale = 1.0 / np.sqrt(self.d)
+        ql, kvl, hq, hkv, d = self.q_len, self.kv_len, self.hq, self.hkv, self.d
+        for l in range(self.L):
+            q = self.q[l]
+            k = self.cache[l, 0]
+            v = self.cache[l, 1]
+            if attn_events is not None:
+                attn_events[l][0].record(stream)
+            N.check(lib.hsd_verify_attention(
+                p(q), q.stride(1), q.stride(0), p(k), k.stride(1), k.stride(0), p(v), v.stride(1),
+                v.stride(0), p(self.out[l]), p(self.lse[l]), ql, kvl, hq, hkv, d, scale,
+                C.byref(self.plan.struct), p(self.status), st), "hsd_verify_attention")
+            if attn_events is not None:
+                attn_events[l][1].record(stream)
+        # 4. acceptance + KMP
+        N.check(lib.hsd_accept_kmp(
+            C.byref(self.cfg), p(self.blocks), p(self.results), p(self.next_ids),
+            p(self.input_ids), p(self.gen_pool), p(self.draft_pool), p(self.tree_dummy),
+            p(self.tree_dummy), p(m.kv_bits), p(self.vis), p(self.filter), p(self.status), st),
+            "hsd_accept_kmp")
+        # 5. keep indices, in-place compaction, visibility remap
+        N.check(lib.hsd_keep_indices(p(self.vis), self.n_blocks, self.stride, p(self.filter),
+                                     self.kv_len, p(self.keep_bits), p(self.keep_idx),
+                                     p(self.counts), st), "hsd_keep_indices")
+        N.check(lib.hsd_compact_kv(p(self.planes), self.planes.numel(), self.row_bytes,
+                                   p(self.keep_idx), -1, p(self.counts), p(self.status), st),
+                "hsd_compact_kv")
+        N.check(lib.hsd_compact_bits(p(self.vis), p(self.vis_next), self.n_blocks, self.stride,
+                                     p(self.keep_idx), p(self.counts), self.stride, st),
+                "hsd_compact_bits")
+
+    # ------------------------------------------------------------------
+    def host_buffers(self):
+        """Pinned host copies of the step's inputs (end-to-end form)."""
+        if self._host is None:
+            self._host = dict(
+                q=self.q.cpu().pin_memory(), new_kv=self.new_kv.cpu().pin_memory(),
+                input_ids=self.input_ids.cpu().pin_memory(),
+                next_ids=self.next_ids.cpu().pin_memory(),
+                results=torch.empty_like(self.results, device="cpu").pin_memory(),
+                counts=torch.empty_like(self.counts, device="cpu").pin_memory())
+        return self._host
+
+    def h2d_bytes(self):
+        h = self.host_buffers()
+        return sum(h[k].numel() * h[k].element_size() for k in ("q", "new_kv", "input_ids",
+                                                                  "next_ids"))
+
+    def d2h_bytes(self):
+        h = self.host_buffers()
+        return sum(h[k].numel() * h[k].element_size() for k in ("results", "counts"))
+
+    def run_from_host(self, stream=None):
+        """End-to-end step: pinned host inputs -> device step -> results to host."""
+        h = self.host_buffers()
+        self.q.copy_(h["q"], non_blocking=True)
+        self.new_kv.copy_(h["new_kv"], non_blocking=True)
+        self.input_ids.copy_(h["input_ids"], non_blocking=True)
+        self.next_ids.copy_(h["next_ids"], non_blocking=True)
+        self.run(stream)
+        h["results"].copy_(self.results, non_blocking=True)
+        h["counts"].copy_(self.counts, non_blocking=True)
+
+    # ------------------------------------------------------------------
+    def attention_flops(self):
+        """(executed-tile FLOPs, allowed-pair FLOPs) per attention launch.
+
+        Executed tiles are FlexAttention's 128x64 tiles (partial + full) of the
+        plan: FLOPs = tiles * 128 * 64 * 4 * D * Hq; allowed pairs likewise
+        count only unmasked (q, kv) pairs.
+        """
+        cls = self.plan.tile_class().cpu().numpy()
+        tiles = int((cls != 0).sum())
+        words = self.plan.mask_words().cpu().numpy().view(np.uint64)
+        pairs = int(np.unpackbits(words.view(np.uint8)).sum())
+        f = 4 * self.d * self.hq
+        return tiles * 128 * 64 * f, pairs * f, tiles, pairs
+
+    def raise_on_device_error(self):
+        code = int(self.status.item())
+        if code:
+            raise N.HSDError(f"device status 0x{code:x} during the verification step")
