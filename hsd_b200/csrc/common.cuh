@@ -66,7 +66,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the phase with the given parity to complete.  Gives up
 // (returns false) when `abort` (shared flag) is raised by another warp, when
-// another CTA has already reported an error, or after kWaitLimitNs.
+// another CTA has already reported an error, or after kWaitLimitNs.  The fast
+// path is a tight poll of the barrier; the shared abort flag is read every 64
+// polls and the global status word only once a wait has lasted 100 us, so a
+// healthy pipeline never pays a global-memory round trip per spin.
+constexpr uint64_t kSlowCheckNs = 100ull * 1000ull;
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           int32_t* status, int32_t where,
                                           bool honour_abort = true) {
@@ -74,14 +79,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i)
+    for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (honour_abort && *abort) return false;
+    const uint64_t dt = globaltimer_ns() - t0;
+    if (dt < kSlowCheckNs) continue;
     if (honour_abort && status && *reinterpret_cast<volatile int32_t*>(status) != 0) {
       *abort = 1;
       return false;
     }
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (dt > kWaitLimitNs) {
       report(status, HSD_DEV_TIMEOUT | where);
       *abort = 1;
       return false;
@@ -132,14 +139,15 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc], bf16 inputs, fp32 accumulate.
+// No "memory" clobber: ordering against the data it reads comes from the
+// mbarrier waits and tcgen05 fences around it (volatile asm keeps order).
 __device__ __forceinline__ void umma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                              uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 // D[tmem] (+)= A[tmem] * B[smem desc]: A (M x 16 bf16) is read from tensor
@@ -150,8 +158,7 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, u
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 // Arrive on `bar` once every tcgen05 async operation this thread issued so

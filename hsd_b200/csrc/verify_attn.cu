@@ -71,6 +71,29 @@ struct Params {
 constexpr uint32_t kIdescS = idesc_bf16_f32(BM, BN, false, false);  // Q K^T: both K-major
 constexpr uint32_t kIdescO = idesc_bf16_f32(BM, HD, false, true);   // P V: V is MN-major
 
+// S = Q K^T for one 128x128 block: 8 MMAs of K = 16.  Descriptors advance
+// inside a 128-byte swizzle atom by adding the byte offset >> 4 to the start
+// address field (two 64-column sub-tiles of 16 KB each).
+__device__ __forceinline__ void issue_s(uint32_t d_tmem, uint32_t q_smem, uint32_t k_smem) {
+  const uint64_t a = sdesc_sw128(q_smem, 16, 1024);
+  const uint64_t b = sdesc_sw128(k_smem, 16, 1024);
+#pragma unroll
+  for (int kk = 0; kk < HD / 16; ++kk) {
+    const uint64_t off = uint64_t(((kk >> 2) * SUB_BYTES + (kk & 3) * 32) >> 4);
+    umma_bf16_ss(d_tmem, a + off, b + off, kIdescS, kk > 0);
+  }
+}
+
+// O (+)= P V: P (bf16 pairs) from TMEM, V MN-major in smem; K step = 16 rows.
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_smem,
+                                         bool acc) {
+  const uint64_t b = sdesc_sw128(v_smem, SUB_BYTES, 1024);
+#pragma unroll
+  for (int kk = 0; kk < BN / 16; ++kk)
+    umma_bf16_ts(d_tmem, p_tmem + kk * 8, b + uint64_t((kk * 2048) >> 4), kIdescO,
+                 (acc || kk > 0) ? 1u : 0u);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     verify_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
@@ -116,11 +139,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = &sm.abort;
 
   // Register split across warpgroups (launch: 384 x 168 = 64512): the
-  // producer/MMA warpgroup keeps 56, each softmax warpgroup gets 224
-  // (2 x 128 x 224 + 128 x 56 = 64512).  Each role's code sits inside the
+  // producer/MMA warpgroup keeps 120, each softmax warpgroup gets 192
+  // (2 x 128 x 192 + 128 x 120 = 64512).  Each role's code sits inside the
   // branch of its own setmaxnreg.
   if (warp >= 8) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 120;\n" ::: "memory");
     if (warp == 8 && lane == 0 && nblk > 0) {
       // ---------------------------------------------------------- producer
       tma_prefetch_desc(&tm_q);
@@ -167,61 +190,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       int stage = 0;
       uint32_t phase = 0;
-      auto next_stage = [&](int& st, uint32_t& ph) {
-        if (++st == NSTAGE) {
-          st = 0;
-          ph ^= 1u;
-        }
-      };
-      // Descriptors advance inside a 128-byte swizzle atom by adding the byte
-      // offset >> 4 to the start-address field; the loops stay rolled so the
-      // warpgroup's small register budget holds.
-      auto issue_s = [&](int s, int kstage) {
-        const uint64_t a = sdesc_sw128(qa0 + s * TILE_BYTES, 16, 1024);
-        const uint64_t b = sdesc_sw128(smem_u32(sm.kv[kstage]), 16, 1024);
-        const uint32_t d = tmem + s * 256;
-#pragma unroll 1
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint64_t off = uint64_t(((kk >> 2) * SUB_BYTES + (kk & 3) * 32) >> 4);
-          umma_bf16_ss(d, a + off, b + off, kIdescS, kk > 0);
-        }
-      };
-      auto issue_pv = [&](int s, int vstage, bool acc) {
-        const uint32_t a = tmem + s * 256;  // P: bf16 pairs in the S columns
-        const uint64_t b = sdesc_sw128(smem_u32(sm.kv[vstage]), SUB_BYTES, 1024);
-        const uint32_t d = tmem + s * 256 + 128;
-#pragma unroll 1
-        for (int kk = 0; kk < BN / 16; ++kk)
-          umma_bf16_ts(d, a + kk * 8, b + uint64_t((kk * 2048) >> 4), kIdescO,
-                       (acc || kk > 0) ? 1u : 0u);
-      };
+      const uint32_t kv0 = smem_u32(sm.kv[0]);
       // prologue: S_s(0)
       const int k0 = stage;
       if (ok) ok = mbar_wait(&sm.bar_full[k0], phase, abort, p.status, 0x201);
       if (ok) {
         tc_fence_after();
         for (int s = 0; s < nslot; ++s) {
-          issue_s(s, k0);
+          issue_s(tmem + s * 256, qa0 + s * TILE_BYTES, kv0 + k0 * TILE_BYTES);
           umma_commit(&sm.bar_s_full[s]);
         }
         umma_commit(&sm.bar_empty[k0]);
       }
-      next_stage(stage, phase);
+      if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
       for (int j = 0; j < nblk && ok; ++j) {
         const int vstage = stage;
         const uint32_t vphase = phase;
-        next_stage(stage, phase);
+        if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
         const bool more = j + 1 < nblk;
         const int nk = stage;
         const uint32_t nkph = phase;
-        if (more) next_stage(stage, phase);
+        if (more) if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
         ok = mbar_wait(&sm.bar_full[vstage], vphase, abort, p.status, 0x202);
         if (!ok) break;
         for (int s = 0; s < nslot && ok; ++s) {
           ok = mbar_wait(&sm.bar_p_full[s], j & 1, abort, p.status, 0x205);
           if (!ok) break;
           tc_fence_after();
-          issue_pv(s, vstage, j > 0);
+          issue_pv(tmem + s * 256 + 128, tmem + s * 256, kv0 + vstage * TILE_BYTES, j > 0);
           umma_commit(&sm.bar_o_done[s]);
           if (more) {
             if (s == 0) {
@@ -229,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (!ok) break;
               tc_fence_after();
             }
-            issue_s(s, nk);
+            issue_s(tmem + s * 256, qa0 + s * TILE_BYTES, kv0 + nk * TILE_BYTES);
             umma_commit(&sm.bar_s_full[s]);
           }
         }
@@ -242,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&sm.bar_final, 0, abort, p.status, 0x206, false);
     }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;\n" ::: "memory");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 192;\n" ::: "memory");
     // ------------------------------------------------------------ softmax
     const int s = warp >> 2;       // head slot
     const int quarter = warp & 3;  // TMEM lane quarter
