@@ -41,7 +41,7 @@ class Plan(C.Structure):
                 ("kv_num_blocks", C.c_void_p), ("kv_indices", C.c_void_p),
                 ("full_kv_num_blocks", C.c_void_p), ("full_kv_indices", C.c_void_p),
                 ("blk_count", C.c_void_p), ("blk_list", C.c_void_p),
-                ("tile_order", C.c_void_p)]
+                ("tile_order", C.c_void_p), ("blk_prefix", C.c_void_p)]
 
 
 class Block(C.Structure):
@@ -74,9 +74,10 @@ SIGNATURES = [
     ("hsd_build_plan_segments", C.c_int,
      [_P, _I32, _P, _P, _I32, _P, C.POINTER(Plan), _P, _P]),
     ("hsd_build_plan_dense", C.c_int, [_P, _I64, C.POINTER(Plan), _P, _P]),
+    ("hsd_attention_workspace_bytes", _SZ, [_I32, _I32, _I32]),
     ("hsd_verify_attention", C.c_int,
      [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64, _P, _P, _I32, _I32, _I32, _I32,
-      _I32, _F, C.POINTER(Plan), _P, _P]),
+      _I32, _F, C.POINTER(Plan), _P, _SZ, _P, _P]),
     ("hsd_compact_kv", C.c_int, [_P, _I32, _I32, _P, _I32, _P, _P, _P]),
     ("hsd_keep_indices", C.c_int, [_P, _I32, _I32, _P, _I32, _P, _P, _P, _P]),
     ("hsd_compact_bits", C.c_int, [_P, _P, _I32, _I32, _P, _P, _I32, _P]),

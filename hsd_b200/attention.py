@@ -12,6 +12,7 @@ nothing is expanded the way ``repeat_kv`` (D:137-146) does.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -20,6 +21,29 @@ from . import _native as N
 from .plan import PackedMask, TilePlan, plan_from_dense
 
 _cache = {"src": None, "plan": None}
+_workspaces = {}
+
+
+class AttentionWorkspace:
+    """Device scratch of the load-balanced schedule (one per device): fp32
+    partial rows of the items an SM's share of the work leaves unfinished,
+    merged by the second kernel of the same call."""
+
+    def __init__(self, nbytes, device):
+        self.buf = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
+        self.base = (self.buf.data_ptr() + 255) & ~255
+        self.nbytes = nbytes
+
+
+def attention_workspace(q_len, hq, hkv, device):
+    """The cached workspace of ``device``, grown to fit (q_len, hq, hkv)."""
+    need = N.load().hsd_attention_workspace_bytes(int(q_len), int(hq), int(hkv))
+    key = torch.device(device).index or 0
+    ws = _workspaces.get(key)
+    if ws is None or ws.nbytes < need:
+        ws = AttentionWorkspace(max(need, 1 << 20), device)
+        _workspaces[key] = ws
+    return ws
 
 
 def _as_heads(x, name):
@@ -38,12 +62,14 @@ def _as_heads(x, name):
 
 
 def verify_attention(q, k, v, plan: TilePlan, scale=None, out=None, lse=None,
-                     need_lse=True, stream=None):
+                     need_lse=True, stream=None, balanced=True):
     """Masked GQA attention over a tile plan.
 
     q: ``[Hq, Q, 128]`` (or ``[1, Hq, Q, 128]``) bf16, any row/head strides;
     k, v: ``[Hkv, KV, 128]`` likewise.  Returns ``(out [Q, Hq, 128] bf16,
-    lse [Hq, Q] fp32 natural log or None)``.
+    lse [Hq, Q] fp32 natural log or None)``.  ``balanced`` selects the
+    stream-K schedule (equal work per SM through the cached workspace);
+    otherwise every (query tile, head pair) gets its own CTA.
     """
     lib = N.load()
     q = _as_heads(q, "query")
@@ -57,17 +83,16 @@ def verify_attention(q, k, v, plan: TilePlan, scale=None, out=None, lse=None,
         out = torch.empty((q_len, hq, d), dtype=torch.bfloat16, device=q.device)
     if need_lse and lse is None:
         lse = torch.empty((hq, q_len), dtype=torch.float32, device=q.device)
+    ws_ptr, ws_bytes = None, 0
+    if balanced:
+        ws = attention_workspace(q_len, hq, hkv, q.device)
+        ws_ptr, ws_bytes = ctypes.c_void_p(ws.base), ws.nbytes
     N.check(lib.hsd_verify_attention(
         N.ptr(q), q.stride(1), q.stride(0), N.ptr(k), k.stride(1), k.stride(0),
         N.ptr(v), v.stride(1), v.stride(0), N.ptr(out), N.ptr(lse) if need_lse else None,
-        q_len, kv_len, hq, hkv, d, float(scale), C_byref(plan), N.ptr(plan.status),
-        N.stream_handle(stream)), "hsd_verify_attention")
+        q_len, kv_len, hq, hkv, d, float(scale), ctypes.byref(plan.struct), ws_ptr, ws_bytes,
+        N.ptr(plan.status), N.stream_handle(stream)), "hsd_verify_attention")
     return out, lse
-
-
-def C_byref(plan):
-    import ctypes
-    return ctypes.byref(plan.struct)
 
 
 def plan_for(attention_mask, q_len, kv_len):

@@ -29,7 +29,7 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct PlanLayout {
   size_t mask_words, tile_class, kv_num, kv_idx, full_num, full_idx, blk_count, blk_list,
-      tile_order, total;
+      tile_order, blk_prefix, total;
 };
 
 PlanLayout plan_layout(int32_t q_len, int32_t kv_len) {
@@ -50,6 +50,7 @@ PlanLayout plan_layout(int32_t q_len, int32_t kv_len) {
   L.blk_count = take(nq * 4);
   L.blk_list = take(nq * n128 * 4);
   L.tile_order = take(nq * 4);
+  L.blk_prefix = take((nq + 1) * 4);
   L.total = off;
   return L;
 }
@@ -98,6 +99,7 @@ int hsd_plan_init(void* workspace, size_t bytes, int32_t q_len, int32_t kv_len,
   plan->blk_count = reinterpret_cast<int32_t*>(base + L.blk_count);
   plan->blk_list = reinterpret_cast<uint32_t*>(base + L.blk_list);
   plan->tile_order = reinterpret_cast<int32_t*>(base + L.tile_order);
+  plan->blk_prefix = reinterpret_cast<int32_t*>(base + L.blk_prefix);
   return HSD_OK;
 }
 

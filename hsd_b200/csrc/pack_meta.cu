@@ -171,8 +171,10 @@ __global__ void __launch_bounds__(256) classify_kernel(SegSource S, hsd_plan_t P
 }
 
 // Query tiles ranked by descending block count (ties: lower tile first), so
-// the attention grid starts the longest tiles first.
+// the attention grid starts the longest tiles first, and the exclusive prefix
+// of block counts in that order (the work offsets of the stream-K schedule).
 __global__ void order_kernel(hsd_plan_t P) {
+  __shared__ int cnt_sorted[1024];
   const int n = P.n_qtiles;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int ci = P.blk_count[i];
@@ -182,6 +184,16 @@ __global__ void order_kernel(hsd_plan_t P) {
       rank += (cj > ci) || (cj == ci && j < i);
     }
     P.tile_order[rank] = i;
+    if (rank < 1024) cnt_sorted[rank] = ci;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int t = 0; t < n; ++t) {
+      P.blk_prefix[t] = acc;
+      acc += (n <= 1024) ? cnt_sorted[t] : P.blk_count[P.tile_order[t]];
+    }
+    P.blk_prefix[n] = acc;
   }
 }
 

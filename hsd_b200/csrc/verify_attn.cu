@@ -40,20 +40,40 @@ constexpr int TILE_BYTES = BN * HD * 2;  // 32 KB: a 128x128 bf16 tile
 constexpr int SUB_BYTES = 128 * 128;     // one 64-column swizzled sub-tile of 128 rows
 constexpr int kThreads = 384;  // 3 warpgroups: softmax slot 0, slot 1, producer + MMA
 constexpr float kRescaleLog2 = 8.0f;
+// P is packed to bf16 by truncation (pack_bf16x2_trunc).  Truncation lowers a
+// value by 0.28% on average, so every exponent gets +log2(1 + k) with
+// k = 0.00282 and the row sum is divided by (1 + k): the packed weights are
+// then unbiased against the exact sum (mean relative error ~1e-6, RMS
+// 1.75e-3 vs 1.66e-3 for round-to-nearest), and l stays the exact sum of
+// exp2(s * scale - m), so O / l and the LSE need no other correction.
+constexpr float kPackBiasLog2 = 0.0040626743f;   // log2(1.00282)
+constexpr float kPackBiasInv = 0.99718800f;      // 1 / 1.00282
+
+constexpr int kMaxTiles = 1024;  // query tiles per launch (q_len <= 131072)
+// Partial record of one (CTA, piece kind, slot): O as [32 chunks][128 rows]
+// of float4 (a warp reads / writes 512 contiguous bytes per access), then
+// (m, l) per row.
+constexpr int kRecFloats = 128 * 128 + 128 * 2;
 
 struct __align__(1024) Smem {
   uint8_t q[NSLOT][TILE_BYTES];
   uint8_t kv[NSTAGE][TILE_BYTES];
   uint64_t bar_q;
+  uint64_t bar_q_free;
   uint64_t bar_full[NSTAGE];
   uint64_t bar_empty[NSTAGE];
   uint64_t bar_s_full[NSLOT];
   uint64_t bar_p_full[NSLOT];
   uint64_t bar_o_done[NSLOT];
+  uint64_t bar_o_free[NSLOT];
   uint64_t bar_final;
   uint32_t tmem_base;
   int abort;
 };
+
+// 227 KB of opt-in shared memory per CTA, plus up to 1 KB lost aligning the
+// dynamic base to the 1024-byte swizzle atom.
+static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory budget exceeded");
 
 struct Params {
   __nv_bfloat16* out;
@@ -62,11 +82,57 @@ struct Params {
   const int32_t* blk_count;
   const uint64_t* mask_words;
   const int32_t* tile_order;
+  const int32_t* blk_prefix;  // [n_qtiles + 1] blocks before each ordered tile
   int32_t* status;
+  float* partials;     // stream-K partial records [G][2][NSLOT][kRecFloats], or null
   int q_len, kv_len, hq, hkv, group, pairs;
   int n_qtiles, n_kv64, n_kv128;
   float scale_log2;
+  int split;  // 1: stream-K over gridDim.x CTAs; 0: one item per CTA
 };
+
+// A piece: blocks [b0, b1) of one item (query tile x head pair).
+struct Piece {
+  int qt, kvh, h0, nslot, b0, b1, nblk, item, start;
+};
+
+// Next piece of the work range [w, w1) (advances w).  Items are the query
+// tiles in tile_order, each split into hkv x pairs head-pair items of
+// blk_count[tile] blocks; W = sum of all items' blocks.
+__device__ __forceinline__ bool next_piece(const Params& p, int& w, int w1, Piece& pc) {
+  if (w >= w1) return false;
+  const int per_tile = p.hkv * p.pairs;
+  int lo = 0, hi = p.n_qtiles - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.blk_prefix[mid] * per_tile <= w)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  const int qt = p.tile_order[lo];
+  const int c = p.blk_count[qt];
+  const int tile_start = p.blk_prefix[lo] * per_tile;
+  const int off = w - tile_start;
+  const int hp = off / c;
+  pc.qt = qt;
+  pc.nblk = c;
+  pc.b0 = off - hp * c;
+  pc.b1 = min(c, pc.b0 + (w1 - w));
+  pc.item = lo * per_tile + hp;
+  pc.start = tile_start + hp * c;
+  pc.kvh = hp / p.pairs;
+  const int pair = hp - pc.kvh * p.pairs;
+  pc.h0 = pc.kvh * p.group + 2 * pair;
+  pc.nslot = (2 * pair + 1 < p.group) ? 2 : 1;
+  w += pc.b1 - pc.b0;
+  return true;
+}
+
+// First work index of CTA k in stream-K mode.
+__device__ __forceinline__ int range_start(int k, int total, int g) {
+  return int((int64_t(k) * total) / g);
+}
 
 constexpr uint32_t kIdescS = idesc_bf16_f32(BM, BN, false, false);  // Q K^T: both K-major
 constexpr uint32_t kIdescO = idesc_bf16_f32(BM, HD, false, true);   // P V: V is MN-major
@@ -94,6 +160,10 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
                  (acc || kk > 0) ? 1u : 0u);
 }
 
+__device__ __forceinline__ void slot_barrier(int s) {
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + s) : "memory");
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     verify_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
@@ -102,19 +172,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                       ~uintptr_t(1023));
   const int warp = warp_id(), lane = lane_id();
-
-  // ---- work item: heaviest query tiles first
   const int per_tile = p.hkv * p.pairs;
-  const int qt = p.tile_order[blockIdx.x / per_tile];
-  const int hp = blockIdx.x % per_tile;
-  const int kvh = hp / p.pairs, pair = hp % p.pairs;
-  const int h0 = kvh * p.group + 2 * pair;
-  const int nslot = (2 * pair + 1 < p.group) ? 2 : 1;
-  const int nblk = p.blk_count[qt];
-  const uint32_t* list = p.blk_list + size_t(qt) * p.n_kv128;
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.bar_q, 1);
+    mbar_init(&sm.bar_q_free, 1);
     for (int i = 0; i < NSTAGE; ++i) {
       mbar_init(&sm.bar_full[i], 1);
       mbar_init(&sm.bar_empty[i], 1);
@@ -123,6 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.bar_s_full[i], 1);
       mbar_init(&sm.bar_p_full[i], 128);
       mbar_init(&sm.bar_o_done[i], 1);
+      mbar_init(&sm.bar_o_free[i], 128);
     }
     mbar_init(&sm.bar_final, 1);
     sm.abort = 0;
@@ -137,6 +200,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
   volatile int* abort = &sm.abort;
+  const int total = p.blk_prefix[p.n_qtiles] * per_tile;
+  const int G = gridDim.x;
+  int w0, w1;
+  if (p.split) {
+    w0 = range_start(blockIdx.x, total, G);
+    w1 = range_start(blockIdx.x + 1, total, G);
+  } else {
+    // one item per CTA: item blockIdx.x of the ordered item list
+    const int t = blockIdx.x / per_tile, hp = blockIdx.x % per_tile;
+    const int c = t < p.n_qtiles ? p.blk_count[p.tile_order[t]] : 0;
+    w0 = t < p.n_qtiles ? p.blk_prefix[t] * per_tile + hp * c : total;
+    w1 = w0 + c;
+  }
 
   // Register split across warpgroups (launch: 384 x 168 = 64512): the
   // producer/MMA warpgroup keeps 120, each softmax warpgroup gets 192
@@ -144,33 +220,43 @@ __global__ void __launch_bounds__(kThreads, 1)
   // branch of its own setmaxnreg.
   if (warp >= 8) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 120;\n" ::: "memory");
-    if (warp == 8 && lane == 0 && nblk > 0) {
+    if (warp == 8 && lane == 0) {
       // ---------------------------------------------------------- producer
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(&sm.bar_q, nslot * TILE_BYTES);
-      for (int s = 0; s < nslot; ++s)
-        for (int d = 0; d < 2; ++d)
-          tma_load_3d(sm.q[s] + d * SUB_BYTES, &tm_q, &sm.bar_q, d * 64, qt * BM, h0 + s);
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;  // K/V tiles issued; ring slot i was used ceil((issued - i) / NSTAGE) times
+      int pieces = 0;
       bool ok = true;
-      for (int j = 0; j < nblk && ok; ++j) {
-        const int kb = int(list[j] & 0xFFFFFFu);
-        for (int which = 0; which < 2 && ok; ++which) {
-          ok = mbar_wait(&sm.bar_empty[stage], phase ^ 1u, abort, p.status, 0x100 + which);
-          if (!ok) break;
-          mbar_arrive_expect_tx(&sm.bar_full[stage], TILE_BYTES);
-          const CUtensorMap* tm = which ? &tm_v : &tm_k;
+      int w = w0;
+      Piece pc;
+      while (ok && next_piece(p, w, w1, pc)) {
+        if (pieces > 0)  // the previous piece's S MMAs no longer read Q
+          ok = mbar_wait(&sm.bar_q_free, uint32_t(pieces - 1) & 1u, abort, p.status, 0x101);
+        if (!ok) break;
+        mbar_arrive_expect_tx(&sm.bar_q, pc.nslot * TILE_BYTES);
+        for (int s = 0; s < pc.nslot; ++s)
           for (int d = 0; d < 2; ++d)
-            tma_load_3d(sm.kv[stage] + d * SUB_BYTES, tm, &sm.bar_full[stage], d * 64, kb * BN,
-                        kvh);
-          ++issued;
-          if (++stage == NSTAGE) {
-            stage = 0;
-            phase ^= 1u;
+            tma_load_3d(sm.q[s] + d * SUB_BYTES, &tm_q, &sm.bar_q, d * 64, pc.qt * BM, pc.h0 + s);
+        ++pieces;
+        const uint32_t* list = p.blk_list + size_t(pc.qt) * p.n_kv128;
+        for (int j = pc.b0; j < pc.b1 && ok; ++j) {
+          const int kb = int(list[j] & 0xFFFFFFu);
+          for (int which = 0; which < 2 && ok; ++which) {
+            ok = mbar_wait(&sm.bar_empty[stage], phase ^ 1u, abort, p.status, 0x100 + which);
+            if (!ok) break;
+            mbar_arrive_expect_tx(&sm.bar_full[stage], TILE_BYTES);
+            const CUtensorMap* tm = which ? &tm_v : &tm_k;
+            for (int d = 0; d < 2; ++d)
+              tma_load_3d(sm.kv[stage] + d * SUB_BYTES, tm, &sm.bar_full[stage], d * 64,
+                          kb * BN, pc.kvh);
+            ++issued;
+            if (++stage == NSTAGE) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
         }
       }
@@ -182,60 +268,86 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (uses > 0)
           mbar_wait(&sm.bar_full[i], uint32_t(uses - 1) & 1u, abort, p.status, 0x110 + i, false);
       }
-      mbar_wait(&sm.bar_q, 0, abort, p.status, 0x120, false);
-    } else if (warp == 9 && lane == 0 && nblk > 0) {
+      if (pieces > 0)
+        mbar_wait(&sm.bar_q, uint32_t(pieces - 1) & 1u, abort, p.status, 0x120, false);
+    } else if (warp == 9 && lane == 0) {
       // ---------------------------------------------------------- MMA issuer
       const uint32_t qa0 = smem_u32(sm.q[0]);
-      bool ok = mbar_wait(&sm.bar_q, 0, abort, p.status, 0x200);
-      tc_fence_after();
+      const uint32_t kv0 = smem_u32(sm.kv[0]);
       int stage = 0;
       uint32_t phase = 0;
-      const uint32_t kv0 = smem_u32(sm.kv[0]);
-      // prologue: S_s(0)
-      const int k0 = stage;
-      if (ok) ok = mbar_wait(&sm.bar_full[k0], phase, abort, p.status, 0x201);
-      if (ok) {
+      int gs[NSLOT] = {0, 0};  // blocks done per slot (barrier parity)
+      int ps[NSLOT] = {0, 0};  // pieces done per slot
+      int pieces = 0;
+      bool ok = true;
+      bool issued_any = false;
+      int w = w0;
+      Piece pc;
+      while (ok && next_piece(p, w, w1, pc)) {
+        ok = mbar_wait(&sm.bar_q, uint32_t(pieces) & 1u, abort, p.status, 0x200);
+        if (!ok) break;
         tc_fence_after();
-        for (int s = 0; s < nslot; ++s) {
+        // prologue: S_s(b0)
+        const int k0 = stage;
+        ok = mbar_wait(&sm.bar_full[k0], phase, abort, p.status, 0x201);
+        if (!ok) break;
+        tc_fence_after();
+        for (int s = 0; s < pc.nslot; ++s) {
           issue_s(tmem + s * 256, qa0 + s * TILE_BYTES, kv0 + k0 * TILE_BYTES);
           umma_commit(&sm.bar_s_full[s]);
         }
         umma_commit(&sm.bar_empty[k0]);
-      }
-      if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
-      for (int j = 0; j < nblk && ok; ++j) {
-        const int vstage = stage;
-        const uint32_t vphase = phase;
+        issued_any = true;
         if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
-        const bool more = j + 1 < nblk;
-        const int nk = stage;
-        const uint32_t nkph = phase;
-        if (more) if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
-        ok = mbar_wait(&sm.bar_full[vstage], vphase, abort, p.status, 0x202);
-        if (!ok) break;
-        for (int s = 0; s < nslot && ok; ++s) {
-          ok = mbar_wait(&sm.bar_p_full[s], j & 1, abort, p.status, 0x205);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(tmem + s * 256 + 128, tmem + s * 256, kv0 + vstage * TILE_BYTES, j > 0);
-          umma_commit(&sm.bar_o_done[s]);
+        for (int j = pc.b0; j < pc.b1 && ok; ++j) {
+          const int vstage = stage;
+          const uint32_t vphase = phase;
+          if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
+          const bool more = j + 1 < pc.b1;
+          const int nk = stage;
+          const uint32_t nkph = phase;
           if (more) {
-            if (s == 0) {
-              ok = mbar_wait(&sm.bar_full[nk], nkph, abort, p.status, 0x203);
-              if (!ok) break;
-              tc_fence_after();
-            }
-            issue_s(tmem + s * 256, qa0 + s * TILE_BYTES, kv0 + nk * TILE_BYTES);
-            umma_commit(&sm.bar_s_full[s]);
+            if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
           }
+          ok = mbar_wait(&sm.bar_full[vstage], vphase, abort, p.status, 0x202);
+          if (!ok) break;
+          for (int s = 0; s < pc.nslot && ok; ++s) {
+            ok = mbar_wait(&sm.bar_p_full[s], uint32_t(gs[s]) & 1u, abort, p.status, 0x205);
+            if (!ok) break;
+            if (j == pc.b0 && ps[s] > 0) {
+              // the softmax has read O of this slot's previous piece
+              ok = mbar_wait(&sm.bar_o_free[s], uint32_t(ps[s] - 1) & 1u, abort, p.status,
+                             0x207);
+              if (!ok) break;
+            }
+            tc_fence_after();
+            issue_pv(tmem + s * 256 + 128, tmem + s * 256, kv0 + vstage * TILE_BYTES, j > pc.b0);
+            umma_commit(&sm.bar_o_done[s]);
+            ++gs[s];
+            if (more) {
+              if (s == 0) {
+                ok = mbar_wait(&sm.bar_full[nk], nkph, abort, p.status, 0x203);
+                if (!ok) break;
+                tc_fence_after();
+              }
+              issue_s(tmem + s * 256, qa0 + s * TILE_BYTES, kv0 + nk * TILE_BYTES);
+              umma_commit(&sm.bar_s_full[s]);
+            }
+          }
+          if (!ok) break;
+          umma_commit(&sm.bar_empty[vstage]);
+          if (more) umma_commit(&sm.bar_empty[nk]);
         }
         if (!ok) break;
-        umma_commit(&sm.bar_empty[vstage]);
-        if (more) umma_commit(&sm.bar_empty[nk]);
+        umma_commit(&sm.bar_q_free);  // every S of this piece has been issued
+        for (int s = 0; s < pc.nslot; ++s) ++ps[s];
+        ++pieces;
       }
       // every MMA this thread issued has completed once bar_final fires
-      umma_commit(&sm.bar_final);
-      mbar_wait(&sm.bar_final, 0, abort, p.status, 0x206, false);
+      if (issued_any) {
+        umma_commit(&sm.bar_final);
+        mbar_wait(&sm.bar_final, 0, abort, p.status, 0x206, false);
+      }
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 192;\n" ::: "memory");
@@ -243,15 +355,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int s = warp >> 2;       // head slot
     const int quarter = warp & 3;  // TMEM lane quarter
     const int r = quarter * 32 + lane;
-    const int q = qt * BM + r;
-    const int h = h0 + s;
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
     const uint32_t t_s = tmem + lane_off + s * 256;
     const uint32_t t_o = t_s + 128;
-    float m = -INFINITY, l = 0.f;
+    int gs = 0;  // blocks this slot has processed (barrier parity)
     bool ok = true;
-    if (s < nslot) {
-      for (int j = 0; j < nblk && ok; ++j) {
+    int w = w0;
+    Piece pc;
+    while (ok && next_piece(p, w, w1, pc)) {
+      if (s >= pc.nslot) continue;
+      const int qt = pc.qt;
+      const int q = qt * BM + r;
+      const int h = pc.h0 + s;
+      const uint32_t* list = p.blk_list + size_t(qt) * p.n_kv128;
+      float m = -INFINITY, l = 0.f;
+      for (int j = pc.b0; j < pc.b1 && ok; ++j) {
         const uint32_t e = list[j];
         const int kb = int(e & 0xFFFFFFu);
         // mask words: absent half = 0, full half = ~0, partial half = its row word
@@ -260,13 +378,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int hf = 0; hf < 2; ++hf) {
           const bool present = (e >> (24 + 2 * hf)) & 1u;
           const bool partial = (e >> (25 + 2 * hf)) & 1u;
-          uint64_t w = present ? ~0ull : 0ull;
-          if (partial) w = p.mask_words[(size_t(qt) * p.n_kv64 + 2 * kb + hf) * 128 + r];
-          mw[2 * hf] = uint32_t(w);
-          mw[2 * hf + 1] = uint32_t(w >> 32);
+          uint64_t wd = present ? ~0ull : 0ull;
+          if (partial) wd = p.mask_words[(size_t(qt) * p.n_kv64 + 2 * kb + hf) * 128 + r];
+          mw[2 * hf] = uint32_t(wd);
+          mw[2 * hf + 1] = uint32_t(wd >> 32);
         }
-        ok = __all_sync(0xffffffffu, mbar_wait(&sm.bar_s_full[s], j & 1, abort, p.status,
-                                               0x300 + s));
+        ok = __all_sync(0xffffffffu, mbar_wait(&sm.bar_s_full[s], uint32_t(gs) & 1u, abort,
+                                               p.status, 0x300 + s));
         if (!ok) break;
         tc_fence_after();
         // S row -> registers: four loads in flight, one wait
@@ -292,77 +410,132 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < 8; ++k) mx8[k] = x[k];
 #pragma unroll
-        for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], x[i]);
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        for (int i = 8; i < 128; i += 16)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) mx8[k] = fmax3(mx8[k], x[i + k], x[i + 8 + k]);
+        const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                               fmaxf(mx8[6], mx8[7]));
         const float m_new = fmaxf(m, mx * p.scale_log2);
         const bool need = m_new > m + kRescaleLog2;  // also true for m = -inf, m_new finite
         const float alpha = need ? ex2_approx(m - m_new) : 1.f;
         if (need) m = m_new;
-        const float nm = (m == -INFINITY) ? 0.f : -m;
-        // O holds sum_{i<j} P_i V_i (PV(j-1) completed before S(j)); rescale it
-        // when this block raised the max.
-        if (j > 0 && __any_sync(0xffffffffu, need)) {
+        const float nm = ((m == -INFINITY) ? 0.f : -m) + kPackBiasLog2;
+        // O holds sum_{i<j} P_i V_i of this piece (PV(j-1) completed before
+        // S(j)); rescale it when this block raised the max.
+        if (j > pc.b0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             uint32_t o[16];
             tmem_ld16(t_o + c * 16, o);
             tmem_wait_ld16(o);
+            const uint64_t al2 = f2_pack(alpha, alpha);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            for (int i = 0; i < 8; ++i) {
+              float lo, hi;
+              f2_unpack(f2_mul(f2_pack(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])),
+                               al2),
+                        lo, hi);
+              o[2 * i] = __float_as_uint(lo);
+              o[2 * i + 1] = __float_as_uint(hi);
+            }
             tmem_st16(t_o + c * 16, o);
           }
         }
         // P = exp2(s * scale - m) -> bf16 pairs -> TMEM columns [0, 64) of S
-        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+        // (scale, subtract) and the row sums run on packed fp32 pairs
+        const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
+        const uint64_t nm2 = f2_pack(nm, nm);
+        uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t pk[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const float a = ex2_approx(fmaf(x[64 * c + 2 * i], p.scale_log2, nm));
-            const float b = ex2_approx(fmaf(x[64 * c + 2 * i + 1], p.scale_log2, nm));
-            sum4[i & 3] += a + b;
-            pk[i] = pack_bf16x2(a, b);
+            float xa, xb;
+            f2_unpack(f2_fma(f2_pack(x[64 * c + 2 * i], x[64 * c + 2 * i + 1]), sc2, nm2), xa, xb);
+            const float a = ex2_approx(xa);
+            const float b = ex2_approx(xb);
+            sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(a, b));
+            pk[i] = pack_bf16x2_trunc(a, b);
           }
           tmem_st32(t_s + c * 32, pk);
         }
-        l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+        float s0, s1, s2, s3, s4, s5, s6, s7;
+        f2_unpack(sum2[0], s0, s1);
+        f2_unpack(sum2[1], s2, s3);
+        f2_unpack(sum2[2], s4, s5);
+        f2_unpack(sum2[3], s6, s7);
+        l = l * alpha + (((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7))) * kPackBiasInv;
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&sm.bar_p_full[s]);
+        ++gs;
       }
-      // ---- epilogue
-      if (ok && nblk > 0)
-        ok = __all_sync(0xffffffffu, mbar_wait(&sm.bar_o_done[s], (nblk - 1) & 1, abort, p.status,
-                                               0x320 + s));
+      if (!ok) break;
+      // ---- epilogue of the piece: O -> registers, then release O
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.bar_o_done[s], uint32_t(gs - 1) & 1u, abort,
+                                             p.status, 0x320 + s));
+      if (!ok) break;
       tc_fence_after();
+      float o[128];
+      {
+        uint32_t u[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_o + c * 32, u[c]);
+        tmem_wait_ld(u[0]);
+        tmem_wait_ld(u[1]);
+        tmem_wait_ld(u[2]);
+        tmem_wait_ld(u[3]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[c * 32 + i] = __uint_as_float(u[c][i]);
+      }
+      tc_fence_before();
+      mbar_arrive(&sm.bar_o_free[s]);
+      const bool whole = pc.b0 == 0 && pc.b1 == pc.nblk;
+      if (!whole) {
+        // stream-K partial: unnormalised O with its (m, l); combine_kernel
+        // merges the pieces of every split item after this launch.
+        const int kind = (pc.start < w0) ? 0 : 1;
+        float* rec = p.partials + ((size_t(blockIdx.x) * 2 + kind) * NSLOT + s) * kRecFloats;
+        float4* rec4 = reinterpret_cast<float4*>(rec);
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          rec4[c * 128 + r] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+        reinterpret_cast<float2*>(rec + 128 * 128)[r] = make_float2(m, l);
+        continue;
+      }
+      // ---- final output of the item
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = p.out + (size_t(q) * p.hq + h) * HD;
+      if (q < p.q_len) {
+        int4* dst = reinterpret_cast<int4*>(p.out + (size_t(q) * p.hq + h) * HD);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t u[32];
-        if (nblk > 0 && ok) {
-          tmem_ld32(t_o + c * 32, u);
-          tmem_wait_ld(u);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) u[i] = 0u;
-        }
-        uint32_t o[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          o[i] = pack_bf16x2(__uint_as_float(u[2 * i]) * inv, __uint_as_float(u[2 * i + 1]) * inv);
-        if (q < p.q_len) {
-          int4* dst = reinterpret_cast<int4*>(orow + c * 32);
-#pragma unroll
-          for (int v = 0; v < 4; ++v)
-            dst[v] = make_int4(int(o[4 * v]), int(o[4 * v + 1]), int(o[4 * v + 2]), int(o[4 * v + 3]));
+        for (int v = 0; v < 16; ++v)
+          dst[v] = make_int4(int(pack_bf16x2(o[8 * v] * inv, o[8 * v + 1] * inv)),
+                             int(pack_bf16x2(o[8 * v + 2] * inv, o[8 * v + 3] * inv)),
+                             int(pack_bf16x2(o[8 * v + 4] * inv, o[8 * v + 5] * inv)),
+                             int(pack_bf16x2(o[8 * v + 6] * inv, o[8 * v + 7] * inv)));
+        if (p.lse)
+          p.lse[size_t(h) * p.q_len + q] =
+              (l > 0.f) ? (m + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
+      }
+    }
+    // query tiles without any visible block: all their rows are fully masked
+    if (ok) {
+      const int tid = threadIdx.x;  // 0..255
+      for (int t = blockIdx.x; t < p.n_qtiles; t += G) {
+        const int qt = p.tile_order[t];
+        if (p.blk_count[qt] != 0) continue;
+        for (int idx = tid; idx < 128 * p.hq; idx += 256) {
+          const int rr = idx / p.hq, hh = idx % p.hq;
+          const int qq = qt * BM + rr;
+          if (qq >= p.q_len) continue;
+          int4* dst = reinterpret_cast<int4*>(p.out + (size_t(qq) * p.hq + hh) * HD);
+          for (int v = 0; v < 16; ++v) dst[v] = make_int4(0, 0, 0, 0);
+          if (p.lse) p.lse[size_t(hh) * p.q_len + qq] = -INFINITY;
         }
       }
-      if (p.lse && q < p.q_len)
-        p.lse[size_t(h) * p.q_len + q] =
-            (l > 0.f) ? (m + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
     }
   }
   tc_fence_before();
@@ -371,6 +544,109 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+// Merge the pieces of every item the stream-K split cut: O = sum_k 2^(m_k-M)
+// O_k / sum_k 2^(m_k-M) l_k per row.  Block (boundary b, slot s): boundary b
+// owns item X when the start of CTA b's range lies strictly inside X and the
+// start of CTA b-1's range does not (the first boundary inside X).  Thread 0
+// resolves ownership and the list of pieces; then thread = (row, 32-column
+// chunk) and the pieces' loads are coalesced across rows.
+constexpr int kMaxCombinePieces = 64;
+
+__global__ void __launch_bounds__(512) combine_kernel(const Params p, int G) {
+  __shared__ int s_np, s_q0, s_h;
+  __shared__ const float* s_rec[kMaxCombinePieces];
+  const int b = 1 + blockIdx.x / NSLOT;
+  const int s = blockIdx.x % NSLOT;
+  if (threadIdx.x == 0) {
+    s_np = 0;
+    const int per_tile = p.hkv * p.pairs;
+    const int total = p.blk_prefix[p.n_qtiles] * per_tile;
+    const int pos = range_start(b, total, G);
+    if (pos > 0 && pos < total) {
+      int lo = 0, hi = p.n_qtiles - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.blk_prefix[mid] * per_tile <= pos)
+          lo = mid;
+        else
+          hi = mid - 1;
+      }
+      const int qt = p.tile_order[lo];
+      const int c = p.blk_count[qt];
+      const int tile_start = p.blk_prefix[lo] * per_tile;
+      const int hp = (pos - tile_start) / c;
+      const int ia = tile_start + hp * c, ib = ia + c - 1;
+      const int pair = hp % p.pairs, kvh = hp / p.pairs;
+      if (pos != ia && range_start(b - 1, total, G) <= ia && 2 * pair + s < p.group) {
+        int np = 0;
+        int rs = range_start(b - 1, total, G);
+        for (int k = b - 1; k < G && rs <= ib; ++k) {
+          const int next = range_start(k + 1, total, G);
+          if (next > rs) {  // non-empty range: one piece
+            if (np >= kMaxCombinePieces) {
+              report(p.status, HSD_DEV_CAPACITY | 0x331);
+              break;
+            }
+            const int kind = (ia < rs) ? 0 : 1;
+            s_rec[np++] = p.partials + ((size_t(k) * 2 + kind) * NSLOT + s) * kRecFloats;
+          }
+          rs = next;
+        }
+        s_np = np;
+        s_q0 = qt * BM;
+        s_h = kvh * p.group + 2 * pair + s;
+      }
+    }
+  }
+  __syncthreads();
+  const int np = s_np;
+  if (np == 0) return;
+  const int r = threadIdx.x & 127, ch = threadIdx.x >> 7;  // row, 32-column chunk
+  float M = -INFINITY, L = 0.f;
+  for (int i = 0; i < np; ++i) {
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(s_rec[i] + 128 * 128) + r);
+    if (ml.x > M) {
+      L = (M == -INFINITY ? 0.f : L * ex2_approx(M - ml.x)) + ml.y;
+      M = ml.x;
+    } else if (ml.x != -INFINITY) {
+      L += ml.y * ex2_approx(ml.x - M);
+    }
+  }
+  float acc[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+  for (int i = 0; i < np; ++i) {
+    const float* rk = s_rec[i];
+    const float mk = __ldcg(reinterpret_cast<const float2*>(rk + 128 * 128) + r).x;
+    const float wk = (M == -INFINITY || mk == -INFINITY) ? 0.f : ex2_approx(mk - M);
+    const float4* r4 = reinterpret_cast<const float4*>(rk);
+    float4 v[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) v[c] = __ldcg(r4 + (ch * 8 + c) * 128 + r);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      acc[4 * c] += wk * v[c].x;
+      acc[4 * c + 1] += wk * v[c].y;
+      acc[4 * c + 2] += wk * v[c].z;
+      acc[4 * c + 3] += wk * v[c].w;
+    }
+  }
+  const int q = s_q0 + r;
+  const int h = s_h;
+  if (q >= p.q_len) return;
+  const float inv = (L > 0.f) ? 1.f / L : 0.f;
+  int4* dst = reinterpret_cast<int4*>(p.out + (size_t(q) * p.hq + h) * HD + ch * 32);
+#pragma unroll
+  for (int v = 0; v < 4; ++v)
+    dst[v] = make_int4(int(pack_bf16x2(acc[8 * v] * inv, acc[8 * v + 1] * inv)),
+                       int(pack_bf16x2(acc[8 * v + 2] * inv, acc[8 * v + 3] * inv)),
+                       int(pack_bf16x2(acc[8 * v + 4] * inv, acc[8 * v + 5] * inv)),
+                       int(pack_bf16x2(acc[8 * v + 6] * inv, acc[8 * v + 7] * inv)));
+  if (ch == 0 && p.lse)
+    p.lse[size_t(h) * p.q_len + q] =
+        (L > 0.f) ? (M + __log2f(L)) * 0.69314718055994530942f : -INFINITY;
 }
 
 }  // namespace attn
@@ -427,12 +703,48 @@ bool strides_ok(const void* p, int64_t rs, int64_t hs) {
 
 }  // namespace
 
+namespace {
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return 148;
+  return n;
+}
+
+struct WsLayout {
+  size_t partials, total;
+  int items, grid;
+};
+
+WsLayout ws_layout(int32_t q_len, int32_t hq, int32_t hkv) {
+  WsLayout L{};
+  const int n_qtiles = (q_len + attn::BM - 1) / attn::BM;
+  const int group = hq / hkv, pairs = (group + 1) / 2;
+  L.items = n_qtiles * hkv * pairs;
+  L.grid = sm_count();
+  L.partials = 0;
+  L.total = size_t(L.grid) * 2 * attn::NSLOT * attn::kRecFloats * sizeof(float);
+  return L;
+}
+
+}  // namespace
+
+extern "C" size_t hsd_attention_workspace_bytes(int32_t q_len, int32_t num_q_heads,
+                                                int32_t num_kv_heads) {
+  if (q_len <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads)
+    return 0;
+  return ws_layout(q_len, num_q_heads, num_kv_heads).total;
+}
+
 extern "C" int hsd_verify_attention(const void* q, int64_t q_row_stride, int64_t q_head_stride,
                                     const void* k, int64_t k_row_stride, int64_t k_head_stride,
                                     const void* v, int64_t v_row_stride, int64_t v_head_stride,
                                     void* out, float* lse, int32_t q_len, int32_t kv_len,
                                     int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-                                    float scale, const hsd_plan_t* plan, int32_t* status,
+                                    float scale, const hsd_plan_t* plan, void* workspace,
+                                    size_t workspace_bytes, int32_t* status,
                                     hsd_stream_t stream) {
   if (head_dim != attn::HD) {
     hsd_host::set_error("hsd_verify_attention: head_dim %d unsupported (128 only)", head_dim);
@@ -449,6 +761,18 @@ extern "C" int hsd_verify_attention(const void* q, int64_t q_row_stride, int64_t
         plan ? plan->kv_len : -1);
     return HSD_ERR_INVALID_ARG;
   }
+  if (plan->n_qtiles > attn::kMaxTiles) {
+    hsd_host::set_error("hsd_verify_attention: q_len %d exceeds %d query tiles", q_len,
+                        attn::kMaxTiles);
+    return HSD_ERR_TOO_LARGE;
+  }
+  const WsLayout W = ws_layout(q_len, num_q_heads, num_kv_heads);
+  const bool split = workspace != nullptr;
+  if (split && ((reinterpret_cast<uintptr_t>(workspace) & 255) || workspace_bytes < W.total)) {
+    hsd_host::set_error("hsd_verify_attention: workspace %zu bytes (need %zu, 256-byte aligned)",
+                        workspace_bytes, W.total);
+    return HSD_ERR_INVALID_ARG;
+  }
   CUtensorMap tq, tk, tv;
   int rc = make_map(&tq, q, q_len, num_q_heads, q_row_stride, q_head_stride, "q");
   if (!rc) rc = make_map(&tk, k, kv_len, num_kv_heads, k_row_stride, k_head_stride, "k");
@@ -461,6 +785,7 @@ extern "C" int hsd_verify_attention(const void* q, int64_t q_row_stride, int64_t
   p.blk_count = plan->blk_count;
   p.mask_words = plan->mask_words;
   p.tile_order = plan->tile_order;
+  p.blk_prefix = plan->blk_prefix;
   p.status = status;
   p.q_len = q_len;
   p.kv_len = kv_len;
@@ -472,6 +797,9 @@ extern "C" int hsd_verify_attention(const void* q, int64_t q_row_stride, int64_t
   p.n_kv64 = plan->n_kv64;
   p.n_kv128 = plan->n_kv128;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.split = split ? 1 : 0;
+  p.partials = split ? reinterpret_cast<float*>(static_cast<char*>(workspace) + W.partials)
+                     : nullptr;
   const size_t smem = sizeof(attn::Smem) + 1024;
   static bool attr_set = false;
   if (!attr_set) {
@@ -482,8 +810,13 @@ extern "C" int hsd_verify_attention(const void* q, int64_t q_row_stride, int64_t
     if (rc) return rc;
     attr_set = true;
   }
-  const int grid = plan->n_qtiles * num_kv_heads * p.pairs;
-  attn::verify_attn_kernel<<<grid, attn::kThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
-      tq, tk, tv, p);
-  return hsd_host::cuda_check(cudaGetLastError(), "verify_attn_kernel launch");
+  // stream-K: one CTA per SM sharing the total work evenly; otherwise one CTA
+  // per (query tile, head pair) item.
+  const int grid = split ? W.grid : W.items;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  attn::verify_attn_kernel<<<grid, attn::kThreads, smem, st>>>(tq, tk, tv, p);
+  rc = hsd_host::cuda_check(cudaGetLastError(), "verify_attn_kernel launch");
+  if (rc || !split || W.grid < 2) return rc;
+  attn::combine_kernel<<<(W.grid - 1) * attn::NSLOT, 512, 0, st>>>(p, W.grid);
+  return hsd_host::cuda_check(cudaGetLastError(), "combine_kernel launch");
 }

@@ -57,6 +57,8 @@ class VerifyStep:
         from .workloads import segment_dicts
         self.mask = PackedMask(self.q_len, self.kv_len, segment_dicts(page), device=dev)
         self.plan = TilePlan(self.q_len, self.kv_len, dev)
+        from .attention import attention_workspace
+        self.ws = attention_workspace(self.q_len, hq, hkv, dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
 
         # acceptance inputs
@@ -143,7 +145,8 @@ class VerifyStep:
             N.check(lib.hsd_verify_attention(
                 p(q), q.stride(1), q.stride(0), p(k), k.stride(1), k.stride(0), p(v), v.stride(1),
                 v.stride(0), p(self.out[l]), p(self.lse[l]), ql, kvl, hq, hkv, d, scale,
-                C.byref(self.plan.struct), p(self.status), st), "hsd_verify_attention")
+                C.byref(self.plan.struct), C.c_void_p(self.ws.base), self.ws.nbytes,
+                p(self.status), st), "hsd_verify_attention")
             if attn_events is not None:
                 attn_events[l][1].record(stream)
         # 4. acceptance + KMP

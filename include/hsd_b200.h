@@ -83,6 +83,7 @@ typedef struct {
   int32_t *blk_count;        /* [n_qtiles] 128-column blocks visited */
   uint32_t *blk_list;        /* [n_qtiles][n_kv128] block | flags << 24 */
   int32_t *tile_order;       /* [n_qtiles] query tiles, most blocks first */
+  int32_t *blk_prefix;       /* [n_qtiles + 1] exclusive prefix of blk_count in tile_order */
 } hsd_plan_t;
 
 /* Per-block state and inputs of the acceptance / re-alignment kernel.  Mirrors
@@ -161,20 +162,30 @@ int hsd_build_plan_dense(const float *mask, int64_t row_stride, hsd_plan_t *plan
 
 /* ---- (1) packed verification attention ---------------------------------- */
 
+/* Device workspace of the load-balanced (stream-K) attention schedule: fp32
+ * partial rows for the two pieces an SM's share of the work can leave
+ * unfinished, for every SM of the current device.  Needs no initialisation;
+ * its contents are scratch between the two kernels of one call. */
+size_t hsd_attention_workspace_bytes(int32_t q_len, int32_t num_q_heads, int32_t num_kv_heads);
+
 /* out = softmax(q k^T * scale + mask) v per query head with grouped KV heads,
  * lse = natural log-sum-exp; replaces flex_attention_forward (D:72-135,
  * H:103-180) including repeat_kv (D:137-146).  q: bf16 [num_q_heads][q_len]
  * [128] at the given element strides (row, head); k, v likewise with
  * num_kv_heads; out: bf16 [q_len][num_q_heads][128] contiguous (the
  * reference's transposed output, D:134); lse: fp32 [num_q_heads][q_len] or
- * NULL.  Fully masked rows give 0 and -inf.  head_dim must be 128. */
+ * NULL.  Fully masked rows give 0 and -inf.  head_dim must be 128.
+ * workspace (256-byte aligned, hsd_attention_workspace_bytes) enables the
+ * stream-K schedule -- one CTA per SM, equal shares of the tile plan's work;
+ * a second kernel merges the (query tile, head pair) items the shares cut,
+ * through the workspace.  With workspace NULL each item gets its own CTA. */
 int hsd_verify_attention(const void *q, int64_t q_row_stride, int64_t q_head_stride,
                          const void *k, int64_t k_row_stride, int64_t k_head_stride,
                          const void *v, int64_t v_row_stride, int64_t v_head_stride,
                          void *out, float *lse, int32_t q_len, int32_t kv_len,
                          int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-                         float scale, const hsd_plan_t *plan, int32_t *status,
-                         hsd_stream_t stream);
+                         float scale, const hsd_plan_t *plan, void *workspace,
+                         size_t workspace_bytes, int32_t *status, hsd_stream_t stream);
 
 /* ---- (2) KV-cache compaction -------------------------------------------- */
 

@@ -41,7 +41,7 @@ def test_struct_sizes_match_header():
     assert C.sizeof(N.Block) == 64
     assert C.sizeof(N.BlockResult) == 32
     assert C.sizeof(N.AcceptConfig) == 4 * 17
-    assert C.sizeof(N.Plan) == 24 + 9 * 8
+    assert C.sizeof(N.Plan) == 24 + 10 * 8
 
 
 def test_plan_layout_host_only():
@@ -57,7 +57,7 @@ def test_plan_layout_host_only():
     assert (plan.n_qtiles, plan.n_kv64, plan.n_kv128) == (12, 24, 12)
     ptrs = [plan.mask_words, plan.tile_class, plan.kv_num_blocks, plan.kv_indices,
             plan.full_kv_num_blocks, plan.full_kv_indices, plan.blk_count, plan.blk_list,
-            plan.tile_order]
+            plan.tile_order, plan.blk_prefix]
     assert all(p % 256 == 0 for p in ptrs)
     assert ptrs == sorted(ptrs) and ptrs[-1] < base + n
     # too small / misaligned workspaces are rejected
@@ -71,9 +71,18 @@ def test_attention_rejects_bad_head_dim_on_host():
     plan = N.Plan()
     plan.q_len, plan.kv_len = 128, 128
     rc = lib.hsd_verify_attention(None, 64, 64, None, 64, 64, None, 64, 64, None, None,
-                                  128, 128, 2, 1, 64, 0.1, C.byref(plan), None, None)
+                                  128, 128, 2, 1, 64, 0.1, C.byref(plan), None, 0, None, None)
     assert rc == N.HSD_OK + 2  # HSD_ERR_UNSUPPORTED
     assert b"head_dim" in lib.hsd_last_error()
+
+
+def test_attention_workspace_size_host_only():
+    lib = N.load()
+    assert lib.hsd_attention_workspace_bytes(0, 12, 2) == 0
+    assert lib.hsd_attention_workspace_bytes(128, 12, 5) == 0
+    n = lib.hsd_attention_workspace_bytes(2176, 12, 2)
+    # partial rows for every SM (148 on B200 when no GPU is visible)
+    assert n >= 148 * 2 * 2 * (128 * 128 + 256) * 4
 
 
 def test_other_entry_points_reject_null_arguments():

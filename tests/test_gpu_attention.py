@@ -38,11 +38,11 @@ def _bf16(x, dev):
     return x.to(torch.bfloat16).to(dev)
 
 
-def run_attention(q, k, v, mask_obj, scale, dev):
+def run_attention(q, k, v, mask_obj, scale, dev, balanced=True):
     from hsd_b200.attention import plan_for, verify_attention
     qd, kd, vd = _bf16(q, dev), _bf16(k, dev), _bf16(v, dev)
     plan = plan_for(mask_obj, q.shape[1], k.shape[1])
-    out, lse = verify_attention(qd, kd, vd, plan, scale=scale)
+    out, lse = verify_attention(qd, kd, vd, plan, scale=scale, balanced=balanced)
     torch.cuda.synchronize()
     plan.raise_on_device_error()
     return out.float().cpu(), lse.cpu(), plan
@@ -193,3 +193,44 @@ def test_attention_large_scores_rescale(dev):
     v = torch.randn(1, 1024, 128)
     out, lse, _ = run_attention(q, k, v, C._dense(allowed).to(dev), 0.3, dev)
     check_close(out, lse, q, k, v, allowed, 0.3)
+
+
+@pytest.mark.parametrize("balanced", [True, False])
+@pytest.mark.parametrize("name", ["cfg1", "step_gqa4", "masked_rows_mqa"])
+def test_attention_both_schedules(dev, name, balanced):
+    """Stream-K (split items combined through the workspace) and one-CTA-per-item."""
+    q, k, v, mask, scale, _ = dict(C.attention_cases())[name]
+    allowed = OB.allowed_from_dense(mask)
+    out, lse, _ = run_attention(q, k, v, mask.to(dev), scale, dev, balanced=balanced)
+    check_close(out, lse, q, k, v, allowed, scale)
+
+
+@pytest.mark.parametrize("qn,kvn", [(128, 256), (64, 70), (300, 5000)])
+def test_attention_small_and_skewed(dev, qn, kvn):
+    """Less work than SMs; one query tile much heavier than the others."""
+    rng = np.random.default_rng(qn + kvn)
+    allowed = rng.random((qn, kvn)) < 0.3
+    allowed[: qn // 3] = False          # a fully masked band of rows
+    if qn >= 256:
+        allowed[:128] = False           # a whole query tile with nothing visible
+        allowed[200:, :] = True         # and a dense one
+    q, k, v = C.qkv(6, 2, qn, kvn, seed=qn)
+    for balanced in (True, False):
+        out, lse, _ = run_attention(q, k, v, C._dense(allowed).to(dev), None, dev, balanced)
+        check_close(out, lse, q, k, v, allowed, None)
+
+
+def test_attention_repeated_launches_reuse_workspace(dev):
+    """Counters are left at zero: many launches in a row stay correct."""
+    from hsd_b200.attention import plan_for, verify_attention
+    allowed = C.cfg1_mask()
+    q, k, v = C.qkv(12, 2, 1512, 1512, seed=21)
+    qd, kd, vd = _bf16(q, dev), _bf16(k, dev), _bf16(v, dev)
+    plan = plan_for(C._dense(allowed).to(dev), 1512, 1512)
+    outs = [verify_attention(qd, kd, vd, plan)[0] for _ in range(6)]
+    torch.cuda.synchronize()
+    ref, _ = verify_attention(qd, kd, vd, plan, balanced=False)
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    err = (outs[0].float() - ref.float()).abs()
+    assert err.max().item() <= 1e-2
