@@ -50,10 +50,11 @@ constexpr float kPackBiasLog2 = 0.0040626743f;   // log2(1.00282)
 constexpr float kPackBiasInv = 0.99718800f;      // 1 / 1.00282
 
 constexpr int kMaxTiles = 1024;  // query tiles per launch (q_len <= 131072)
-// Partial record of one (CTA, piece kind, slot): O as [32 chunks][128 rows]
-// of float4 (a warp reads / writes 512 contiguous bytes per access), then
-// (m, l) per row.
-constexpr int kRecFloats = 128 * 128 + 128 * 2;
+// Partial record of one (CTA, piece kind, slot): the piece's normalised
+// O / l in bf16 as [16 chunks][128 rows] of 16-byte vectors (a warp reads or
+// writes 512 contiguous bytes per access), then (m, l) per row in fp32.
+// Units of 4 bytes.
+constexpr int kRecWords = 128 * 64 + 128 * 2;
 
 struct __align__(1024) Smem {
   uint8_t q[NSLOT][TILE_BYTES];
@@ -84,7 +85,8 @@ struct Params {
   const int32_t* tile_order;
   const int32_t* blk_prefix;  // [n_qtiles + 1] blocks before each ordered tile
   int32_t* status;
-  float* partials;     // stream-K partial records [G][2][NSLOT][kRecFloats], or null
+  uint32_t* partials;  // stream-K partial records [G][2][NSLOT][kRecWords], or null
+  int32_t* combine_desc;  // [G][4] per range boundary: owner item (see combine_kernel)
   int q_len, kv_len, hq, hkv, group, pairs;
   int n_qtiles, n_kv64, n_kv128;
   float scale_log2;
@@ -220,6 +222,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   // branch of its own setmaxnreg.
   if (warp >= 8) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 120;\n" ::: "memory");
+    if (warp == 10 && lane == 0 && p.split) {
+      // Combine descriptor of the boundary at the start of this CTA's range:
+      // {owner, first query row, first head of the pair, last CTA holding a
+      // piece}.  Boundary b owns item X when b's start lies strictly inside X
+      // and b-1's start does not; X's pieces are then CTA b-1's last piece and
+      // the first pieces of the non-empty ranges b..khi.
+      int32_t* d = p.combine_desc + 4 * blockIdx.x;
+      int owner = 0, q0 = 0, hfirst = 0, khi = 0;
+      if (blockIdx.x > 0 && w0 < total) {
+        int w = w0;
+        Piece pc;
+        next_piece(p, w, total, pc);
+        const int ib = pc.start + pc.nblk - 1;
+        if (pc.start < w0 && range_start(blockIdx.x - 1, total, G) <= pc.start) {
+          owner = 1;
+          q0 = pc.qt * BM;
+          hfirst = pc.h0;
+          khi = blockIdx.x;
+          while (khi + 1 < G && range_start(khi + 1, total, G) <= ib) ++khi;
+          owner = pc.nslot;  // number of slots to combine (1 or 2)
+        }
+      }
+      d[0] = owner;
+      d[1] = q0;
+      d[2] = hfirst;
+      d[3] = khi;
+    }
     if (warp == 8 && lane == 0) {
       // ---------------------------------------------------------- producer
       tma_prefetch_desc(&tm_q);
@@ -495,15 +524,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&sm.bar_o_free[s]);
       const bool whole = pc.b0 == 0 && pc.b1 == pc.nblk;
       if (!whole) {
-        // stream-K partial: unnormalised O with its (m, l); combine_kernel
+        // stream-K partial: O / l in bf16 with its (m, l); combine_kernel
         // merges the pieces of every split item after this launch.
         const int kind = (pc.start < w0) ? 0 : 1;
-        float* rec = p.partials + ((size_t(blockIdx.x) * 2 + kind) * NSLOT + s) * kRecFloats;
-        float4* rec4 = reinterpret_cast<float4*>(rec);
+        uint32_t* rec = p.partials + ((size_t(blockIdx.x) * 2 + kind) * NSLOT + s) * kRecWords;
+        const float invl = (l > 0.f) ? 1.f / l : 0.f;
+        int4* rec4 = reinterpret_cast<int4*>(rec);
 #pragma unroll
-        for (int c = 0; c < 32; ++c)
-          rec4[c * 128 + r] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-        reinterpret_cast<float2*>(rec + 128 * 128)[r] = make_float2(m, l);
+        for (int c = 0; c < 16; ++c)
+          rec4[c * 128 + r] = make_int4(int(pack_bf16x2(o[8 * c] * invl, o[8 * c + 1] * invl)),
+                                        int(pack_bf16x2(o[8 * c + 2] * invl, o[8 * c + 3] * invl)),
+                                        int(pack_bf16x2(o[8 * c + 4] * invl, o[8 * c + 5] * invl)),
+                                        int(pack_bf16x2(o[8 * c + 6] * invl, o[8 * c + 7] * invl)));
+        reinterpret_cast<float2*>(rec + 128 * 64)[r] = make_float2(m, l);
         continue;
       }
       // ---- final output of the item
@@ -540,6 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -556,48 +590,30 @@ constexpr int kMaxCombinePieces = 64;
 
 __global__ void __launch_bounds__(512) combine_kernel(const Params p, int G) {
   __shared__ int s_np, s_q0, s_h;
-  __shared__ const float* s_rec[kMaxCombinePieces];
+  __shared__ const uint32_t* s_rec[kMaxCombinePieces];
   const int b = 1 + blockIdx.x / NSLOT;
   const int s = blockIdx.x % NSLOT;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // descriptors and partials
   if (threadIdx.x == 0) {
     s_np = 0;
-    const int per_tile = p.hkv * p.pairs;
-    const int total = p.blk_prefix[p.n_qtiles] * per_tile;
-    const int pos = range_start(b, total, G);
-    if (pos > 0 && pos < total) {
-      int lo = 0, hi = p.n_qtiles - 1;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (p.blk_prefix[mid] * per_tile <= pos)
-          lo = mid;
-        else
-          hi = mid - 1;
-      }
-      const int qt = p.tile_order[lo];
-      const int c = p.blk_count[qt];
-      const int tile_start = p.blk_prefix[lo] * per_tile;
-      const int hp = (pos - tile_start) / c;
-      const int ia = tile_start + hp * c, ib = ia + c - 1;
-      const int pair = hp % p.pairs, kvh = hp / p.pairs;
-      if (pos != ia && range_start(b - 1, total, G) <= ia && 2 * pair + s < p.group) {
-        int np = 0;
-        int rs = range_start(b - 1, total, G);
-        for (int k = b - 1; k < G && rs <= ib; ++k) {
-          const int next = range_start(k + 1, total, G);
-          if (next > rs) {  // non-empty range: one piece
-            if (np >= kMaxCombinePieces) {
-              report(p.status, HSD_DEV_CAPACITY | 0x331);
-              break;
-            }
-            const int kind = (ia < rs) ? 0 : 1;
-            s_rec[np++] = p.partials + ((size_t(k) * 2 + kind) * NSLOT + s) * kRecFloats;
-          }
-          rs = next;
+    const int4 d = __ldcg(reinterpret_cast<const int4*>(p.combine_desc) + b);
+    if (d.x > s) {  // owner boundary and the pair uses this slot
+      const int per_tile = p.hkv * p.pairs;
+      const int total = p.blk_prefix[p.n_qtiles] * per_tile;
+      const bool dense = total >= G;  // every range non-empty
+      int np = 0;
+      s_rec[np++] = p.partials + ((size_t(b - 1) * 2 + 1) * NSLOT + s) * kRecWords;
+      for (int k = b; k <= d.w; ++k) {
+        if (!dense && range_start(k + 1, total, G) == range_start(k, total, G)) continue;
+        if (np >= kMaxCombinePieces) {
+          report(p.status, HSD_DEV_CAPACITY | 0x331);
+          break;
         }
-        s_np = np;
-        s_q0 = qt * BM;
-        s_h = kvh * p.group + 2 * pair + s;
+        s_rec[np++] = p.partials + ((size_t(k) * 2 + 0) * NSLOT + s) * kRecWords;
       }
+      s_np = np;
+      s_q0 = d.y;
+      s_h = d.z + s;
     }
   }
   __syncthreads();
@@ -606,7 +622,7 @@ __global__ void __launch_bounds__(512) combine_kernel(const Params p, int G) {
   const int r = threadIdx.x & 127, ch = threadIdx.x >> 7;  // row, 32-column chunk
   float M = -INFINITY, L = 0.f;
   for (int i = 0; i < np; ++i) {
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(s_rec[i] + 128 * 128) + r);
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(s_rec[i] + 128 * 64) + r);
     if (ml.x > M) {
       L = (M == -INFINITY ? 0.f : L * ex2_approx(M - ml.x)) + ml.y;
       M = ml.x;
@@ -618,19 +634,22 @@ __global__ void __launch_bounds__(512) combine_kernel(const Params p, int G) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) acc[i] = 0.f;
   for (int i = 0; i < np; ++i) {
-    const float* rk = s_rec[i];
-    const float mk = __ldcg(reinterpret_cast<const float2*>(rk + 128 * 128) + r).x;
-    const float wk = (M == -INFINITY || mk == -INFINITY) ? 0.f : ex2_approx(mk - M);
-    const float4* r4 = reinterpret_cast<const float4*>(rk);
-    float4 v[8];
+    const uint32_t* rk = s_rec[i];
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(rk + 128 * 64) + r);
+    // weight of the piece's normalised O: 2^(m_k - M) l_k
+    const float wk = (M == -INFINITY || ml.x == -INFINITY) ? 0.f : ex2_approx(ml.x - M) * ml.y;
+    const int4* r4 = reinterpret_cast<const int4*>(rk);
+    int4 v[4];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) v[c] = __ldcg(r4 + (ch * 8 + c) * 128 + r);
+    for (int c = 0; c < 4; ++c) v[c] = __ldcg(r4 + (ch * 4 + c) * 128 + r);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      acc[4 * c] += wk * v[c].x;
-      acc[4 * c + 1] += wk * v[c].y;
-      acc[4 * c + 2] += wk * v[c].z;
-      acc[4 * c + 3] += wk * v[c].w;
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t w[4] = {uint32_t(v[c].x), uint32_t(v[c].y), uint32_t(v[c].z), uint32_t(v[c].w)};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[8 * c + 2 * e] += wk * __uint_as_float(w[e] << 16);
+        acc[8 * c + 2 * e + 1] += wk * __uint_as_float(w[e] & 0xFFFF0000u);
+      }
     }
   }
   const int q = s_q0 + r;
@@ -714,7 +733,7 @@ int sm_count() {
 }
 
 struct WsLayout {
-  size_t partials, total;
+  size_t partials, desc, total;
   int items, grid;
 };
 
@@ -725,7 +744,8 @@ WsLayout ws_layout(int32_t q_len, int32_t hq, int32_t hkv) {
   L.items = n_qtiles * hkv * pairs;
   L.grid = sm_count();
   L.partials = 0;
-  L.total = size_t(L.grid) * 2 * attn::NSLOT * attn::kRecFloats * sizeof(float);
+  L.desc = size_t(L.grid) * 2 * attn::NSLOT * attn::kRecWords * sizeof(uint32_t);
+  L.total = L.desc + size_t(L.grid) * 4 * sizeof(int32_t);
   return L;
 }
 
@@ -798,8 +818,10 @@ extern "C" int hsd_verify_attention(const void* q, int64_t q_row_stride, int64_t
   p.n_kv128 = plan->n_kv128;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.split = split ? 1 : 0;
-  p.partials = split ? reinterpret_cast<float*>(static_cast<char*>(workspace) + W.partials)
+  p.partials = split ? reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + W.partials)
                      : nullptr;
+  p.combine_desc =
+      split ? reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + W.desc) : nullptr;
   const size_t smem = sizeof(attn::Smem) + 1024;
   static bool attr_set = false;
   if (!attr_set) {
@@ -817,6 +839,19 @@ extern "C" int hsd_verify_attention(const void* q, int64_t q_row_stride, int64_t
   attn::verify_attn_kernel<<<grid, attn::kThreads, smem, st>>>(tq, tk, tv, p);
   rc = hsd_host::cuda_check(cudaGetLastError(), "verify_attn_kernel launch");
   if (rc || !split || W.grid < 2) return rc;
-  attn::combine_kernel<<<(W.grid - 1) * attn::NSLOT, 512, 0, st>>>(p, W.grid);
-  return hsd_host::cuda_check(cudaGetLastError(), "combine_kernel launch");
+  // programmatic dependent launch: the combine grid starts its item lookup
+  // while the attention grid drains and waits (griddepcontrol.wait) for its
+  // partials
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned((W.grid - 1) * attn::NSLOT));
+  cfg.blockDim = dim3(512);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return hsd_host::cuda_check(cudaLaunchKernelEx(&cfg, attn::combine_kernel, p, W.grid),
+                              "combine_kernel launch");
 }

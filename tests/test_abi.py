@@ -82,7 +82,7 @@ def test_attention_workspace_size_host_only():
     assert lib.hsd_attention_workspace_bytes(128, 12, 5) == 0
     n = lib.hsd_attention_workspace_bytes(2176, 12, 2)
     # partial rows for every SM (148 on B200 when no GPU is visible)
-    assert n >= 148 * 2 * 2 * (128 * 128 + 256) * 4
+    assert n >= 148 * 2 * 2 * (128 * 64 + 256) * 4
 
 
 def test_other_entry_points_reject_null_arguments():

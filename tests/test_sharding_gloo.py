@@ -1,0 +1,79 @@
+"""Page sharding and the rank-0 result gather, on CPU ranks over gloo."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from hsd_b200 import sharding as S
+
+
+def test_lpt_sharding_covers_every_page_once_and_balances():
+    costs = [((i * 7919) % 97) + 1 for i in range(256)]
+    for world in (1, 2, 4, 8):
+        shards = S.shard_pages(costs, world)
+        flat = sorted(i for s in shards for i in s)
+        assert flat == list(range(256))
+        loads = [sum(costs[i] for i in s) for s in shards]
+        assert max(loads) - min(loads) <= max(costs)
+
+
+def test_sharding_is_deterministic():
+    costs = [5, 5, 3, 3, 8, 1, 1, 9]
+    assert S.shard_pages(costs, 3) == S.shard_pages(list(costs), 3)
+
+
+def test_page_cost_orders_by_size():
+    from hsd_b200 import workloads as W
+    small, large = W.multi_page(0), W.multi_page(1)
+    pages = sorted([small, large], key=lambda p: p.q_len * p.prefix)
+    assert S.page_cost(pages[0]) <= S.page_cost(pages[1])
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, n_pages, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        costs = [(i % 5) + 1 for i in range(n_pages)]
+        mine = S.shard_pages(costs, world)[rank]
+        # each page's "result" is a deterministic variable-length token list
+        local = {i: torch.arange(i % 7 + 1) + 1000 * i for i in mine}
+        out = S.gather_page_results(local, n_pages, dst=0)
+        if rank == 0:
+            q.put({k: v.tolist() for k, v in out.items()})
+        else:
+            q.put(None if out is None else "unexpected")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gather_to_rank0_over_gloo(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    n_pages = 11
+    procs = [ctx.Process(target=_worker, args=(r, world, port, n_pages, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    gathered = [r for r in results if isinstance(r, dict)]
+    assert len(gathered) == 1 and all(r is None for r in results if not isinstance(r, dict))
+    got = gathered[0]
+    assert sorted(got) == list(range(n_pages))
+    for i in range(n_pages):
+        assert got[i] == [1000 * i + t for t in range(i % 7 + 1)]
