@@ -246,6 +246,9 @@ def run_ours(args):
     # per-launch attention events of the timed steps (same stream)
     ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(step.L)]
           for _ in range(args.steps)]
+    phases = ("append", "plan", "accept", "keep", "compact", "bits")
+    pev = [{k: [torch.cuda.Event(enable_timing=True) for _ in range(2)] for k in phases}
+           for _ in range(args.steps)]
     gpu_index = local
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     if vis:
@@ -263,7 +266,7 @@ def run_ours(args):
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
     for i in range(args.steps):
-        step.run(stream, attn_events=ev[i])
+        step.run(stream, attn_events=ev[i], phase_events=pev[i])
     t_end.record(stream)
     torch.cuda.synchronize()
     if world > 1:
@@ -274,6 +277,10 @@ def run_ours(args):
     attn_ms = [ev[i][l][0].elapsed_time(ev[i][l][1]) for i in range(args.steps)
                for l in range(step.L)]
     attn_avg_ms = sum(attn_ms) / len(attn_ms)
+    breakdown = {k: sum(pev[i][k][0].elapsed_time(pev[i][k][1]) for i in range(args.steps))
+                 / args.steps for k in phases}
+    breakdown["attention_all_layers"] = attn_avg_ms * step.L
+    comp_bytes, comp_moved, comp_kept = step.compaction_bytes()
 
     # end to end: pinned host inputs in, results out, every step
     step.host_buffers()
@@ -326,6 +333,14 @@ def run_ours(args):
             "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": step.h2d_bytes(),
                     "d2h_bytes_per_step": step.d2h_bytes()},
+            "breakdown_ms_per_step": breakdown,
+            "compaction": {"bound": "hbm", "bytes_per_launch": comp_bytes,
+                           "rows_moved": comp_moved, "rows_kept": comp_kept,
+                           "planes": int(step.planes.numel()),
+                           "achieved_gbs": comp_bytes / (breakdown["compact"] * 1e-3) / 1e9,
+                           "peak_gbs": peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]),
+                           "frac": comp_bytes / (breakdown["compact"] * 1e-3) / 1e9
+                           / peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])},
             "gpu_launches": args.steps * step.kernel_launches_per_step,
             "clocks": clocks,
         }

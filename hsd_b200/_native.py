@@ -79,6 +79,7 @@ SIGNATURES = [
      [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64, _P, _P, _I32, _I32, _I32, _I32,
       _I32, _F, C.POINTER(Plan), _P, _SZ, _P, _P]),
     ("hsd_compact_kv", C.c_int, [_P, _I32, _I32, _P, _I32, _P, _P, _P]),
+    ("hsd_kv_append", C.c_int, [_P, _P, _I32, _I32, _I32, _I32, _P]),
     ("hsd_keep_indices", C.c_int, [_P, _I32, _I32, _P, _I32, _P, _P, _P, _P]),
     ("hsd_compact_bits", C.c_int, [_P, _P, _I32, _I32, _P, _P, _I32, _P]),
     ("hsd_accept_kmp", C.c_int,

@@ -62,6 +62,16 @@ def compact_kv(planes, row_bytes, keep_idx, n_keep=None, counts=None, status=Non
                                N.ptr(status), N.stream_handle(stream)), "hsd_compact_kv")
 
 
+def kv_append(dst_planes, src_planes, row_bytes, dst_row0, n_rows, stream=None):
+    """Append ``n_rows`` rows of every source plane at ``dst_row0`` of its
+    destination plane (the cache update ``DynamicCache.update`` does with
+    ``torch.cat``)."""
+    lib = N.load()
+    N.check(lib.hsd_kv_append(N.ptr(dst_planes), N.ptr(src_planes), dst_planes.numel(),
+                              int(row_bytes), int(dst_row0), int(n_rows),
+                              N.stream_handle(stream)), "hsd_kv_append")
+
+
 def compact_bits(in_bits, keep_idx, counts, out_words, out=None, stream=None):
     """Visibility rows after compaction: out[r] bit i = in[r] bit keep_idx[i]."""
     lib = N.load()

@@ -21,7 +21,7 @@ namespace hsd {
 namespace compact {
 
 constexpr int kThreads = 256;
-constexpr int kVec = 8;  // 16-byte vectors staged per thread per wave
+constexpr int kVec = 16;  // 16-byte vectors staged per thread per wave
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
@@ -172,6 +172,33 @@ __global__ void compact_bits_kernel(const uint64_t* in, uint64_t* out, int n_row
   }
 }
 
+// Batched row append: plane p gets n_rows rows at dst_row0 from src plane p.
+// One CTA streams a contiguous span of one plane with 16-byte vectors, four
+// loads in flight per thread.
+__global__ void __launch_bounds__(256) append_kernel(const uint64_t* __restrict__ dst_planes,
+                                                     const uint64_t* __restrict__ src_planes,
+                                                     int n_planes, int row_bytes, int dst_row0,
+                                                     int n_rows, int chunks) {
+  const int plane = blockIdx.x / chunks, chunk = blockIdx.x % chunks;
+  if (plane >= n_planes) return;
+  const size_t nvec = size_t(n_rows) * (row_bytes >> 4);
+  const size_t per = (nvec + chunks - 1) / chunks;
+  const size_t v0 = size_t(chunk) * per, v1 = v0 + per < nvec ? v0 + per : nvec;
+  const int4* src = reinterpret_cast<const int4*>(src_planes[plane]);
+  int4* dst = reinterpret_cast<int4*>(reinterpret_cast<char*>(dst_planes[plane]) +
+                                      size_t(dst_row0) * row_bytes);
+  size_t v = v0 + threadIdx.x;
+  for (; v + 3 * blockDim.x < v1; v += 4 * blockDim.x) {
+    const int4 a = __ldcs(src + v), b = __ldcs(src + v + blockDim.x),
+               c = __ldcs(src + v + 2 * blockDim.x), d = __ldcs(src + v + 3 * blockDim.x);
+    dst[v] = a;
+    dst[v + blockDim.x] = b;
+    dst[v + 2 * blockDim.x] = c;
+    dst[v + 3 * blockDim.x] = d;
+  }
+  for (; v < v1; v += blockDim.x) dst[v] = __ldcs(src + v);
+}
+
 }  // namespace compact
 }  // namespace hsd
 
@@ -212,6 +239,23 @@ int hsd_compact_kv(const uint64_t* plane_ptrs, int32_t n_planes, int32_t row_byt
       cudaLaunchKernelEx(&cfg, compact::compact_planes_kernel, plane_ptrs, int(n_planes),
                          int(row_bytes), keep_idx, int(n_keep), counts, status),
       "compact_planes_kernel launch");
+}
+
+int hsd_kv_append(const uint64_t* dst_planes, const uint64_t* src_planes, int32_t n_planes,
+                  int32_t row_bytes, int32_t dst_row0, int32_t n_rows, hsd_stream_t stream) {
+  if (!dst_planes || !src_planes || n_planes <= 0 || row_bytes <= 0 || (row_bytes & 15) ||
+      dst_row0 < 0 || n_rows < 0) {
+    hsd_host::set_error("hsd_kv_append: bad arguments (n_planes=%d row_bytes=%d)", n_planes,
+                        row_bytes);
+    return HSD_ERR_INVALID_ARG;
+  }
+  if (n_rows == 0) return HSD_OK;
+  const int64_t nvec = int64_t(n_rows) * (row_bytes >> 4);
+  int chunks = int((nvec + 4095) / 4096);  // ~64 KB per CTA
+  if (chunks < 1) chunks = 1;
+  compact::append_kernel<<<n_planes * chunks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      dst_planes, src_planes, n_planes, row_bytes, dst_row0, n_rows, chunks);
+  return hsd_host::cuda_check(cudaGetLastError(), "append_kernel launch");
 }
 
 int hsd_keep_indices(const uint64_t* live_bits, int32_t n_live, int32_t live_stride,

@@ -109,30 +109,53 @@ class VerifyStep:
                 for h in range(hkv):
                     planes.append(self.cache[l, kv, h].data_ptr())
         self.planes = torch.tensor(planes, dtype=torch.int64, device=dev)
+        src = []
+        for l in range(L):
+            for kv in range(2):
+                for h in range(hkv):
+                    src.append(self.new_kv[l, kv, h].data_ptr())
+        self.new_planes = torch.tensor(src, dtype=torch.int64, device=dev)
         self.row_bytes = d * 2
         self.period = period
         self._host = None
         self.attn_launches_per_step = L
-        self.kernel_launches_per_step = 2 + L + 1 + 1 + 1 + 1
+        # append 1 + plan 2 + attention L x (main + combine) + accept 1 + keep 1
+        # + compact 1 + bits 1
+        self.kernel_launches_per_step = 1 + 2 + 2 * L + 4
 
     # ------------------------------------------------------------------
     def _ptr(self, t):
         return C.c_void_p(t.data_ptr())
 
-    def run(self, stream=None, attn_events=None):
-        """Launch one verification step on ``stream`` (no host sync)."""
+    def run(self, stream=None, attn_events=None, phase_events=None):
+        """Launch one verification step on ``stream`` (no host sync).
+
+        ``attn_events[l]`` (start, end) bracket layer l's attention call;
+        ``phase_events`` (dict of name -> (start, end)) bracket the phases
+        append / plan / accept / keep / compact / bits.
+        """
         lib = N.load()
         st = N.stream_handle(stream)
         p = self._ptr
+        ev = phase_events or {}
+
+        def mark(name, i):
+            if name in ev:
+                ev[name][i].record(stream)
         # 1. KV append (the model's cache update)
-        self.cache[:, :, :, self.prefix:self.prefix + self.q_len].copy_(self.new_kv)
+        mark("append", 0)
+        N.check(lib.hsd_kv_append(p(self.planes), p(self.new_planes), self.planes.numel(),
+                                  self.row_bytes, self.prefix, self.q_len, st), "hsd_kv_append")
+        mark("append", 1)
         self.filter.zero_()
         self.blocks.copy_(self.blocks0)
+        mark("plan", 0)
         # 2. tile plan
         m = self.mask
         N.check(lib.hsd_build_plan_segments(
             p(m.segs), m.n_segs, p(m.row_seg), p(m.kv_bits), m.stride, p(m.tree_bits),
             C.byref(self.plan.struct), p(self.status), st), "hsd_build_plan_segments")
+        mark("plan", 1)
         # 3. attention, every layer
         scale = 1.0 / np.sqrt(self.d)
         ql, kvl, hq, hkv, d = self.q_len, self.kv_len, self.hq, self.hkv, self.d
@@ -150,21 +173,35 @@ class VerifyStep:
             if attn_events is not None:
                 attn_events[l][1].record(stream)
         # 4. acceptance + KMP
+        mark("accept", 0)
         N.check(lib.hsd_accept_kmp(
             C.byref(self.cfg), p(self.blocks), p(self.results), p(self.next_ids),
             p(self.input_ids), p(self.gen_pool), p(self.draft_pool), p(self.tree_dummy),
             p(self.tree_dummy), p(m.kv_bits), p(self.vis), p(self.filter), p(self.status), st),
             "hsd_accept_kmp")
+        mark("accept", 1)
         # 5. keep indices, in-place compaction, visibility remap
+        mark("keep", 0)
         N.check(lib.hsd_keep_indices(p(self.vis), self.n_blocks, self.stride, p(self.filter),
                                      self.kv_len, p(self.keep_bits), p(self.keep_idx),
                                      p(self.counts), st), "hsd_keep_indices")
+        mark("keep", 1)
+        mark("compact", 0)
         N.check(lib.hsd_compact_kv(p(self.planes), self.planes.numel(), self.row_bytes,
                                    p(self.keep_idx), -1, p(self.counts), p(self.status), st),
                 "hsd_compact_kv")
+        mark("compact", 1)
+        mark("bits", 0)
         N.check(lib.hsd_compact_bits(p(self.vis), p(self.vis_next), self.n_blocks, self.stride,
                                      p(self.keep_idx), p(self.counts), self.stride, st),
                 "hsd_compact_bits")
+        mark("bits", 1)
+
+    def compaction_bytes(self):
+        """(bytes moved by the last compaction (read + write), rows moved, rows kept)."""
+        n_keep, first = (int(x) for x in self.counts.cpu().tolist())
+        moved = max(0, n_keep - first)
+        return 2 * moved * self.row_bytes * self.planes.numel(), moved, n_keep
 
     # ------------------------------------------------------------------
     def host_buffers(self):

@@ -200,6 +200,13 @@ int hsd_compact_kv(const uint64_t *plane_ptrs, int32_t n_planes, int32_t row_byt
                    const int32_t *keep_idx, int32_t n_keep,
                    const int32_t *counts, int32_t *status, hsd_stream_t stream);
 
+/* KV-cache append: for every plane p, rows [dst_row0, dst_row0 + n_rows) of
+ * dst_planes[p] <- rows [0, n_rows) of src_planes[p] (row_bytes contiguous
+ * bytes each).  The per-layer cache update the reference gets from
+ * DynamicCache.update, a torch.cat along the sequence (D:356-359). */
+int hsd_kv_append(const uint64_t *dst_planes, const uint64_t *src_planes, int32_t n_planes,
+                  int32_t row_bytes, int32_t dst_row0, int32_t n_rows, hsd_stream_t stream);
+
 /* keep = (OR of live_bits rows [0, n_live)) & ~filter_bits, then the ascending
  * indices of set bits (keep_idx), their count and the first index that moves
  * (D:1679-1707).  Counts land in counts[0] = n_keep, counts[1] = first_moved. */

@@ -93,3 +93,19 @@ def test_compact_bits_remaps_visibility(dev):
     got = np.unpackbits(out.cpu().numpy().view(np.uint8).reshape(7, stride, 8), axis=-1,
                         bitorder="little").reshape(7, stride * 64)[:, :n].astype(bool)
     np.testing.assert_array_equal(got, exp)
+
+
+def test_kv_append_matches_slice_copy(dev):
+    from hsd_b200.compaction import kv_append
+    L, hkv, cap, q, d = 3, 2, 900, 333, 128
+    cache = torch.randn(L, 2, hkv, cap, d, device=dev).to(torch.bfloat16)
+    new = torch.randn(L, 2, hkv, q, d, device=dev).to(torch.bfloat16)
+    ref = cache.clone()
+    ref[:, :, :, 500:500 + q] = new
+    dst = torch.tensor([cache[l, k, h].data_ptr() for l in range(L) for k in range(2)
+                        for h in range(hkv)], dtype=torch.int64, device=dev)
+    src = torch.tensor([new[l, k, h].data_ptr() for l in range(L) for k in range(2)
+                        for h in range(hkv)], dtype=torch.int64, device=dev)
+    kv_append(dst, src, d * 2, 500, q)
+    torch.cuda.synchronize()
+    assert torch.equal(cache, ref)
