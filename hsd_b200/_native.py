@@ -78,6 +78,10 @@ SIGNATURES = [
     ("hsd_verify_attention", C.c_int,
      [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64, _P, _P, _I32, _I32, _I32, _I32,
       _I32, _F, C.POINTER(Plan), _P, _SZ, _P, _P]),
+    ("hsd_attention_static_scratch_bytes", _SZ, []),
+    ("hsd_verify_attention_static_scratch", C.c_int,
+     [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64, _P, _P, _I32, _I32, _I32, _I32,
+      _I32, _F, C.POINTER(Plan), _P, _P]),
     ("hsd_compact_kv", C.c_int, [_P, _I32, _I32, _P, _I32, _P, _P, _P]),
     ("hsd_kv_append", C.c_int, [_P, _P, _I32, _I32, _I32, _I32, _P]),
     ("hsd_keep_indices", C.c_int, [_P, _I32, _I32, _P, _I32, _P, _P, _P, _P]),

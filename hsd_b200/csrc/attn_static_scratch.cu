@@ -1,0 +1,95 @@
+// Verification attention whose stream-K scratch lives in a static device
+// array instead of a caller-allocated workspace.
+//
+// For callers that cannot allocate device memory at the point of the call:
+// code running under a CUDA graph capture (cudaMalloc is not capturable), a
+// serving loop that must not go through an allocator between steps, or a
+// host binding that has no device allocator of its own.  The kernels and the
+// schedule are those of hsd_verify_attention; only where the scratch comes
+// from differs.
+//
+// Setup: the first call on each device (that device current) looks up the
+// array's device address with cudaGetSymbolAddress and caches it; this may
+// load the module, so make that first call before any stream capture.
+// Later calls only read the cached address.
+//
+// Limits: the scratch holds kStaticScratchBytes (20 MiB), enough for the
+// stream-K schedule on devices of up to 155 SMs (each SM's CTA needs
+// 2 x 2 x 33 KB of partial records plus a 16-byte descriptor).  A call whose
+// scratch need exceeds it returns HSD_ERR_TOO_LARGE and launches nothing.
+// Nothing in the scratch has to start at zero: every word the merge kernel
+// reads is written earlier in the same call.  There is one scratch per
+// device, so calls on one device must not overlap in time -- issue them on
+// one stream (or order them with events); two concurrent calls race on the
+// partial records and corrupt each other's output.
+#include <mutex>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(20) << 20;
+constexpr int kMaxDevices = 64;
+
+__device__ __align__(256) unsigned char g_attn_scratch[kStaticScratchBytes];
+
+std::mutex g_mu;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+int scratch_for_current_device(void** out) {
+  int dev = 0;
+  int rc = hsd_host::cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= kMaxDevices) {
+    hsd_host::set_error("hsd_verify_attention_static_scratch: device ordinal %d >= %d", dev,
+                        kMaxDevices);
+    return HSD_ERR_UNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    rc = hsd_host::cuda_check(cudaGetSymbolAddress(&p, g_attn_scratch),
+                              "cudaGetSymbolAddress(static attention scratch)");
+    if (rc) return rc;
+    if (!p || (reinterpret_cast<uintptr_t>(p) & 255)) {
+      hsd_host::set_error("hsd_verify_attention_static_scratch: scratch address %p not "
+                          "256-byte aligned", p);
+      return HSD_ERR_CUDA;
+    }
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return HSD_OK;
+}
+
+}  // namespace
+
+extern "C" size_t hsd_attention_static_scratch_bytes(void) { return kStaticScratchBytes; }
+
+extern "C" int hsd_verify_attention_static_scratch(
+    const void* q, int64_t q_row_stride, int64_t q_head_stride, const void* k,
+    int64_t k_row_stride, int64_t k_head_stride, const void* v, int64_t v_row_stride,
+    int64_t v_head_stride, void* out, float* lse, int32_t q_len, int32_t kv_len,
+    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, float scale,
+    const hsd_plan_t* plan, int32_t* status, hsd_stream_t stream) {
+  const size_t need = hsd_attention_workspace_bytes(q_len, num_q_heads, num_kv_heads);
+  if (need == 0) {
+    hsd_host::set_error("hsd_verify_attention_static_scratch: bad sizes (q_len=%d heads=%d/%d)",
+                        q_len, num_q_heads, num_kv_heads);
+    return HSD_ERR_INVALID_ARG;
+  }
+  if (need > kStaticScratchBytes) {
+    hsd_host::set_error("hsd_verify_attention_static_scratch: needs %zu bytes of scratch on "
+                        "this device, the static scratch holds %zu; use hsd_verify_attention "
+                        "with a workspace",
+                        need, kStaticScratchBytes);
+    return HSD_ERR_TOO_LARGE;
+  }
+  void* scratch = nullptr;
+  const int rc = scratch_for_current_device(&scratch);
+  if (rc) return rc;
+  return hsd_verify_attention(q, q_row_stride, q_head_stride, k, k_row_stride, k_head_stride, v,
+                              v_row_stride, v_head_stride, out, lse, q_len, kv_len, num_q_heads,
+                              num_kv_heads, head_dim, scale, plan, scratch, kStaticScratchBytes,
+                              status, stream);
+}

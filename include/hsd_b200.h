@@ -187,6 +187,29 @@ int hsd_verify_attention(const void *q, int64_t q_row_stride, int64_t q_head_str
                          float scale, const hsd_plan_t *plan, void *workspace,
                          size_t workspace_bytes, int32_t *status, hsd_stream_t stream);
 
+/* No counterpart in the reference (it allocates through PyTorch on every
+ * call).  hsd_verify_attention with the stream-K scratch taken from a static
+ * device array of hsd_attention_static_scratch_bytes() bytes (20 MiB, enough
+ * for devices of up to 155 SMs) instead of a caller workspace, so the call
+ * allocates nothing: for callers under a CUDA graph capture, or that must not
+ * reach an allocator between serving steps.  The first call on each device
+ * (that device current) looks up the array's address -- make it before any
+ * stream capture.  A scratch need above the array's size returns
+ * HSD_ERR_TOO_LARGE.  Nothing in the scratch needs to start at zero.  One
+ * scratch per device: calls on one device must not overlap in time (one
+ * stream, or ordered by events), or they race on it.  Other arguments as
+ * hsd_verify_attention. */
+size_t hsd_attention_static_scratch_bytes(void);
+int hsd_verify_attention_static_scratch(const void *q, int64_t q_row_stride,
+                                        int64_t q_head_stride, const void *k,
+                                        int64_t k_row_stride, int64_t k_head_stride,
+                                        const void *v, int64_t v_row_stride,
+                                        int64_t v_head_stride, void *out, float *lse,
+                                        int32_t q_len, int32_t kv_len, int32_t num_q_heads,
+                                        int32_t num_kv_heads, int32_t head_dim, float scale,
+                                        const hsd_plan_t *plan, int32_t *status,
+                                        hsd_stream_t stream);
+
 /* ---- (2) KV-cache compaction -------------------------------------------- */
 
 /* In place, for every plane p (one layer's K or V of one KV head, rows of
