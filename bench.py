@@ -23,6 +23,7 @@ layer of attention per step, extrapolated to all layers.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -63,9 +64,12 @@ def profile_traffic(name):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during timing."""
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms; ``stop()``
+    keeps the samples taken between ``mark_start()`` and ``mark_end()`` (the
+    timed region), or all of them if the region was shorter than one
+    sampling interval."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -73,6 +77,13 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self.t0 = self.t1 = None
+
+    def mark_start(self):
+        self.t0 = datetime.datetime.now()
+
+    def mark_end(self):
+        self.t1 = datetime.datetime.now()
 
     def start(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
@@ -80,7 +91,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -96,9 +107,17 @@ class ClockSampler:
         rows = []
         for line in open(self.path):
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
-                rows.append(parts)
+            if len(parts) >= 10 and parts[2].replace(".", "").isdigit():
+                try:
+                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+                except ValueError:
+                    ts = None
+                rows.append((ts, parts[1:]))
         os.unlink(self.path)
+        inside = [r for ts, r in rows if ts is not None and self.t0 is not None
+                  and self.t1 is not None and self.t0 <= ts <= self.t1]
+        window = "timed region" if inside else "around the timed region"
+        rows = inside or [r for _, r in rows]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         sm = [float(r[1]) for r in rows]
@@ -107,7 +126,8 @@ class ClockSampler:
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
         loaded = [s for s in sm if s > 0.5 * mx] or sm
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows)}
+                "samples": len(rows), "window": window,
+                "power_w_max": max(float(r[3]) for r in rows)}
 
 
 # ---------------------------------------------------------------- CPU side
@@ -264,11 +284,13 @@ def run_ours(args):
     torch.cuda.synchronize()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    sampler.mark_start()
     t_start.record(stream)
     for i in range(args.steps):
         step.run(stream, attn_events=ev[i], phase_events=pev[i])
     t_end.record(stream)
     torch.cuda.synchronize()
+    sampler.mark_end()
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
@@ -362,7 +384,7 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="stage1_regions",

@@ -7,10 +7,14 @@
 //
 // In place is safe because keep_idx is ascending, so keep_idx[i] >= i: a
 // "wave" of destination rows [w0, w1) reads sources >= w0 and earlier waves
-// only wrote rows < w0.  Within a wave every source is read into registers
-// before any destination is written, and the CTAs that share one plane form a
-// thread-block cluster whose hardware barrier separates the read and write
-// phases -- no global spin-waits.
+// only wrote rows < w0.  Within a wave every source is read before any
+// destination is written.  Two launch shapes:
+//  * many planes (>= kPlaneCtaMinPlanes): one CTA per plane moving rows with
+//    the bulk-copy engine through two shared-memory buffers
+//    (compact_plane_bulk_kernel);
+//  * few planes: a thread-block cluster per plane staging a wave in
+//    registers, the cluster's hardware barrier separating the read and write
+//    phases (compact_planes_kernel) -- no global spin-waits in either.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -85,6 +89,137 @@ __global__ void __launch_bounds__(kThreads) compact_planes_kernel(
     }
     cluster_sync_all();
   }
+}
+
+constexpr int kIdxCache = 8192;  // staged keep indices (32 KB); the rest read from global
+
+// ---- bulk-copy (TMA engine) variant of the one-CTA-per-plane compaction
+//
+// The copy engine keeps far more bytes in flight per SM than 16-byte register
+// loads, so one CTA per plane streams close to HBM speed.  Waves of destination rows
+// [d0, d1) alternate between two shared-memory buffers: the sources of a wave
+// are fetched as runs of consecutive rows (at most 32 rows per run, found
+// with one warp ballot per 32 destinations) completing on the buffer's
+// mbarrier, then the whole wave goes back with one contiguous bulk store.  The
+// hazard argument is the one above: a wave's sources lie at or above its first
+// destination, which is above every row an earlier wave stores, and a wave's
+// store is issued only after its own loads have landed (after the loads of
+// every earlier wave).  Before a buffer is refilled, the store that read it
+// must have finished reading shared memory.
+constexpr int kBulkThreads = 256;
+constexpr int kBulkBuf = 96 * 1024;  // bytes per staging buffer (two buffers)
+constexpr int kBulkSmem = 2 * kBulkBuf + kIdxCache * 4 + 64;
+
+__device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst_smem)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_store(void* dst, const void* src_smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+               ::"l"(reinterpret_cast<uint64_t>(dst)), "r"(smem_u32(src_smem)), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kBulkThreads, 1) compact_plane_bulk_kernel(
+    const uint64_t* __restrict__ plane_ptrs, int n_planes, int row_bytes,
+    const int32_t* __restrict__ keep_idx, int n_keep_host, const int32_t* counts,
+    int32_t* status) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  int32_t* s_idx = reinterpret_cast<int32_t*>(smem + 2 * kBulkBuf);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * kBulkBuf + kIdxCache * 4);
+  volatile int* abort = reinterpret_cast<volatile int*>(bar + 2);
+  const int plane = blockIdx.x;
+  const int n_keep = counts ? counts[0] : n_keep_host;
+  const int first = counts ? counts[1] : 0;
+  if (plane >= n_planes || first >= n_keep) return;
+  char* base = reinterpret_cast<char*>(plane_ptrs[plane]);
+  if (reinterpret_cast<uintptr_t>(base) & 15) {  // bulk copies need 16-byte alignment
+    if (threadIdx.x == 0) report(status, HSD_DEV_BAD_INDEX | 5);
+    return;
+  }
+  const int n_moved = n_keep - first;
+  const int n_cached = n_moved < kIdxCache ? n_moved : kIdxCache;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i < n_cached; i += kBulkThreads) s_idx[i] = keep_idx[first + i];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int rows_per_wave = kBulkBuf / row_bytes;
+  const int n_waves = (n_moved + rows_per_wave - 1) / rows_per_wave;
+  // Loads of wave wv+1 are issued before wave wv is waited for, so two waves
+  // of loads are in flight; wave wv+1's sources lie above every row wave wv
+  // stores, and its buffer was last read by the store of wave wv-1.
+  int issued = 0;
+  auto issue_wave = [&](int wv) {
+    const int b = wv & 1;
+    const int d0 = first + wv * rows_per_wave;
+    const int d1 = d0 + rows_per_wave < n_keep ? d0 + rows_per_wave : n_keep;
+    if (threadIdx.x == 0) {
+      bulk_wait_read_all();  // the store that last read buffer b is done reading it
+      mbar_arrive_expect_tx(&bar[b], uint32_t(d1 - d0) * uint32_t(row_bytes));
+    }
+    __syncthreads();
+    for (int g0 = d0 + warp * 32; g0 < d1; g0 += kBulkThreads) {
+      const int d = g0 + lane;
+      const bool valid = d < d1;
+      const int j = d - first;
+      const int src = valid ? (j < kIdxCache ? s_idx[j] : keep_idx[d]) : 0;
+      const int prev = __shfl_up_sync(0xffffffffu, src, 1);
+      const bool start = valid && (lane == 0 || src != prev + 1);
+      const uint32_t starts = __ballot_sync(0xffffffffu, start);
+      if (start) {
+        if (src < d) report(status, HSD_DEV_BAD_INDEX | 4);  // not ascending
+        const uint32_t above = starts & ~((2u << lane) - 1u);
+        const int end = g0 + (above ? __ffs(above) - 1 : 32);
+        const int e = end < d1 ? end : d1;
+        bulk_load(smem + size_t(b) * kBulkBuf + size_t(d - d0) * row_bytes,
+                  base + size_t(src) * row_bytes, uint32_t(e - d) * uint32_t(row_bytes), &bar[b]);
+      }
+    }
+    issued = wv + 1;
+  };
+  issue_wave(0);
+  for (int wv = 0; wv < n_waves; ++wv) {
+    if (wv + 1 < n_waves) issue_wave(wv + 1);
+    const int b = wv & 1;
+    const uint32_t parity = uint32_t(wv >> 1) & 1u;
+    const int d0 = first + wv * rows_per_wave;
+    const int d1 = d0 + rows_per_wave < n_keep ? d0 + rows_per_wave : n_keep;
+    if (threadIdx.x == 0) {
+      if (!mbar_wait(&bar[b], parity, abort, status, 0x500 + b, false)) {
+        // loads of this wave (and of the next, if issued) are still in
+        // flight: let them land before the CTA's shared memory goes away
+        mbar_wait(&bar[b], parity, abort, nullptr, 0, false);
+        if (issued > wv + 1)
+          mbar_wait(&bar[b ^ 1], uint32_t((wv + 1) >> 1) & 1u, abort, nullptr, 0, false);
+        *abort = 1;
+      } else {
+        bulk_store(base + size_t(d0) * row_bytes, smem + size_t(b) * kBulkBuf,
+                   uint32_t(d1 - d0) * uint32_t(row_bytes));
+      }
+    }
+    __syncthreads();
+    if (*abort) break;
+  }
+  if (threadIdx.x == 0) bulk_wait_all();
 }
 
 // keep = OR(live rows) & ~filter; ascending indices of set bits; n_keep and
@@ -204,6 +339,13 @@ __global__ void __launch_bounds__(256) append_kernel(const uint64_t* __restrict_
 
 using namespace hsd;
 
+namespace {
+// With at least this many planes one CTA per plane keeps most SMs streaming.
+constexpr int kPlaneCtaMinPlanes = 64;
+constexpr int kMaxDevices = 64;
+bool g_bulk_attr_set[kMaxDevices] = {};
+}  // namespace
+
 extern "C" {
 
 int hsd_compact_kv(const uint64_t* plane_ptrs, int32_t n_planes, int32_t row_bytes,
@@ -219,8 +361,33 @@ int hsd_compact_kv(const uint64_t* plane_ptrs, int32_t n_planes, int32_t row_byt
     hsd_host::set_error("hsd_compact_kv: n_keep < 0 needs the device counts");
     return HSD_ERR_INVALID_ARG;
   }
-  // Enough CTAs per plane to cover the SMs a few times over, at most 8
-  // (portable cluster size).
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  static_assert(compact::kThreads * compact::kVec * 16 <= compact::kBulkBuf,
+                "every accepted row fits a bulk staging buffer");
+  if (n_planes >= kPlaneCtaMinPlanes) {
+    int dev = 0;
+    int rc = hsd_host::cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+    if (rc) return rc;
+    if (dev < 0 || dev >= kMaxDevices) {
+      hsd_host::set_error("hsd_compact_kv: device ordinal %d >= %d", dev, kMaxDevices);
+      return HSD_ERR_UNSUPPORTED;
+    }
+    if (!g_bulk_attr_set[dev]) {
+      rc = hsd_host::cuda_check(
+          cudaFuncSetAttribute(compact::compact_plane_bulk_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, compact::kBulkSmem),
+          "cudaFuncSetAttribute(compact_plane_bulk_kernel)");
+      if (rc) return rc;
+      g_bulk_attr_set[dev] = true;
+    }
+    compact::compact_plane_bulk_kernel<<<n_planes, compact::kBulkThreads, compact::kBulkSmem,
+                                         st>>>(plane_ptrs, n_planes, row_bytes, keep_idx, n_keep,
+                                               counts, status);
+    return hsd_host::cuda_check(cudaGetLastError(), "compact_plane_bulk_kernel launch");
+  }
+
+  // Few planes: a cluster of CTAs per plane, enough to cover the SMs a few
+  // times over, at most 8 (portable cluster size).
   int cs = 1;
   while (cs < 8 && n_planes * cs < 148 * 4) cs <<= 1;
   cudaLaunchConfig_t cfg = {};
