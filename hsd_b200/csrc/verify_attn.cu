@@ -10,22 +10,27 @@
 // empty 128x64 tiles never appear, partial 64-column halves carry per-row
 // 64-bit masks, absent halves are masked out).
 //
-//   warp 8      TMA producer: Q (once), then K_j and V_j into a 5-slot ring
-//   warp 9      MMA issuer (one thread): S = Q K^T (A, B in smem) and
-//               O += P V (P from TMEM, V in smem) on tcgen05
-//   warps 10-11 idle (complete the third warpgroup for setmaxnreg)
+//   warp 8      TMA producer: Q per piece, then K and V tiles into a 3-stage
+//               FIFO in the order the MMAs consume them: K_b0, then per block
+//               j: K_{j+1}, V_j
+//   warp 9      MMA issuer (one thread), tcgen05 with both operands in smem:
+//               S = Q K^T and O += P V
+//   warp 10     writes the stream-K merge descriptor; warp 11 idle (the
+//               third warpgroup is whole for setmaxnreg)
 //   warps 0-3   softmax + epilogue of head slot 0 (thread = query row)
 //   warps 4-7   softmax + epilogue of head slot 1
 //
 // TMEM (512 columns): slot s holds S_s at columns [256 s, 256 s + 128) and
 // O_s at [256 s + 128, 256 s + 256), fp32, lane = query row.  The softmax
-// overwrites the first 64 columns of S_s with P_s (bf16 pairs), which the PV
-// MMA reads as its A operand.  Per slot the MMA thread issues
-// PV_s(j) before S_s(j+1); tcgen05 MMAs of one thread complete in order, so
-// when the softmax sees S_s(j) complete, PV_s(j-1) is complete too -- O can be
-// rescaled and the S/P columns reused without further waits.  Softmax keeps a
-// running max in log2 units and rescales O only when the max grows by more
-// than kRescaleLog2 (exact: the final O / l and LSE use the same stale max).
+// reads S_s(j) into registers and releases the S columns at once (s_free), so
+// the MMA thread computes S_s(j+1) while the softmax of block j is still
+// running; P_s(j) goes to shared memory (bf16, the K-major 128-byte swizzled
+// layout of an MMA A operand) and O_s += P_s(j) V_j follows when the softmax
+// signals p_full.  The chain per slot is therefore softmax(j) -> softmax(j+1)
+// with the MMAs in its shadow.  Before the softmax rescales O or overwrites
+// P_s it waits for the previous PV (o_done).  Softmax keeps a running max in
+// log2 units and rescales O only when the max grows by more than
+// kRescaleLog2 (exact: the final O / l and LSE use the same stale max).
 #include "common.cuh"
 
 namespace hsd {
@@ -35,7 +40,7 @@ constexpr int BM = 128;  // query rows per tile
 constexpr int BN = 128;  // KV columns per block
 constexpr int HD = 128;  // head dim
 constexpr int NSLOT = 2;
-constexpr int NSTAGE = 5;
+constexpr int NSTAGE = 3;
 constexpr int TILE_BYTES = BN * HD * 2;  // 32 KB: a 128x128 bf16 tile
 constexpr int SUB_BYTES = 128 * 128;     // one 64-column swizzled sub-tile of 128 rows
 constexpr int kThreads = 384;  // 3 warpgroups: softmax slot 0, slot 1, producer + MMA
@@ -58,16 +63,19 @@ constexpr int kRecWords = 128 * 64 + 128 * 2;
 
 struct __align__(1024) Smem {
   uint8_t q[NSLOT][TILE_BYTES];
+  uint8_t pb[NSLOT][TILE_BYTES];  // P of the current block per slot (MMA A operand)
   uint8_t kv[NSTAGE][TILE_BYTES];
   uint64_t bar_q;
   uint64_t bar_q_free;
   uint64_t bar_full[NSTAGE];
   uint64_t bar_empty[NSTAGE];
   uint64_t bar_s_full[NSLOT];
+  uint64_t bar_s_free[NSLOT];
   uint64_t bar_p_full[NSLOT];
   uint64_t bar_o_done[NSLOT];
   uint64_t bar_o_free[NSLOT];
-  uint64_t bar_final;
+  uint64_t bar_mufu[NSLOT];  // exponential phases alternate between the slots
+  uint64_t bar_final[NSLOT];
   uint32_t tmem_base;
   int abort;
 };
@@ -152,14 +160,18 @@ __device__ __forceinline__ void issue_s(uint32_t d_tmem, uint32_t q_smem, uint32
   }
 }
 
-// O (+)= P V: P (bf16 pairs) from TMEM, V MN-major in smem; K step = 16 rows.
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_smem,
+// O (+)= P V: P K-major in smem (the layout of Q), V MN-major in smem;
+// K step = 16 KV rows.
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_smem, uint32_t v_smem,
                                          bool acc) {
+  const uint64_t a = sdesc_sw128(p_smem, 16, 1024);
   const uint64_t b = sdesc_sw128(v_smem, SUB_BYTES, 1024);
 #pragma unroll
-  for (int kk = 0; kk < BN / 16; ++kk)
-    umma_bf16_ts(d_tmem, p_tmem + kk * 8, b + uint64_t((kk * 2048) >> 4), kIdescO,
+  for (int kk = 0; kk < BN / 16; ++kk) {
+    const uint64_t a_off = uint64_t(((kk >> 2) * SUB_BYTES + (kk & 3) * 32) >> 4);
+    umma_bf16_ss(d_tmem, a + a_off, b + uint64_t((kk * 2048) >> 4), kIdescO,
                  (acc || kk > 0) ? 1u : 0u);
+  }
 }
 
 __device__ __forceinline__ void slot_barrier(int s) {
@@ -177,19 +189,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int per_tile = p.hkv * p.pairs;
 
   if (threadIdx.x == 0) {
+    // Q and every K/V stage are released by both MMA issuers (one per slot;
+    // the slot-0 issuer releases twice when slot 1 has no head in a piece)
     mbar_init(&sm.bar_q, 1);
-    mbar_init(&sm.bar_q_free, 1);
+    mbar_init(&sm.bar_q_free, NSLOT);
     for (int i = 0; i < NSTAGE; ++i) {
       mbar_init(&sm.bar_full[i], 1);
-      mbar_init(&sm.bar_empty[i], 1);
+      mbar_init(&sm.bar_empty[i], NSLOT);
     }
     for (int i = 0; i < NSLOT; ++i) {
       mbar_init(&sm.bar_s_full[i], 1);
+      mbar_init(&sm.bar_s_free[i], 128);
       mbar_init(&sm.bar_p_full[i], 128);
       mbar_init(&sm.bar_o_done[i], 1);
       mbar_init(&sm.bar_o_free[i], 128);
+      mbar_init(&sm.bar_mufu[i], 128);
     }
-    mbar_init(&sm.bar_final, 1);
+    for (int i = 0; i < NSLOT; ++i) mbar_init(&sm.bar_final[i], 1);
     sm.abort = 0;
     fence_barrier_init();
   }
@@ -271,21 +287,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_3d(sm.q[s] + d * SUB_BYTES, &tm_q, &sm.bar_q, d * 64, pc.qt * BM, pc.h0 + s);
         ++pieces;
         const uint32_t* list = p.blk_list + size_t(pc.qt) * p.n_kv128;
-        for (int j = pc.b0; j < pc.b1 && ok; ++j) {
+        // consumption order of the MMA thread: K_b0, then per block j
+        // K_{j+1} (if any) before V_j
+        const int n_loads = 2 * (pc.b1 - pc.b0);
+        for (int i = 0; i < n_loads && ok; ++i) {
+          const bool is_v = i > 0 && (i == n_loads - 1 || (i & 1) == 0);
+          const int j = pc.b0 + (i == 0 ? 0 : (is_v ? (i - 1) / 2 : (i + 1) / 2));
           const int kb = int(list[j] & 0xFFFFFFu);
-          for (int which = 0; which < 2 && ok; ++which) {
-            ok = mbar_wait(&sm.bar_empty[stage], phase ^ 1u, abort, p.status, 0x100 + which);
-            if (!ok) break;
-            mbar_arrive_expect_tx(&sm.bar_full[stage], TILE_BYTES);
-            const CUtensorMap* tm = which ? &tm_v : &tm_k;
-            for (int d = 0; d < 2; ++d)
-              tma_load_3d(sm.kv[stage] + d * SUB_BYTES, tm, &sm.bar_full[stage], d * 64,
-                          kb * BN, pc.kvh);
-            ++issued;
-            if (++stage == NSTAGE) {
-              stage = 0;
-              phase ^= 1u;
-            }
+          ok = mbar_wait(&sm.bar_empty[stage], phase ^ 1u, abort, p.status, 0x100 + int(is_v));
+          if (!ok) break;
+          mbar_arrive_expect_tx(&sm.bar_full[stage], TILE_BYTES);
+          const CUtensorMap* tm = is_v ? &tm_v : &tm_k;
+          for (int d = 0; d < 2; ++d)
+            tma_load_3d(sm.kv[stage] + d * SUB_BYTES, tm, &sm.bar_full[stage], d * 64, kb * BN,
+                        pc.kvh);
+          ++issued;
+          if (++stage == NSTAGE) {
+            stage = 0;
+            phase ^= 1u;
           }
         }
       }
@@ -299,83 +318,89 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (pieces > 0)
         mbar_wait(&sm.bar_q, uint32_t(pieces - 1) & 1u, abort, p.status, 0x120, false);
-    } else if (warp == 9 && lane == 0) {
-      // ---------------------------------------------------------- MMA issuer
-      const uint32_t qa0 = smem_u32(sm.q[0]);
+    } else if ((warp == 9 || warp == 11) && lane == 0) {
+      // ---------------------------------------------------------- MMA issuers
+      // One thread per slot (warp 9: slot 0, warp 11: slot 1), so each slot's
+      // MMAs follow its own softmax.  tcgen05.commit tracks the MMAs of the
+      // committing thread only; K/V stages and Q are released by both.
+      const int s = warp == 9 ? 0 : 1;
+      const uint32_t qa = smem_u32(sm.q[s]);
+      const uint32_t pa = smem_u32(sm.pb[s]);
       const uint32_t kv0 = smem_u32(sm.kv[0]);
+      const uint32_t t_sl = tmem + s * 256;
       int stage = 0;
       uint32_t phase = 0;
-      int gs[NSLOT] = {0, 0};  // blocks done per slot (barrier parity)
-      int ps[NSLOT] = {0, 0};  // pieces done per slot
+      int ns = 0;  // S issued (s_free parity)
+      int gs = 0;  // PV issued (p_full parity)
+      int ps = 0;  // pieces done (o_free parity)
       int pieces = 0;
       bool ok = true;
       bool issued_any = false;
       int w = w0;
       Piece pc;
       while (ok && next_piece(p, w, w1, pc)) {
-        ok = mbar_wait(&sm.bar_q, uint32_t(pieces) & 1u, abort, p.status, 0x200);
-        if (!ok) break;
-        tc_fence_after();
-        // prologue: S_s(b0)
-        const int k0 = stage;
-        ok = mbar_wait(&sm.bar_full[k0], phase, abort, p.status, 0x201);
-        if (!ok) break;
-        tc_fence_after();
-        for (int s = 0; s < pc.nslot; ++s) {
-          issue_s(tmem + s * 256, qa0 + s * TILE_BYTES, kv0 + k0 * TILE_BYTES);
-          umma_commit(&sm.bar_s_full[s]);
+        const int n_loads = 2 * (pc.b1 - pc.b0);
+        if (s >= pc.nslot) {  // no head of this piece in slot 1: skip its FIFO entries
+          for (int i = 0; i < n_loads; ++i)
+            if (++stage == NSTAGE) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          ++pieces;
+          continue;
         }
-        umma_commit(&sm.bar_empty[k0]);
-        issued_any = true;
-        if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
-        for (int j = pc.b0; j < pc.b1 && ok; ++j) {
-          const int vstage = stage;
-          const uint32_t vphase = phase;
-          if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
-          const bool more = j + 1 < pc.b1;
-          const int nk = stage;
-          const uint32_t nkph = phase;
-          if (more) {
-            if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
-          }
-          ok = mbar_wait(&sm.bar_full[vstage], vphase, abort, p.status, 0x202);
+        const int rel = pc.nslot == NSLOT ? 1 : NSLOT;  // releases owed per stage
+        ok = mbar_wait(&sm.bar_q, uint32_t(pieces) & 1u, abort, p.status, 0x200 + s);
+        if (!ok) break;
+        tc_fence_after();
+        for (int i = 0; i < n_loads && ok; ++i) {
+          // FIFO entry i of the piece: K_b0, then per block j K_{j+1}, V_j
+          const bool is_v = i > 0 && (i == n_loads - 1 || (i & 1) == 0);
+          const int j = pc.b0 + (i == 0 ? 0 : (is_v ? (i - 1) / 2 : (i + 1) / 2));
+          const int st = stage;
+          ok = mbar_wait(&sm.bar_full[st], phase, abort, p.status, 0x202 + s);
           if (!ok) break;
-          for (int s = 0; s < pc.nslot && ok; ++s) {
-            ok = mbar_wait(&sm.bar_p_full[s], uint32_t(gs[s]) & 1u, abort, p.status, 0x205);
-            if (!ok) break;
-            if (j == pc.b0 && ps[s] > 0) {
-              // the softmax has read O of this slot's previous piece
-              ok = mbar_wait(&sm.bar_o_free[s], uint32_t(ps[s] - 1) & 1u, abort, p.status,
-                             0x207);
+          if (++stage == NSTAGE) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          if (!is_v) {
+            // S(j) once the softmax has read S(j-1) of this slot
+            if (ns > 0) {
+              ok = mbar_wait(&sm.bar_s_free[s], uint32_t(ns - 1) & 1u, abort, p.status,
+                             0x204 + s);
               if (!ok) break;
             }
             tc_fence_after();
-            issue_pv(tmem + s * 256 + 128, tmem + s * 256, kv0 + vstage * TILE_BYTES, j > pc.b0);
-            umma_commit(&sm.bar_o_done[s]);
-            ++gs[s];
-            if (more) {
-              if (s == 0) {
-                ok = mbar_wait(&sm.bar_full[nk], nkph, abort, p.status, 0x203);
-                if (!ok) break;
-                tc_fence_after();
-              }
-              issue_s(tmem + s * 256, qa0 + s * TILE_BYTES, kv0 + nk * TILE_BYTES);
-              umma_commit(&sm.bar_s_full[s]);
+            issue_s(t_sl, qa, kv0 + st * TILE_BYTES);
+            umma_commit(&sm.bar_s_full[s]);
+            ++ns;
+          } else {
+            ok = mbar_wait(&sm.bar_p_full[s], uint32_t(gs) & 1u, abort, p.status, 0x206 + s);
+            if (!ok) break;
+            if (j == pc.b0 && ps > 0) {
+              // the softmax has read O of this slot's previous piece
+              ok = mbar_wait(&sm.bar_o_free[s], uint32_t(ps - 1) & 1u, abort, p.status,
+                             0x208 + s);
+              if (!ok) break;
             }
+            tc_fence_after();
+            issue_pv(t_sl + 128, pa, kv0 + st * TILE_BYTES, j > pc.b0);
+            umma_commit(&sm.bar_o_done[s]);
+            ++gs;
           }
-          if (!ok) break;
-          umma_commit(&sm.bar_empty[vstage]);
-          if (more) umma_commit(&sm.bar_empty[nk]);
+          issued_any = true;
+          for (int k = 0; k < rel; ++k) umma_commit(&sm.bar_empty[st]);
         }
         if (!ok) break;
-        umma_commit(&sm.bar_q_free);  // every S of this piece has been issued
-        for (int s = 0; s < pc.nslot; ++s) ++ps[s];
+        for (int k = 0; k < rel; ++k) umma_commit(&sm.bar_q_free);  // every S issued
+        ++ps;
         ++pieces;
       }
-      // every MMA this thread issued has completed once bar_final fires
+      // every MMA this thread issued has completed once its bar_final fires
       if (issued_any) {
-        umma_commit(&sm.bar_final);
-        mbar_wait(&sm.bar_final, 0, abort, p.status, 0x206, false);
+        umma_commit(&sm.bar_final[s]);
+        mbar_wait(&sm.bar_final[s], 0, abort, p.status, 0x20a + s, false);
       }
     }
   } else {
@@ -388,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t t_s = tmem + lane_off + s * 256;
     const uint32_t t_o = t_s + 128;
     int gs = 0;  // blocks this slot has processed (barrier parity)
+    int hs = 0;  // blocks with both slots active (exponential-phase handshakes)
     bool ok = true;
     int w = w0;
     Piece pc;
@@ -424,6 +450,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld(u[1]);
         tmem_wait_ld(u[2]);
         tmem_wait_ld(u[3]);
+        // S is in registers: the MMA thread may overwrite the S columns
+        tc_fence_before();
+        mbar_arrive(&sm.bar_s_free[s]);
         float x[128];
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -449,9 +478,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float alpha = need ? ex2_approx(m - m_new) : 1.f;
         if (need) m = m_new;
         const float nm = ((m == -INFINITY) ? 0.f : -m) + kPackBiasLog2;
-        // O holds sum_{i<j} P_i V_i of this piece (PV(j-1) completed before
-        // S(j)); rescale it when this block raised the max.
+        // O holds sum_{i<j} P_i V_i of this piece once PV(j-1) completes;
+        // rescale it when this block raised the max.  PV of the previous block
+        // must also be done before P is overwritten below.
+        bool pv_done = gs == 0;
         if (j > pc.b0 && __any_sync(0xffffffffu, need)) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&sm.bar_o_done[s], uint32_t(gs - 1) & 1u, abort,
+                                                 p.status, 0x310 + s));
+          if (!ok) break;
+          pv_done = true;
+          tc_fence_after();
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             uint32_t o[16];
@@ -470,24 +506,51 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st16(t_o + c * 16, o);
           }
         }
-        // P = exp2(s * scale - m) -> bf16 pairs -> TMEM columns [0, 64) of S
-        // (scale, subtract) and the row sums run on packed fp32 pairs
+        if (!pv_done) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&sm.bar_o_done[s], uint32_t(gs - 1) & 1u, abort,
+                                                 p.status, 0x312 + s));
+          if (!ok) break;
+        }
+        // When both slots are active their exponential phases take turns on
+        // the MUFU (slot 0 first): each slot's max / load / wait phases then
+        // run under the other slot's exponentials instead of in lockstep.
+        const bool pingpong = pc.nslot == 2;
+        if (pingpong && (s == 1 || hs > 0)) {
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(&sm.bar_mufu[s], uint32_t(s == 0 ? hs - 1 : hs) & 1u, abort,
+                                    p.status, 0x314 + s));
+          if (!ok) break;
+        }
+        // P = exp2(s * scale - m) -> bf16 pairs -> row r of the slot's P tile
+        // (two 64-column sub-tiles, 128-byte rows, 16-byte chunk c stored at
+        // chunk c ^ (r & 7): the TMA / MMA 128-byte swizzle).  The scale,
+        // subtract and row sums run on packed fp32 pairs.
         const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
         const uint64_t nm2 = f2_pack(nm, nm);
         uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+        const uint32_t prow = smem_u32(sm.pb[s]) + uint32_t(r) * 128u;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          uint32_t pk[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float xa, xb;
-            f2_unpack(f2_fma(f2_pack(x[64 * c + 2 * i], x[64 * c + 2 * i + 1]), sc2, nm2), xa, xb);
-            const float a = ex2_approx(xa);
-            const float b = ex2_approx(xb);
-            sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(a, b));
-            pk[i] = pack_bf16x2_trunc(a, b);
+          for (int ch = 0; ch < 8; ++ch) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int col = 64 * c + 8 * ch + 2 * i;
+              float xa, xb;
+              f2_unpack(f2_fma(f2_pack(x[col], x[col + 1]), sc2, nm2), xa, xb);
+              const float a = ex2_approx(xa);
+              const float b = ex2_approx(xb);
+              sum2[i] = f2_add(sum2[i], f2_pack(a, b));
+              pk[i] = pack_bf16x2_trunc(a, b);
+            }
+            st_shared_v4(prow + uint32_t(c * SUB_BYTES) + (uint32_t(ch ^ (r & 7)) << 4), pk[0],
+                         pk[1], pk[2], pk[3]);
           }
-          tmem_st32(t_s + c * 32, pk);
+        }
+        if (pingpong) {
+          mbar_arrive(&sm.bar_mufu[s ^ 1]);
+          ++hs;
         }
         float s0, s1, s2, s3, s4, s5, s6, s7;
         f2_unpack(sum2[0], s0, s1);
@@ -495,8 +558,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         f2_unpack(sum2[2], s4, s5);
         f2_unpack(sum2[3], s6, s7);
         l = l * alpha + (((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7))) * kPackBiasInv;
-        tmem_wait_st();
+        tmem_wait_st();  // O rescale stores, if any
         tc_fence_before();
+        fence_async_shared();  // P stores -> visible to the MMA (async proxy)
         mbar_arrive(&sm.bar_p_full[s]);
         ++gs;
       }
