@@ -25,12 +25,13 @@ _workspaces = {}
 
 
 class AttentionWorkspace:
-    """Device scratch of the load-balanced schedule (one per device): fp32
-    partial rows of the items an SM's share of the work leaves unfinished,
-    merged by the second kernel of the same call."""
+    """Device scratch of the load-balanced schedule (one per device): the
+    partial rows of items cut between two SMs' shares of the work, their
+    ready flags and a launch generation.  Zero-filled once here; every call
+    leaves it ready for the next (calls sharing it must not overlap)."""
 
     def __init__(self, nbytes, device):
-        self.buf = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
+        self.buf = torch.zeros(nbytes + 256, dtype=torch.uint8, device=device)
         self.base = (self.buf.data_ptr() + 255) & ~255
         self.nbytes = nbytes
 

@@ -326,6 +326,43 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
+// ---------------------------------------------------------------- flags
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait until *flag == value (another CTA of the same launch sets it
+// with st_release_u32).  Gives up like mbar_wait: on abort, on another error
+// in status after kSlowCheckNs, or after kWaitLimitNs (HSD_DEV_TIMEOUT | where).
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t value,
+                                          volatile int* abort, int32_t* status, int32_t where) {
+  if (ld_acquire_u32(flag) == value) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (ld_acquire_u32(flag) == value) return true;
+    if (*abort) return false;
+    const uint64_t dt = globaltimer_ns() - t0;
+    if (dt < kSlowCheckNs) continue;
+    if (status && *reinterpret_cast<volatile int32_t*>(status) != 0) {
+      *abort = 1;
+      return false;
+    }
+    if (dt > kWaitLimitNs) {
+      report(status, HSD_DEV_TIMEOUT | where);
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
 }  // namespace hsd
 
 // Host-side helpers shared by the .cu files of the library.

@@ -13,10 +13,9 @@
 //   warp 8      TMA producer: Q per piece, then K and V tiles into a 3-stage
 //               FIFO in the order the MMAs consume them: K_b0, then per block
 //               j: K_{j+1}, V_j
-//   warp 9      MMA issuer (one thread), tcgen05 with both operands in smem:
-//               S = Q K^T and O += P V
-//   warp 10     writes the stream-K merge descriptor; warp 11 idle (the
-//               third warpgroup is whole for setmaxnreg)
+//   warps 9, 11 MMA issuers (one thread each), slot 0 and slot 1: tcgen05
+//               with both operands in smem, S = Q K^T and O += P V
+//   warp 10     idle (the third warpgroup is whole for setmaxnreg)
 //   warps 0-3   softmax + epilogue of head slot 0 (thread = query row)
 //   warps 4-7   softmax + epilogue of head slot 1
 //
@@ -31,6 +30,16 @@
 // P_s it waits for the previous PV (o_done).  Softmax keeps a running max in
 // log2 units and rescales O only when the max grows by more than
 // kRescaleLog2 (exact: the final O / l and LSE use the same stale max).
+//
+// Stream-K: with a workspace, one CTA per SM takes an equal share of the
+// cost-ordered work, so (query tile, head pair) items get cut between
+// consecutive CTAs.  The CTA holding an item's first blocks (its last piece,
+// finished at the end of its range) owns the item: the later pieces sit at
+// the start of the following CTAs' ranges, finished early, and each publishes
+// its normalised rows with one flag per (CTA, slot, warp).  The owner merges
+// them into its own O in the epilogue; no second kernel.  Flags hold the
+// launch generation + 1 (the generation lives in the workspace and the last
+// CTA to exit advances it), so they never need clearing.
 #include "common.cuh"
 
 namespace hsd {
@@ -55,10 +64,10 @@ constexpr float kPackBiasLog2 = 0.0040626743f;   // log2(1.00282)
 constexpr float kPackBiasInv = 0.99718800f;      // 1 / 1.00282
 
 constexpr int kMaxTiles = 1024;  // query tiles per launch (q_len <= 131072)
-// Partial record of one (CTA, piece kind, slot): the piece's normalised
-// O / l in bf16 as [16 chunks][128 rows] of 16-byte vectors (a warp reads or
-// writes 512 contiguous bytes per access), then (m, l) per row in fp32.
-// Units of 4 bytes.
+// Partial record of one (CTA, slot): the normalised O / l in bf16 of the
+// CTA's first piece when that piece continues an item begun by an earlier CTA,
+// as [16 chunks][128 rows] of 16-byte vectors (a warp reads or writes 512
+// contiguous bytes per access), then (m, l) per row in fp32.  Units of 4 bytes.
 constexpr int kRecWords = 128 * 64 + 128 * 2;
 
 struct __align__(1024) Smem {
@@ -93,8 +102,9 @@ struct Params {
   const int32_t* tile_order;
   const int32_t* blk_prefix;  // [n_qtiles + 1] blocks before each ordered tile
   int32_t* status;
-  uint32_t* partials;  // stream-K partial records [G][2][NSLOT][kRecWords], or null
-  int32_t* combine_desc;  // [G][4] per range boundary: owner item (see combine_kernel)
+  uint32_t* partials;  // stream-K partial records [G][NSLOT][kRecWords], or null
+  uint32_t* flags;     // [G][NSLOT][4]: record rows of warp w published (= generation + 1)
+  uint32_t* sync;      // {generation, CTAs finished}: the last CTA to exit bumps the generation
   int q_len, kv_len, hq, hkv, group, pairs;
   int n_qtiles, n_kv64, n_kv128;
   float scale_log2;
@@ -220,6 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = &sm.abort;
   const int total = p.blk_prefix[p.n_qtiles] * per_tile;
   const int G = gridDim.x;
+  const uint32_t gen = p.split ? __ldcg(p.sync) : 0u;  // launch generation (stream-K flags)
   int w0, w1;
   if (p.split) {
     w0 = range_start(blockIdx.x, total, G);
@@ -238,33 +249,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // branch of its own setmaxnreg.
   if (warp >= 8) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 120;\n" ::: "memory");
-    if (warp == 10 && lane == 0 && p.split) {
-      // Combine descriptor of the boundary at the start of this CTA's range:
-      // {owner, first query row, first head of the pair, last CTA holding a
-      // piece}.  Boundary b owns item X when b's start lies strictly inside X
-      // and b-1's start does not; X's pieces are then CTA b-1's last piece and
-      // the first pieces of the non-empty ranges b..khi.
-      int32_t* d = p.combine_desc + 4 * blockIdx.x;
-      int owner = 0, q0 = 0, hfirst = 0, khi = 0;
-      if (blockIdx.x > 0 && w0 < total) {
-        int w = w0;
-        Piece pc;
-        next_piece(p, w, total, pc);
-        const int ib = pc.start + pc.nblk - 1;
-        if (pc.start < w0 && range_start(blockIdx.x - 1, total, G) <= pc.start) {
-          owner = 1;
-          q0 = pc.qt * BM;
-          hfirst = pc.h0;
-          khi = blockIdx.x;
-          while (khi + 1 < G && range_start(khi + 1, total, G) <= ib) ++khi;
-          owner = pc.nslot;  // number of slots to combine (1 or 2)
-        }
-      }
-      d[0] = owner;
-      d[1] = q0;
-      d[2] = hfirst;
-      d[3] = khi;
-    }
     if (warp == 8 && lane == 0) {
       // ---------------------------------------------------------- producer
       tma_prefetch_desc(&tm_q);
@@ -587,11 +571,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&sm.bar_o_free[s]);
       const bool whole = pc.b0 == 0 && pc.b1 == pc.nblk;
-      if (!whole) {
-        // stream-K partial: O / l in bf16 with its (m, l); combine_kernel
-        // merges the pieces of every split item after this launch.
-        const int kind = (pc.start < w0) ? 0 : 1;
-        uint32_t* rec = p.partials + ((size_t(blockIdx.x) * 2 + kind) * NSLOT + s) * kRecWords;
+      if (!whole && pc.start < w0) {
+        // a later piece of an item begun by an earlier CTA (this CTA's first
+        // piece): publish O / l in bf16 with its (m, l) for the item's owner;
+        // one flag per warp covers the warp's 32 rows.
+        uint32_t* rec = p.partials + (size_t(blockIdx.x) * NSLOT + s) * kRecWords;
         const float invl = (l > 0.f) ? 1.f / l : 0.f;
         int4* rec4 = reinterpret_cast<int4*>(rec);
 #pragma unroll
@@ -601,7 +585,46 @@ __global__ void __launch_bounds__(kThreads, 1)
                                         int(pack_bf16x2(o[8 * c + 4] * invl, o[8 * c + 5] * invl)),
                                         int(pack_bf16x2(o[8 * c + 6] * invl, o[8 * c + 7] * invl)));
         reinterpret_cast<float2*>(rec + 128 * 64)[r] = make_float2(m, l);
+        __threadfence();
+        __syncwarp();
+        if (lane == 0)
+          st_release_u32(p.flags + (size_t(blockIdx.x) * NSLOT + s) * 4 + quarter, gen + 1u);
         continue;
+      }
+      if (!whole) {
+        // this piece holds the item's first blocks: merge the later pieces,
+        // the first pieces of the non-empty ranges blockIdx.x+1 .. khi
+        const int ib = pc.start + pc.nblk - 1;  // the item's last work unit
+        int khi = blockIdx.x;
+        while (khi + 1 < G && range_start(khi + 1, total, G) <= ib) ++khi;
+        for (int k = blockIdx.x + 1; k <= khi && ok; ++k) {
+          if (range_start(k + 1, total, G) == range_start(k, total, G)) continue;  // empty
+          const uint32_t* rec = p.partials + (size_t(k) * NSLOT + s) * kRecWords;
+          ok = wait_flag(p.flags + (size_t(k) * NSLOT + s) * 4 + quarter, gen + 1u, abort,
+                         p.status, 0x330 + s);
+          if (!ok) break;
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec + 128 * 64) + r);
+          if (ml.y > 0.f) {
+            const float nm = fmaxf(m, ml.x);
+            const float a = ex2_approx(m - nm);  // 0 when this row had nothing yet (m = -inf)
+            const float b = ex2_approx(ml.x - nm) * ml.y;
+            const int4* rec4 = reinterpret_cast<const int4*>(rec);
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              const int4 v = __ldcg(rec4 + c * 128 + r);
+              const uint32_t wv[4] = {uint32_t(v.x), uint32_t(v.y), uint32_t(v.z), uint32_t(v.w)};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                o[8 * c + 2 * i] = o[8 * c + 2 * i] * a + __uint_as_float(wv[i] << 16) * b;
+                o[8 * c + 2 * i + 1] =
+                    o[8 * c + 2 * i + 1] * a + __uint_as_float(wv[i] & 0xffff0000u) * b;
+              }
+            }
+            l = l * a + b;
+            m = nm;
+          }
+        }
+        if (!ok) break;
       }
       // ---- final output of the item
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
@@ -637,99 +660,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (p.split && threadIdx.x == 0) {
+    // the last CTA to finish advances the generation for the next launch
+    __threadfence();
+    if (atomicAdd(p.sync + 1, 1u) == uint32_t(G) - 1u) {
+      p.sync[1] = 0u;
+      __threadfence();
+      st_release_u32(p.sync, gen + 1u);
+    }
+  }
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
-}
-
-// Merge the pieces of every item the stream-K split cut: O = sum_k 2^(m_k-M)
-// O_k / sum_k 2^(m_k-M) l_k per row.  Block (boundary b, slot s): boundary b
-// owns item X when the start of CTA b's range lies strictly inside X and the
-// start of CTA b-1's range does not (the first boundary inside X).  Thread 0
-// resolves ownership and the list of pieces; then thread = (row, 32-column
-// chunk) and the pieces' loads are coalesced across rows.
-constexpr int kMaxCombinePieces = 64;
-
-__global__ void __launch_bounds__(512) combine_kernel(const Params p, int G) {
-  __shared__ int s_np, s_q0, s_h;
-  __shared__ const uint32_t* s_rec[kMaxCombinePieces];
-  const int b = 1 + blockIdx.x / NSLOT;
-  const int s = blockIdx.x % NSLOT;
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // descriptors and partials
-  if (threadIdx.x == 0) {
-    s_np = 0;
-    const int4 d = __ldcg(reinterpret_cast<const int4*>(p.combine_desc) + b);
-    if (d.x > s) {  // owner boundary and the pair uses this slot
-      const int per_tile = p.hkv * p.pairs;
-      const int total = p.blk_prefix[p.n_qtiles] * per_tile;
-      const bool dense = total >= G;  // every range non-empty
-      int np = 0;
-      s_rec[np++] = p.partials + ((size_t(b - 1) * 2 + 1) * NSLOT + s) * kRecWords;
-      for (int k = b; k <= d.w; ++k) {
-        if (!dense && range_start(k + 1, total, G) == range_start(k, total, G)) continue;
-        if (np >= kMaxCombinePieces) {
-          report(p.status, HSD_DEV_CAPACITY | 0x331);
-          break;
-        }
-        s_rec[np++] = p.partials + ((size_t(k) * 2 + 0) * NSLOT + s) * kRecWords;
-      }
-      s_np = np;
-      s_q0 = d.y;
-      s_h = d.z + s;
-    }
-  }
-  __syncthreads();
-  const int np = s_np;
-  if (np == 0) return;
-  const int r = threadIdx.x & 127, ch = threadIdx.x >> 7;  // row, 32-column chunk
-  float M = -INFINITY, L = 0.f;
-  for (int i = 0; i < np; ++i) {
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(s_rec[i] + 128 * 64) + r);
-    if (ml.x > M) {
-      L = (M == -INFINITY ? 0.f : L * ex2_approx(M - ml.x)) + ml.y;
-      M = ml.x;
-    } else if (ml.x != -INFINITY) {
-      L += ml.y * ex2_approx(ml.x - M);
-    }
-  }
-  float acc[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-  for (int i = 0; i < np; ++i) {
-    const uint32_t* rk = s_rec[i];
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(rk + 128 * 64) + r);
-    // weight of the piece's normalised O: 2^(m_k - M) l_k
-    const float wk = (M == -INFINITY || ml.x == -INFINITY) ? 0.f : ex2_approx(ml.x - M) * ml.y;
-    const int4* r4 = reinterpret_cast<const int4*>(rk);
-    int4 v[4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) v[c] = __ldcg(r4 + (ch * 4 + c) * 128 + r);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint32_t w[4] = {uint32_t(v[c].x), uint32_t(v[c].y), uint32_t(v[c].z), uint32_t(v[c].w)};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        acc[8 * c + 2 * e] += wk * __uint_as_float(w[e] << 16);
-        acc[8 * c + 2 * e + 1] += wk * __uint_as_float(w[e] & 0xFFFF0000u);
-      }
-    }
-  }
-  const int q = s_q0 + r;
-  const int h = s_h;
-  if (q >= p.q_len) return;
-  const float inv = (L > 0.f) ? 1.f / L : 0.f;
-  int4* dst = reinterpret_cast<int4*>(p.out + (size_t(q) * p.hq + h) * HD + ch * 32);
-#pragma unroll
-  for (int v = 0; v < 4; ++v)
-    dst[v] = make_int4(int(pack_bf16x2(acc[8 * v] * inv, acc[8 * v + 1] * inv)),
-                       int(pack_bf16x2(acc[8 * v + 2] * inv, acc[8 * v + 3] * inv)),
-                       int(pack_bf16x2(acc[8 * v + 4] * inv, acc[8 * v + 5] * inv)),
-                       int(pack_bf16x2(acc[8 * v + 6] * inv, acc[8 * v + 7] * inv)));
-  if (ch == 0 && p.lse)
-    p.lse[size_t(h) * p.q_len + q] =
-        (L > 0.f) ? (M + __log2f(L)) * 0.69314718055994530942f : -INFINITY;
 }
 
 }  // namespace attn
@@ -796,8 +740,10 @@ int sm_count() {
   return n;
 }
 
+// Stream-K workspace: partial records [G][NSLOT][kRecWords], flags
+// [G][NSLOT][4], then {generation, CTAs finished}.  G = SMs of the device.
 struct WsLayout {
-  size_t partials, desc, total;
+  size_t partials, flags, sync, total;
   int items, grid;
 };
 
@@ -808,10 +754,14 @@ WsLayout ws_layout(int32_t q_len, int32_t hq, int32_t hkv) {
   L.items = n_qtiles * hkv * pairs;
   L.grid = sm_count();
   L.partials = 0;
-  L.desc = size_t(L.grid) * 2 * attn::NSLOT * attn::kRecWords * sizeof(uint32_t);
-  L.total = L.desc + size_t(L.grid) * 4 * sizeof(int32_t);
+  L.flags = size_t(L.grid) * attn::NSLOT * attn::kRecWords * sizeof(uint32_t);
+  L.sync = L.flags + size_t(L.grid) * attn::NSLOT * 4 * sizeof(uint32_t);
+  L.total = L.sync + 256;
   return L;
 }
+
+constexpr int kMaxDevices = 64;
+bool g_attr_set[kMaxDevices] = {};
 
 }  // namespace
 
@@ -882,40 +832,30 @@ extern "C" int hsd_verify_attention(const void* q, int64_t q_row_stride, int64_t
   p.n_kv128 = plan->n_kv128;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.split = split ? 1 : 0;
-  p.partials = split ? reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + W.partials)
-                     : nullptr;
-  p.combine_desc =
-      split ? reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + W.desc) : nullptr;
+  char* ws = static_cast<char*>(workspace);
+  p.partials = split ? reinterpret_cast<uint32_t*>(ws + W.partials) : nullptr;
+  p.flags = split ? reinterpret_cast<uint32_t*>(ws + W.flags) : nullptr;
+  p.sync = split ? reinterpret_cast<uint32_t*>(ws + W.sync) : nullptr;
   const size_t smem = sizeof(attn::Smem) + 1024;
-  static bool attr_set = false;
-  if (!attr_set) {
+  int dev = 0;
+  rc = hsd_host::cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= kMaxDevices) {
+    hsd_host::set_error("hsd_verify_attention: device ordinal %d >= %d", dev, kMaxDevices);
+    return HSD_ERR_UNSUPPORTED;
+  }
+  if (!g_attr_set[dev]) {
     rc = hsd_host::cuda_check(
         cudaFuncSetAttribute(attn::verify_attn_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
         "cudaFuncSetAttribute(verify_attn_kernel)");
     if (rc) return rc;
-    attr_set = true;
+    g_attr_set[dev] = true;
   }
   // stream-K: one CTA per SM sharing the total work evenly; otherwise one CTA
   // per (query tile, head pair) item.
   const int grid = split ? W.grid : W.items;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   attn::verify_attn_kernel<<<grid, attn::kThreads, smem, st>>>(tq, tk, tv, p);
-  rc = hsd_host::cuda_check(cudaGetLastError(), "verify_attn_kernel launch");
-  if (rc || !split || W.grid < 2) return rc;
-  // programmatic dependent launch: the combine grid starts its item lookup
-  // while the attention grid drains and waits (griddepcontrol.wait) for its
-  // partials
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned((W.grid - 1) * attn::NSLOT));
-  cfg.blockDim = dim3(512);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return hsd_host::cuda_check(cudaLaunchKernelEx(&cfg, attn::combine_kernel, p, W.grid),
-                              "combine_kernel launch");
+  return hsd_host::cuda_check(cudaGetLastError(), "verify_attn_kernel launch");
 }
