@@ -327,27 +327,57 @@ __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
 // ---------------------------------------------------------------- flags
-__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
+// Orders this thread's generic-proxy view of global memory before its later
+// async-proxy (bulk copy) reads of it.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Untiled bulk copy global -> this CTA's shared memory, completion counted in
+// bytes on `bar` (16-byte aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst_smem)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t (&v)[4]) {
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+               : "r"(addr)
+               : "memory");
+}
+
 // Bounded wait until *flag == value (another CTA of the same launch sets it
-// with st_release_u32).  Gives up like mbar_wait: on abort, on another error
-// in status after kSlowCheckNs, or after kWaitLimitNs (HSD_DEV_TIMEOUT | where).
+// with st_release_u32), polling with relaxed loads: the caller issues
+// fence_acq_rel_gpu() after its last flag before reading the flagged data.
+// Gives up like mbar_wait: on abort, on another error in status after
+// kSlowCheckNs, or after kWaitLimitNs (HSD_DEV_TIMEOUT | where).
 __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t value,
                                           volatile int* abort, int32_t* status, int32_t where) {
-  if (ld_acquire_u32(flag) == value) return true;
+  if (ld_relaxed_u32(flag) == value) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
-      if (ld_acquire_u32(flag) == value) return true;
+      if (ld_relaxed_u32(flag) == value) return true;
     if (*abort) return false;
     const uint64_t dt = globaltimer_ns() - t0;
     if (dt < kSlowCheckNs) continue;

@@ -110,14 +110,6 @@ constexpr int kBulkThreads = 256;
 constexpr int kBulkBuf = 96 * 1024;  // bytes per staging buffer (two buffers)
 constexpr int kBulkSmem = 2 * kBulkBuf + kIdxCache * 4 + 64;
 
-__device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint32_t bytes,
-                                          uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      ::"r"(smem_u32(dst_smem)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes),
-      "r"(smem_u32(bar))
-      : "memory");
-}
 
 __device__ __forceinline__ void bulk_store(void* dst, const void* src_smem, uint32_t bytes) {
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"

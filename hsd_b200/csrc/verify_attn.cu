@@ -603,6 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = wait_flag(p.flags + (size_t(k) * NSLOT + s) * 4 + quarter, gen + 1u, abort,
                          p.status, 0x330 + s);
           if (!ok) break;
+          fence_acq_rel_gpu();
           const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec + 128 * 64) + r);
           if (ml.y > 0.f) {
             const float nm = fmaxf(m, ml.x);
