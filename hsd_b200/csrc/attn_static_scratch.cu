@@ -14,14 +14,14 @@
 // Later calls only read the cached address.
 //
 // Limits: the scratch holds kStaticScratchBytes (20 MiB), enough for the
-// stream-K schedule on devices of up to 155 SMs (each SM's CTA needs
-// 2 x 2 x 33 KB of partial records plus a 16-byte descriptor).  A call whose
-// scratch need exceeds it returns HSD_ERR_TOO_LARGE and launches nothing.
-// Nothing in the scratch has to start at zero: every word the merge kernel
-// reads is written earlier in the same call.  There is one scratch per
-// device, so calls on one device must not overlap in time -- issue them on
-// one stream (or order them with events); two concurrent calls race on the
-// partial records and corrupt each other's output.
+// stream-K schedule on devices of up to 310 SMs (each SM's CTA needs a 33 KB
+// partial record per head slot and 32 bytes of flags).  A call whose scratch
+// need exceeds it returns HSD_ERR_TOO_LARGE and launches nothing.  The
+// scratch starts zero-filled (static storage), which its flags and launch
+// generation need, and every call leaves it ready for the next.  There is
+// one scratch per device, so calls on one device must not overlap in time --
+// issue them on one stream (or order them with events); two concurrent calls
+// race on the partial records and corrupt each other's output.
 #include <mutex>
 
 #include "common.cuh"

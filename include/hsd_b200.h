@@ -162,10 +162,10 @@ int hsd_build_plan_dense(const float *mask, int64_t row_stride, hsd_plan_t *plan
 
 /* ---- (1) packed verification attention ---------------------------------- */
 
-/* Device workspace of the load-balanced (stream-K) attention schedule: fp32
- * partial rows for the two pieces an SM's share of the work can leave
- * unfinished, for every SM of the current device.  Needs no initialisation;
- * its contents are scratch between the two kernels of one call. */
+/* Device workspace of the load-balanced (stream-K) attention schedule: per SM
+ * of the current device and head slot, the bf16 partial rows of the piece
+ * that continues an item begun by the previous SM, their ready flags, and a
+ * launch generation.  Zero-fill it before first use. */
 size_t hsd_attention_workspace_bytes(int32_t q_len, int32_t num_q_heads, int32_t num_kv_heads);
 
 /* out = softmax(q k^T * scale + mask) v per query head with grouped KV heads,
@@ -177,8 +177,11 @@ size_t hsd_attention_workspace_bytes(int32_t q_len, int32_t num_q_heads, int32_t
  * NULL.  Fully masked rows give 0 and -inf.  head_dim must be 128.
  * workspace (256-byte aligned, hsd_attention_workspace_bytes) enables the
  * stream-K schedule -- one CTA per SM, equal shares of the tile plan's work;
- * a second kernel merges the (query tile, head pair) items the shares cut,
- * through the workspace.  With workspace NULL each item gets its own CTA. */
+ * the CTA holding the first blocks of a (query tile, head pair) item that the
+ * shares cut merges the item's other pieces through the workspace.  The
+ * workspace must be zero-filled before its first use; each call leaves it
+ * ready for the next, and calls sharing one must not overlap in time.  With
+ * workspace NULL each item gets its own CTA. */
 int hsd_verify_attention(const void *q, int64_t q_row_stride, int64_t q_head_stride,
                          const void *k, int64_t k_row_stride, int64_t k_head_stride,
                          const void *v, int64_t v_row_stride, int64_t v_head_stride,
@@ -190,13 +193,13 @@ int hsd_verify_attention(const void *q, int64_t q_row_stride, int64_t q_head_str
 /* No counterpart in the reference (it allocates through PyTorch on every
  * call).  hsd_verify_attention with the stream-K scratch taken from a static
  * device array of hsd_attention_static_scratch_bytes() bytes (20 MiB, enough
- * for devices of up to 155 SMs) instead of a caller workspace, so the call
+ * for devices of up to 310 SMs) instead of a caller workspace, so the call
  * allocates nothing: for callers under a CUDA graph capture, or that must not
  * reach an allocator between serving steps.  The first call on each device
  * (that device current) looks up the array's address -- make it before any
  * stream capture.  A scratch need above the array's size returns
- * HSD_ERR_TOO_LARGE.  Nothing in the scratch needs to start at zero.  One
- * scratch per device: calls on one device must not overlap in time (one
+ * HSD_ERR_TOO_LARGE.  The array starts zero-filled (static storage) and each
+ * call leaves it ready for the next.  One scratch per device: calls on one device must not overlap in time (one
  * stream, or ordered by events), or they race on it.  Other arguments as
  * hsd_verify_attention. */
 size_t hsd_attention_static_scratch_bytes(void);

@@ -19,10 +19,11 @@ from hsd_b200 import _native as N
 def test_static_scratch_size_is_stated():
     lib = N.load()
     assert lib.hsd_attention_static_scratch_bytes() == 20 << 20
-    # one CTA per SM needs 2 x 2 partial records of 33 KB plus a 16-byte
-    # descriptor: 148 SMs fit, and so would 155
-    per_sm = 2 * 2 * (128 * 64 + 256) * 4 + 16
-    assert 155 * per_sm <= 20 << 20 < 156 * per_sm
+    # one CTA per SM needs a 33 KB partial record per head slot plus 32 bytes
+    # of flags, and the whole scratch 256 bytes of counters: 148 SMs fit, and
+    # so would 310
+    per_sm = 2 * (128 * 64 + 256) * 4 + 32
+    assert 310 * per_sm + 256 <= 20 << 20 < 311 * per_sm + 256
     assert lib.hsd_attention_workspace_bytes(1024, 12, 2) <= 20 << 20
 
 
