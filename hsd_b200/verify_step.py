@@ -119,9 +119,8 @@ class VerifyStep:
         self.period = period
         self._host = None
         self.attn_launches_per_step = L
-        # append 1 + plan 2 + attention L x (main + combine) + accept 1 + keep 1
-        # + compact 1 + bits 1
-        self.kernel_launches_per_step = 1 + 2 + 2 * L + 4
+        # append 1 + plan 2 + attention L + accept 1 + keep 1 + compact 1 + bits 1
+        self.kernel_launches_per_step = 1 + 2 + L + 4
 
     # ------------------------------------------------------------------
     def _ptr(self, t):
