@@ -1,0 +1,290 @@
+"""The verification loop of ``batch_generate`` on the device.
+
+Drives the reference's iteration (hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py
+D:923-1767) for region blocks with the kernels of this package:
+
+* the packed mask of a step is a :class:`~hsd_b200.plan.PackedMask` whose
+  per-block visibility rows stay in device memory: the acceptance kernel
+  writes each block's row of its last accepted token (the row the
+  reference's next mask inherits, D:1634-1667), and after compaction the
+  rows are remapped with the keep indices (D:1723);
+* acceptance, stop rules and KMP re-alignment run in one launch
+  (:func:`hsd_b200.accept.accept_kmp`); only the 8-int result rows of the
+  blocks come back to the host, which packs the next input (speculative
+  draft slice, or the next token) as D:1421-1567 does;
+* keep columns, the compaction rule and in-place compaction of the
+  registered KV planes (D:1679-1731).
+
+The target model stays outside: :meth:`VerifyLoop.inputs` gives the packed
+``input_ids`` / ``position_ids`` and the step's :class:`PackedMask` (its
+tile plan is what :func:`hsd_b200.attention.flex_attention_forward`
+consumes), and :meth:`VerifyLoop.step` takes the model's argmax per packed
+row.  Not driven by this loop: tree decoding (``enable_tree_decode``), tight
+packing (HSD_TIGHT_PACK) and the page block's tokenizer-driven parsers.
+"""
+from __future__ import annotations
+
+import math
+import time
+
+import numpy as np
+import torch
+
+from . import _native as N
+from .accept import DOTS_SENTINEL, F, R, accept_kmp, make_config
+from .compaction import compact_bits, compact_kv, keep_indices
+from .plan import SEG_CAUSAL, SEG_SINGLE, PackedMask, pack_bits
+
+
+class VerifyLoop:
+    """Region blocks verified in parallel, one :meth:`step` per forward.
+
+    ``prompts[b]`` is block b's prefill input (its own prompt: blocks do not
+    share KV columns, as in the reference's stage-1 packing, RD:232-245) and
+    ``drafts[b]`` its tokenized draft.  ``kv_tokens`` (device int32, one
+    token per KV column) is kept compacted alongside the mask; pass
+    ``kv_planes`` (device int64 plane addresses, see
+    :func:`hsd_b200.compaction.plane_pointers`) and ``row_bytes`` to have
+    model caches compacted in place too.
+    """
+
+    def __init__(self, prompts, drafts, *, eos_token_id, max_new_tokens, pad_token_id=0,
+                 match_window_size=3, match_window_size_upper_bound=10, min_input_length=128,
+                 max_spec_len=0, compact_period=1,
+                 repeat_sentinel=DOTS_SENTINEL, kv_planes=None, row_bytes=0,
+                 kv_capacity=None, device="cuda"):
+        if len(prompts) != len(drafts) or not prompts:
+            raise ValueError("one draft per prompt, at least one block")
+        self.device = torch.device(device)
+        dev = self.device
+        self.nb = len(prompts)
+        self.pad = int(pad_token_id)
+        self.eos = list(eos_token_id) if isinstance(eos_token_id, (list, tuple)) else [
+            int(eos_token_id)]
+        self.max_new_tokens = int(max_new_tokens)
+        self.mws0 = int(match_window_size)
+        self.mws_ub = int(match_window_size_upper_bound)
+        self.mil = int(min_input_length)
+        self.max_spec_len = int(max_spec_len)
+        self.period = int(compact_period)
+        self.sentinel = int(repeat_sentinel)
+        self.kv_planes, self.row_bytes = kv_planes, int(row_bytes)
+        self.drafts = [list(map(int, d)) for d in drafts]
+        lens = [len(p) for p in prompts]
+        if kv_capacity is None:
+            longest = max([self.mil] + [len(d) for d in self.drafts])
+            kv_capacity = sum(lens) + self.max_new_tokens + 4 * self.nb * longest + 64
+        self.kv_cap = int(kv_capacity)
+        self.stride = (self.kv_cap + 63) // 64
+        cap = self.max_new_tokens + max([len(d) for d in self.drafts] + [0]) + self.mil + 8
+        self.gen_cap = cap
+
+        # host state of the current step
+        self.input_ids = np.concatenate([np.asarray(p, dtype=np.int64) for p in prompts])
+        self.position_ids = np.concatenate([np.arange(n, dtype=np.int64) for n in lens])
+        self.q_start = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+        self.q_len = np.asarray(lens, dtype=np.int64)
+        self.kinds = [SEG_CAUSAL] * self.nb
+        self.modes = [N.HSD_MODE_NORMAL] * self.nb   # D:978
+        # non-pad rows per block (the reference counts them while
+        # block_valid_counts is None, D:1108-1111)
+        self.valid = [int(np.count_nonzero(np.asarray(p) != self.pad)) for p in prompts]
+        self.kv_len = int(self.input_ids.size)       # the prefill forward fills the cache
+        self.decode_times = 0
+        self.new_tokens = 0
+        self.done = False
+        self.compaction_s = 0.0
+        self.compaction_calls = 0
+        self.compactions_skipped = 0
+
+        # device state
+        blocks = np.zeros((self.nb, 16), dtype=np.int32)
+        doff = 0
+        for b in range(self.nb):
+            blocks[b, F["gen_off"]] = b * cap
+            blocks[b, F["gen_cap"]] = cap
+            blocks[b, F["draft_off"]] = doff
+            blocks[b, F["draft_len"]] = len(self.drafts[b])
+            blocks[b, F["mws"]] = self.mws0
+            blocks[b, F["seg"]] = b
+            doff += len(self.drafts[b])
+        self.blocks = torch.from_numpy(blocks).to(dev)
+        self.draft_pool = torch.tensor(sum(self.drafts, []) or [0], dtype=torch.int32, device=dev)
+        self.gen_pool = torch.zeros(self.nb * cap, dtype=torch.int32, device=dev)
+        self.seg_bits = torch.zeros((self.nb, self.stride), dtype=torch.int64, device=dev)
+        self.out_bits = torch.zeros_like(self.seg_bits)
+        self.filter = torch.zeros(self.stride, dtype=torch.int64, device=dev)
+        self.results = torch.zeros((self.nb, len(R)), dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.kv_tokens = torch.from_numpy(self.input_ids.astype(np.int32)).to(dev)
+        self._mask = None
+
+    # ------------------------------------------------------------------
+    def inputs(self):
+        """``(input_ids int32 [Q], position_ids int64 [Q], PackedMask)`` of this step."""
+        if self._mask is None:
+            q = int(self.input_ids.size)
+            segs = np.zeros((self.nb, 6), dtype=np.int32)
+            row_seg = np.full(q, -1, dtype=np.int32)
+            for b in range(self.nb):
+                qs, ql = int(self.q_start[b]), int(self.q_len[b])
+                segs[b, :3] = (qs, ql, self.kinds[b])
+                row_seg[qs:qs + ql] = b
+            self._mask = PackedMask.from_bits(q, self.kv_len, segs, row_seg, self.seg_bits,
+                                              self.device)
+        ids = torch.from_numpy(self.input_ids.astype(np.int32)).to(self.device)
+        pos = torch.from_numpy(self.position_ids).to(self.device)
+        return ids, pos, self._mask
+
+    def step(self, next_ids):
+        """Consume the target argmax of every packed row; prepare the next step.
+
+        Returns False once generation is finished (every block finished or
+        ``max_new_tokens`` generated, D:1589-1591).
+        """
+        if self.done:
+            raise RuntimeError("the loop has finished")
+        dev = self.device
+        self.decode_times += 1
+        q = int(self.input_ids.size)
+        kv = self.kv_len
+        upd = torch.tensor(np.stack([np.asarray(self.modes), self.q_start, self.q_len,
+                                     np.asarray(self.valid)], 1),
+                           dtype=torch.int32, device=dev)
+        self.blocks[:, F["mode"]] = upd[:, 0]
+        self.blocks[:, F["q_start"]] = upd[:, 1]
+        self.blocks[:, F["q_len"]] = upd[:, 2]
+        self.blocks[:, F["valid_count"]] = upd[:, 3]
+        self.filter.zero_()
+        self.out_bits.zero_()
+        cfg = make_config(self.nb, kv, q, self.stride, self.eos, self.mws0, self.mws_ub,
+                          self.max_spec_len, self.sentinel)
+        ids, _, _ = self.inputs()
+        accept_kmp(cfg, self.blocks, next_ids.to(torch.int32), ids, self.gen_pool,
+                   self.draft_pool, self.seg_bits, self.out_bits, self.filter,
+                   results=self.results, status=self.status)
+        res = self.results.cpu().numpy()
+        self._check()
+
+        # next inputs (D:1421-1565) from the result rows
+        new_ids, new_pos, new_lens = [], [], [0] * self.nb
+        new_modes, new_valid, new_kinds = list(self.modes), [0] * self.nb, list(self.kinds)
+        for b in range(self.nb):
+            if self.modes[b] == N.HSD_MODE_FINISHED:
+                continue
+            r = res[b]
+            self.new_tokens += int(r[R["increment"]])
+            if r[R["finished"]]:
+                new_modes[b] = N.HSD_MODE_FINISHED
+                continue
+            base = int(self.position_ids[int(r[R["pointer"]])]) + 1
+            if r[R["match_count"]] == 1:
+                toks = self.drafts[b][int(r[R["slice_begin"]]):int(r[R["slice_end"]])]
+                n = len(toks)
+                toks = toks + [self.pad] * (math.ceil(n / self.mil) * self.mil - n)
+                new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_SPEC, SEG_CAUSAL, n
+                pos = list(range(base, base + len(toks)))
+            else:
+                toks = [int(r[R["next_token"]])] + [self.pad] * (self.mil - 1)
+                pos = [base] + [0] * (self.mil - 1)
+                new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_NORMAL, SEG_SINGLE, 1
+            new_ids.append(toks)
+            new_pos.append(pos)
+            new_lens[b] = len(toks)
+        if self.new_tokens >= self.max_new_tokens or all(
+                m == N.HSD_MODE_FINISHED for m in new_modes):
+            self.modes = new_modes
+            self.done = True
+            return False
+
+        # pad columns of this step's input are filtered (D:1596-1599)
+        pad_cols = np.zeros(self.stride * 64, dtype=bool)
+        pad_cols[kv - q:kv] = self.input_ids == self.pad
+        self.filter |= torch.from_numpy(pack_bits(pad_cols).view(np.int64)).to(dev)
+
+        # keep = OR(rows of the active blocks) & ~filter (D:1679-1687)
+        t_c = time.perf_counter()
+        self.compaction_calls += 1
+        active = [b for b in range(self.nb) if new_modes[b] != N.HSD_MODE_FINISHED]
+        live = self.out_bits[torch.tensor(active, dtype=torch.long, device=dev)]
+        keep_bits, keep_idx, counts = keep_indices(live, self.filter, kv)
+        n_keep = int(counts[0].item())
+        dead = kv - n_keep
+        rule = self.period > 0 and (self.period <= 1 or self.decode_times % self.period == 0
+                                    or dead > kv * 0.2)
+        nw = (kv + 63) // 64
+        if rule and n_keep < kv:                      # compact (D:1704-1723)
+            if self.kv_planes is not None:
+                compact_kv(self.kv_planes, self.row_bytes, keep_idx, counts=counts,
+                           status=self.status)
+            self.kv_tokens = self.kv_tokens[keep_idx[:n_keep].long()]
+            self.seg_bits = compact_bits(self.out_bits, keep_idx, counts, self.stride)
+            kv = n_keep
+        elif not rule:                                # dead columns masked (D:1724-1729)
+            self.seg_bits = self.out_bits.clone()
+            self.seg_bits[:, :nw] &= keep_bits[None, :nw]
+            self.compactions_skipped += 1
+        else:
+            self.seg_bits = self.out_bits.clone()
+        self.compaction_s += time.perf_counter() - t_c
+
+        # the next packed input and its KV columns
+        self.input_ids = np.concatenate([np.asarray(t, dtype=np.int64) for t in new_ids])
+        self.position_ids = np.concatenate([np.asarray(t, dtype=np.int64) for t in new_pos])
+        ends = np.cumsum(new_lens)
+        self.q_len = np.asarray(new_lens, dtype=np.int64)
+        self.q_start = ends - self.q_len
+        self.modes, self.valid, self.kinds = new_modes, new_valid, new_kinds
+        self.kv_len = kv + int(self.input_ids.size)
+        if self.kv_len > self.kv_cap:
+            raise N.HSDError(f"KV columns {self.kv_len} exceed the loop's capacity {self.kv_cap}")
+        self.kv_tokens = torch.cat([self.kv_tokens,
+                                    torch.from_numpy(self.input_ids.astype(np.int32)).to(dev)])
+        self._mask = None
+        return True
+
+    def generated(self):
+        """Generated tokens of every block (EOS dropped, D:1303)."""
+        lens = self.blocks[:, F["gen_len"]].cpu().numpy()
+        pool = self.gen_pool.cpu().numpy()
+        return [pool[b * self.gen_cap: b * self.gen_cap + int(lens[b])].tolist()
+                for b in range(self.nb)]
+
+    def _check(self):
+        code = int(self.status.item())
+        if code:
+            raise N.HSDError(f"device status 0x{code:x} in the verification loop")
+
+
+def batch_generate(model_fn, prompts, drafts, *, eos_token_id, max_new_tokens, **loop_kwargs):
+    """Run the loop to completion with ``model_fn(input_ids, position_ids,
+    mask, kv_tokens) -> next_ids`` (the target forward + argmax per packed
+    row; ``mask`` is the step's :class:`PackedMask`, ``kv_tokens`` the token
+    of every KV column, which a model holding its own cache can ignore).
+
+    Returns the reference's result shape (D:1801-1810): ``(generated_tokens,
+    decode_times, (forward_s, outside_forward_s, 0.0, 0.0, first_forward_s,
+    compaction_s, compaction_calls, compactions_skipped))`` -- the setup and
+    preparation times have no counterpart here and are 0.
+    """
+    loop = VerifyLoop(prompts, drafts, eos_token_id=eos_token_id,
+                      max_new_tokens=max_new_tokens, **loop_kwargs)
+    t_fwd = t_out = first = 0.0
+    while True:
+        ids, pos, mask = loop.inputs()
+        torch.cuda.synchronize(loop.device)
+        t0 = time.perf_counter()
+        nxt = model_fn(ids, pos, mask, loop.kv_tokens)
+        torch.cuda.synchronize(loop.device)
+        t1 = time.perf_counter()
+        more = loop.step(nxt)
+        t2 = time.perf_counter()
+        t_fwd += t1 - t0
+        t_out += t2 - t1
+        if loop.decode_times == 1:
+            first = t1 - t0
+        if not more:
+            break
+    return loop.generated(), loop.decode_times, (t_fwd, t_out, 0.0, 0.0, first,
+                                                   loop.compaction_s, loop.compaction_calls,
+                                                   loop.compactions_skipped)

@@ -146,6 +146,31 @@ class PackedMask:
         self.tree_bits = torch.from_numpy(tree.view(np.int64)).to(device)
         self._plan = None
 
+    @classmethod
+    def from_bits(cls, q_len, kv_len, segs, row_seg, kv_bits, device="cuda", tree_bits=None):
+        """A mask whose segment visibility rows are already in device memory.
+
+        ``segs``: int32 ``[n, 6]`` rows of ``hsd_segment_t``; ``row_seg``:
+        int32 ``[q_len]`` (-1: row fully masked); ``kv_bits``: device int64
+        ``[n, stride]`` visibility rows (bit c of row i = column c), e.g. the
+        rows the acceptance kernel writes.  Tree segments need ``tree_bits``.
+        """
+        self = cls.__new__(cls)
+        self.q_len, self.kv_len = int(q_len), int(kv_len)
+        self.stride = int(kv_bits.shape[-1])
+        if self.stride * 64 < self.kv_len:
+            raise ValueError("visibility rows shorter than kv_len")
+        segs = np.asarray(segs, dtype=np.int32).reshape(-1, 6)
+        self.n_segs = segs.shape[0]
+        self.device = device
+        self.segs = torch.from_numpy(segs).to(device)
+        self.row_seg = torch.from_numpy(np.asarray(row_seg, dtype=np.int32)).to(device)
+        self.kv_bits = kv_bits
+        self.tree_bits = (tree_bits if tree_bits is not None
+                          else torch.zeros(1, dtype=torch.int64, device=device))
+        self._plan = None
+        return self
+
     def plan(self, stream=None) -> TilePlan:
         """Build (once) the device tile plan of this mask."""
         if self._plan is None:

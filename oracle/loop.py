@@ -1,0 +1,145 @@
+"""The verification loop of ``batch_generate`` restated on the CPU (test
+infrastructure only).
+
+Composes the per-step restatements of this package into the reference's
+iteration (hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py):
+
+* prefill packing: block-diagonal causal mask over the blocks' prompts,
+  ``pointer`` = cumulative ends - 1 (RD:232-245), every block starts in
+  ``normal`` mode (D:978-986);
+* per iteration: target argmax for every packed row (D:1057-1064), the
+  per-block acceptance / stop rules / KMP re-alignment / next input
+  (D:1103-1567), the generation-finished test (D:1589-1591), the pad filter
+  (D:1596-1599), keep columns and the compaction rule (D:1679-1731), the next
+  dense mask (D:1634-1667, D:1737-1748) and the next pointer (D:1604-1606);
+* the KV cache grows by the packed input of every forward (DynamicCache) and
+  loses the compacted columns.
+
+Only region blocks are restated: the page block's text/select/bbox parsers
+need the tokenizer and stay on the host (D:1337-1419), so the loop also has
+no "last block finished" stop (D:1591-1592).  ``model(input_ids,
+position_ids, allowed, kv_tokens)`` stands for the target forward + argmax:
+``allowed`` is the step's [Q, KV] visibility, ``kv_tokens`` the token of
+every KV column.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from .accept import FINISHED, BlockState, accept_block, next_block_input, realign_block
+from .compact import apply_to_mask, compaction_action, keep_columns, pad_filter
+from .masks import (assemble_next_mask, initial_packed_mask, normal_block_mask,
+                    spec_block_mask, tree_block_mask)
+
+
+def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1,
+                   max_iters=1000):
+    """Run the loop; returns ``(generated tokens per block, trace)``.
+
+    ``trace`` holds, per iteration, the packed ``input_ids``,
+    ``position_ids``, the bool ``allowed`` mask [Q, KV] and the compaction
+    action taken after the step.
+    """
+    nb = len(prompts)
+    lens = [len(p) for p in prompts]
+    input_ids = np.concatenate([np.asarray(p, dtype=np.int64) for p in prompts])
+    position_ids = np.concatenate([np.arange(n, dtype=np.int64) for n in lens])
+    mask = initial_packed_mask(lens)
+    kv_tokens = input_ids.copy()
+    pointer = [int(x) for x in np.cumsum(lens) - 1]
+    states = [BlockState(draft=list(d), mws=cfg.match_window_size) for d in drafts]
+    new_tokens = 0
+    trace = []
+    for decode_times in range(1, max_iters + 1):
+        allowed = (mask[0, 0] > -0.1).numpy()
+        q = len(input_ids)
+        kv = allowed.shape[1]
+        next_ids = np.asarray(model(input_ids, position_ids, allowed, kv_tokens), dtype=np.int64)
+        step = dict(input_ids=input_ids.copy(), position_ids=position_ids.copy(),
+                    allowed=allowed.copy())
+        trace.append(step)
+        kv_base = kv - q
+        filt = np.zeros(kv, dtype=bool)
+        next_list, input_list = next_ids.tolist(), input_ids.tolist()
+        new_ids, new_pos = [], []
+        new_lens, new_masks = [0] * nb, [None] * nb
+        bs = 0
+        for b in range(nb):
+            be = pointer[b] + 1
+            st = states[b]
+            if st.mode == FINISHED:
+                bs = be
+                continue
+            ptr, nxt, inc, fin = accept_block(st, bs, be, next_list, input_list, cfg, filt,
+                                              kv_base, lambda row: allowed[row], False)
+            pointer[b] = ptr
+            new_tokens += inc
+            bs = be
+            if fin:
+                continue
+            window, matches, trie = realign_block(st, cfg)
+            ids, pos, kind, n = next_block_input(st, cfg, window, matches, trie, nxt,
+                                                 int(position_ids[ptr]) + 1)
+            new_ids.append(ids)
+            new_pos.append(pos)
+            new_lens[b] = n
+            if kind == "causal":
+                new_masks[b] = spec_block_mask(n)
+            elif kind == "tree":
+                new_masks[b] = tree_block_mask(st.tree_parents, n)
+            else:
+                new_masks[b] = normal_block_mask(n)
+        if new_tokens >= max_new_tokens or all(st.mode == FINISHED for st in states):
+            step["action"] = "stop"
+            break
+        filt = pad_filter(filt, input_ids, cfg.pad_token_id)
+        active = [pointer[b] for b in range(nb) if states[b].mode != FINISHED]
+        keep = keep_columns(allowed, active, filt)
+        action = compaction_action(kv, int(keep.sum()), decode_times, compact_period)
+        step["action"] = action
+        mask = apply_to_mask(mask, keep, action)
+        if action == "compact":
+            kv_tokens = kv_tokens[keep]
+        mask = assemble_next_mask(mask, pointer, new_lens, new_masks)
+        input_ids = np.concatenate([np.asarray(x, dtype=np.int64) for x in new_ids])
+        position_ids = np.concatenate([np.asarray(x, dtype=np.int64) for x in new_pos])
+        kv_tokens = np.concatenate([kv_tokens, input_ids])
+        pointer = [int(x) for x in np.cumsum(new_lens) - 1]
+    return [list(st.gen) for st in states], trace
+
+
+def true_text_model(prompts, truths, vocab, eos_id):
+    """Deterministic stand-in for the target model's argmax.
+
+    A row's context is the token of every KV column it sees, in column order
+    (its own column last).  The block is identified by its prompt (prompts
+    are distinct); when the tokens after the prompt match a prefix of the
+    block's true text, the model predicts the next true token (EOS past the
+    end), otherwise a token hashed from the last four context tokens.  Rows
+    that see nothing predict 0.
+    """
+    heads = {tuple(int(t) for t in p[:4]): b for b, p in enumerate(prompts)}
+
+    def model(input_ids, position_ids, allowed, kv_tokens):
+        kv_tokens = np.asarray(kv_tokens, dtype=np.int64)
+        out = np.zeros(allowed.shape[0], dtype=np.int64)
+        for r in range(allowed.shape[0]):
+            ctx = kv_tokens[allowed[r]]
+            if len(ctx) == 0:
+                continue
+            b = heads.get(tuple(int(t) for t in ctx[:4]))
+            if b is not None:
+                gen = ctx[len(prompts[b]):]
+                truth = truths[b]
+                if len(gen) <= len(truth) and np.array_equal(gen, truth[:len(gen)]):
+                    out[r] = truth[len(gen)] if len(gen) < len(truth) else eos_id
+                    continue
+            tail = [int(t) for t in ctx[-4:]]
+            h = 0
+            for t in tail:
+                h = (h * 1000003 + t + 1) % 2147483647
+            out[r] = 1 + h % (vocab - 1)
+        return out
+
+    return model

@@ -1,0 +1,86 @@
+"""The multi-step verification loop: oracle restatement and device loop.
+
+The synthetic target model continues each block's true text whenever the
+context matches it, so verified generation must reproduce the true texts
+exactly (speculative decoding is lossless), whatever the drafts.  The device
+loop must follow the oracle loop step by step: the same packed inputs and
+positions, the same dense mask (read back from the device tile plan) and the
+same generated tokens.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import accept as OA
+from oracle import loop as OL
+from tests import loop_cases as LC
+
+MIL = 16
+
+
+def _cfg():
+    return OA.StepConfig(pad_token_id=LC.PAD, eos_token_ids=(LC.EOS,), min_input_length=MIL)
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_oracle_loop_reproduces_true_texts(seed):
+    prompts, truths, drafts = LC.make_loop_case(seed)
+    model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
+    gen, trace = OL.reference_loop(prompts, drafts, model, _cfg(), max_new_tokens=10 ** 6)
+    for b, (g, t) in enumerate(zip(gen, truths)):
+        if b % 4 == 3:   # repetition stop: the draft replaces the output
+            assert g == drafts[b]
+        else:
+            assert g == list(map(int, t)), b
+    # drafts save steps: fewer forwards than the longest text has tokens
+    assert len(trace) < max(len(t) for t in truths)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("seed,period", [(0, 1), (1, 1), (2, 3)])
+def test_device_loop_follows_oracle_loop(seed, period):
+    from hsd_b200.loop import VerifyLoop
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    dev = torch.device("cuda:0")
+    prompts, truths, drafts = LC.make_loop_case(seed)
+    model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
+    ref_gen, trace = OL.reference_loop(prompts, drafts, model, _cfg(), max_new_tokens=10 ** 6,
+                                       compact_period=period)
+    loop = VerifyLoop(prompts, drafts, eos_token_id=LC.EOS, max_new_tokens=10 ** 6,
+                      pad_token_id=LC.PAD, min_input_length=MIL, compact_period=period,
+                      device=dev)
+    for it, ref in enumerate(trace):
+        ids, pos, mask = loop.inputs()
+        np.testing.assert_array_equal(ids.cpu().numpy(), ref["input_ids"], err_msg=f"step {it}")
+        np.testing.assert_array_equal(pos.cpu().numpy(), ref["position_ids"])
+        plan = mask.plan()
+        allowed = plan.dense_allowed()
+        plan.raise_on_device_error()
+        assert allowed.shape == ref["allowed"].shape, (it, allowed.shape, ref["allowed"].shape)
+        np.testing.assert_array_equal(allowed, ref["allowed"], err_msg=f"mask, step {it}")
+        kv_tokens = loop.kv_tokens.cpu().numpy()
+        nxt = model(ref["input_ids"], ref["position_ids"], allowed, kv_tokens)
+        more = loop.step(torch.from_numpy(nxt).to(dev))
+        assert more == (it + 1 < len(trace)), it
+    assert loop.generated() == ref_gen
+
+
+@pytest.mark.gpu
+def test_batch_generate_returns_true_texts():
+    from hsd_b200.loop import batch_generate
+    dev = torch.device("cuda:0")
+    prompts, truths, drafts = LC.make_loop_case(5)
+    model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
+    ref_gen, trace = OL.reference_loop(prompts, drafts, model, _cfg(), max_new_tokens=10 ** 6)
+
+    def model_fn(ids, pos, mask, kv_tokens):
+        allowed = mask.plan().dense_allowed()
+        return torch.from_numpy(model(ids.cpu().numpy(), pos.cpu().numpy(), allowed,
+                                      kv_tokens.cpu().numpy())).to(dev)
+
+    gen, decode_times, timings = batch_generate(
+        model_fn, prompts, drafts, eos_token_id=LC.EOS, max_new_tokens=10 ** 6,
+        pad_token_id=LC.PAD, min_input_length=MIL, device=dev)
+    assert gen == ref_gen
+    assert decode_times == len(trace)
+    assert len(timings) == 8 and timings[6] == decode_times - 1
