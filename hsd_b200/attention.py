@@ -116,13 +116,18 @@ def flex_attention_forward(module, query, key, value, attention_mask, scaling=No
                            softcap=None, head_mask=None, **kwargs):
     """Drop-in for the reference's ``flex_attention_forward``.
 
-    Returns ``(attn_output [1, Q, Hq, D] contiguous, lse [1, Hq, Q] in the
-    value dtype)`` like D:131-135.  ``softcap`` and ``head_mask`` are not used
-    by the reference's FlexAttention call either (D:118-130).
+    Returns ``(attn_output [1, Q, Hq, D] contiguous, lse [1, Hq, Q])`` in the
+    value dtype like D:131-135.  The kernel computes in bf16 (fp32
+    accumulation): fp32 / fp16 models get their q, k, v cast to bf16 and the
+    output cast back.  ``softcap`` and ``head_mask`` are not used by the
+    reference's FlexAttention call either (D:118-130).
     """
     if attention_mask is None:
         raise ValueError("packed verification needs a mask (dense, PackedMask or TilePlan)")
     q_len, kv_len = query.shape[-2], key.shape[-2]
     plan = plan_for(attention_mask, q_len, kv_len)
+    dtype = value.dtype
+    if dtype != torch.bfloat16:
+        query, key, value = (t.to(torch.bfloat16) for t in (query, key, value))
     out, lse = verify_attention(query, key, value, plan, scale=scaling)
-    return out.unsqueeze(0), lse.to(value.dtype).unsqueeze(0)
+    return out.to(dtype).unsqueeze(0), lse.to(dtype).unsqueeze(0)

@@ -171,6 +171,23 @@ def test_attention_strided_query_layout(dev):
     assert err.max().item() <= MAX_ABS and err.mean().item() <= MEAN_ABS
 
 
+def test_drop_in_fp32_model_cfg1(dev):
+    """The reference's first config runs FlexAttention in fp32: the drop-in
+    takes fp32 q/k/v (computed in bf16) and returns fp32, within the bf16
+    tolerance of the fp32 reference."""
+    from hsd_b200.attention import flex_attention_forward
+    q, k, v, mask, scale, _ = dict(C.attention_cases())["cfg1"]
+    allowed = OB.allowed_from_dense(mask)
+    out, lse = flex_attention_forward(None, q[None].to(dev), k[None].to(dev), v[None].to(dev),
+                                      mask.to(dev), scaling=scale)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float32 and lse.dtype == torch.float32
+    ref_out, ref_lse = OA.attention_fp32(q, k, v, allowed, scale)
+    err = (out[0].cpu() - ref_out).abs()
+    assert err.max().item() <= MAX_ABS and err.mean().item() <= MEAN_ABS
+    assert (lse[0].cpu() - ref_lse).abs().max().item() <= LSE_ABS
+
+
 def test_attention_long_prefix_many_blocks(dev):
     """Stage-2 shape slice: one causal segment over a long cached prefix."""
     kv_old, ql = 2000, 300
