@@ -19,8 +19,10 @@ The target model stays outside: :meth:`VerifyLoop.inputs` gives the packed
 ``input_ids`` / ``position_ids`` and the step's :class:`PackedMask` (its
 tile plan is what :func:`hsd_b200.attention.flex_attention_forward`
 consumes), and :meth:`VerifyLoop.step` takes the model's argmax per packed
-row.  Not driven by this loop: tree decoding (``enable_tree_decode``), tight
-packing (HSD_TIGHT_PACK) and the page block's tokenizer-driven parsers.
+row.  With ``enable_tree_decode`` a block without exactly one KMP match
+proposes its draft's continuation tree (:mod:`hsd_b200.trie`, D:1488-1543).
+Not driven by this loop: tight packing (HSD_TIGHT_PACK) and the page block's
+tokenizer-driven parsers.
 """
 from __future__ import annotations
 
@@ -33,7 +35,8 @@ import torch
 from . import _native as N
 from .accept import DOTS_SENTINEL, F, R, accept_kmp, make_config
 from .compaction import compact_bits, compact_kv, keep_indices
-from .plan import SEG_CAUSAL, SEG_SINGLE, PackedMask, pack_bits
+from .plan import SEG_CAUSAL, SEG_SINGLE, SEG_TREE, PackedMask, pack_bits
+from .trie import continuation_tree
 
 
 class VerifyLoop:
@@ -50,7 +53,8 @@ class VerifyLoop:
 
     def __init__(self, prompts, drafts, *, eos_token_id, max_new_tokens, pad_token_id=0,
                  match_window_size=3, match_window_size_upper_bound=10, min_input_length=128,
-                 max_spec_len=0, compact_period=1,
+                 max_spec_len=0, compact_period=1, enable_tree_decode=False,
+                 max_tree_depth=15, max_tree_len=256,
                  repeat_sentinel=DOTS_SENTINEL, kv_planes=None, row_bytes=0,
                  kv_capacity=None, device="cuda"):
         if len(prompts) != len(drafts) or not prompts:
@@ -66,6 +70,10 @@ class VerifyLoop:
         self.mws_ub = int(match_window_size_upper_bound)
         self.mil = int(min_input_length)
         self.max_spec_len = int(max_spec_len)
+        self.tree_decode = bool(enable_tree_decode)
+        self.tree_depth = int(max_tree_depth)
+        self.tree_cap = (min(int(max_tree_len), self.max_spec_len) if self.max_spec_len > 0
+                         else int(max_tree_len))
         self.period = int(compact_period)
         self.sentinel = int(repeat_sentinel)
         self.kv_planes, self.row_bytes = kv_planes, int(row_bytes)
@@ -85,6 +93,7 @@ class VerifyLoop:
         self.q_start = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
         self.q_len = np.asarray(lens, dtype=np.int64)
         self.kinds = [SEG_CAUSAL] * self.nb
+        self.trees = [None] * self.nb                # (tokens, parents) of TREE blocks
         self.modes = [N.HSD_MODE_NORMAL] * self.nb   # D:978
         # non-pad rows per block (the reference counts them while
         # block_valid_counts is None, D:1108-1111)
@@ -126,12 +135,30 @@ class VerifyLoop:
             q = int(self.input_ids.size)
             segs = np.zeros((self.nb, 6), dtype=np.int32)
             row_seg = np.full(q, -1, dtype=np.int32)
+            tree_rows, tree_off = [], 0
             for b in range(self.nb):
                 qs, ql = int(self.q_start[b]), int(self.q_len[b])
                 segs[b, :3] = (qs, ql, self.kinds[b])
                 row_seg[qs:qs + ql] = b
+                if self.kinds[b] == SEG_TREE:
+                    # node i sees itself and its ancestors (D:1506-1533); pad rows nothing
+                    tw = (ql + 63) // 64
+                    anc = np.zeros((ql, tw * 64), dtype=bool)
+                    parents = self.trees[b][1]
+                    for i in range(len(parents)):
+                        a = i
+                        while a >= 0:
+                            anc[i, a] = True
+                            a = parents[a]
+                    tree_rows.append(pack_bits(anc).reshape(-1))
+                    segs[b, 3], segs[b, 4] = tree_off, tw
+                    tree_off += ql * tw
+            tree_bits = None
+            if tree_rows:
+                tree_bits = torch.from_numpy(np.concatenate(tree_rows).view(np.int64)).to(
+                    self.device)
             self._mask = PackedMask.from_bits(q, self.kv_len, segs, row_seg, self.seg_bits,
-                                              self.device)
+                                              self.device, tree_bits)
         ids = torch.from_numpy(self.input_ids.astype(np.int32)).to(self.device)
         pos = torch.from_numpy(self.position_ids).to(self.device)
         return ids, pos, self._mask
@@ -155,6 +182,18 @@ class VerifyLoop:
         self.blocks[:, F["q_start"]] = upd[:, 1]
         self.blocks[:, F["q_len"]] = upd[:, 2]
         self.blocks[:, F["valid_count"]] = upd[:, 3]
+        tree_tok, tree_par, toff = [], [], np.zeros(self.nb, dtype=np.int32)
+        tnodes = np.zeros(self.nb, dtype=np.int32)
+        for b in range(self.nb):
+            if self.modes[b] == N.HSD_MODE_TREE:
+                toff[b], tnodes[b] = len(tree_tok), len(self.trees[b][0])
+                tree_tok += self.trees[b][0]
+                tree_par += self.trees[b][1]
+        if tree_tok:
+            self.blocks[:, F["tree_off"]] = torch.from_numpy(toff).to(dev)
+            self.blocks[:, F["tree_nodes"]] = torch.from_numpy(tnodes).to(dev)
+        d_tok = torch.tensor(tree_tok or [0], dtype=torch.int32, device=dev)
+        d_par = torch.tensor(tree_par or [0], dtype=torch.int32, device=dev)
         self.filter.zero_()
         self.out_bits.zero_()
         cfg = make_config(self.nb, kv, q, self.stride, self.eos, self.mws0, self.mws_ub,
@@ -162,13 +201,15 @@ class VerifyLoop:
         ids, _, _ = self.inputs()
         accept_kmp(cfg, self.blocks, next_ids.to(torch.int32), ids, self.gen_pool,
                    self.draft_pool, self.seg_bits, self.out_bits, self.filter,
-                   results=self.results, status=self.status)
+                   tree_tokens=d_tok, tree_parents=d_par, results=self.results,
+                   status=self.status)
         res = self.results.cpu().numpy()
         self._check()
 
         # next inputs (D:1421-1565) from the result rows
         new_ids, new_pos, new_lens = [], [], [0] * self.nb
         new_modes, new_valid, new_kinds = list(self.modes), [0] * self.nb, list(self.kinds)
+        new_trees = [None] * self.nb
         for b in range(self.nb):
             if self.modes[b] == N.HSD_MODE_FINISHED:
                 continue
@@ -185,9 +226,22 @@ class VerifyLoop:
                 new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_SPEC, SEG_CAUSAL, n
                 pos = list(range(base, base + len(toks)))
             else:
-                toks = [int(r[R["next_token"]])] + [self.pad] * (self.mil - 1)
-                pos = [base] + [0] * (self.mil - 1)
-                new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_NORMAL, SEG_SINGLE, 1
+                tree = None
+                if self.tree_decode:
+                    tree = continuation_tree(self.drafts[b], int(r[R["next_token"]]),
+                                             self.tree_depth, self.tree_cap)
+                if tree is not None and len(tree[0]) > 1:    # D:1488-1543
+                    tokens, depths, parents = tree
+                    n = len(tokens)
+                    pad_n = math.ceil(n / self.mil) * self.mil - n
+                    toks = list(tokens) + [self.pad] * pad_n
+                    pos = [d + base for d in depths] + [0] * pad_n
+                    new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_TREE, SEG_TREE, n
+                    new_trees[b] = (list(tokens), list(parents))
+                else:                                        # D:1544-1565
+                    toks = [int(r[R["next_token"]])] + [self.pad] * (self.mil - 1)
+                    pos = [base] + [0] * (self.mil - 1)
+                    new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_NORMAL, SEG_SINGLE, 1
             new_ids.append(toks)
             new_pos.append(pos)
             new_lens[b] = len(toks)
@@ -235,6 +289,7 @@ class VerifyLoop:
         self.q_len = np.asarray(new_lens, dtype=np.int64)
         self.q_start = ends - self.q_len
         self.modes, self.valid, self.kinds = new_modes, new_valid, new_kinds
+        self.trees = new_trees
         self.kv_len = kv + int(self.input_ids.size)
         if self.kv_len > self.kv_cap:
             raise N.HSDError(f"KV columns {self.kv_len} exceed the loop's capacity {self.kv_cap}")

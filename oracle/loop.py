@@ -38,8 +38,8 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
     """Run the loop; returns ``(generated tokens per block, trace)``.
 
     ``trace`` holds, per iteration, the packed ``input_ids``,
-    ``position_ids``, the bool ``allowed`` mask [Q, KV] and the compaction
-    action taken after the step.
+    ``position_ids``, the bool ``allowed`` mask [Q, KV], the blocks' modes
+    and the compaction action taken after the step.
     """
     nb = len(prompts)
     lens = [len(p) for p in prompts]
@@ -57,7 +57,7 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
         kv = allowed.shape[1]
         next_ids = np.asarray(model(input_ids, position_ids, allowed, kv_tokens), dtype=np.int64)
         step = dict(input_ids=input_ids.copy(), position_ids=position_ids.copy(),
-                    allowed=allowed.copy())
+                    allowed=allowed.copy(), modes=[st.mode for st in states])
         trace.append(step)
         kv_base = kv - q
         filt = np.zeros(kv, dtype=bool)

@@ -18,15 +18,19 @@ from tests import loop_cases as LC
 MIL = 16
 
 
-def _cfg():
-    return OA.StepConfig(pad_token_id=LC.PAD, eos_token_ids=(LC.EOS,), min_input_length=MIL)
+def _cfg(tree=False):
+    return OA.StepConfig(pad_token_id=LC.PAD, eos_token_ids=(LC.EOS,), min_input_length=MIL,
+                         enable_tree_decode=tree)
 
 
-@pytest.mark.parametrize("seed", [0, 1, 2])
-def test_oracle_loop_reproduces_true_texts(seed):
+@pytest.mark.parametrize("seed,tree", [(0, False), (1, False), (2, False), (3, True),
+                                       (4, True)])
+def test_oracle_loop_reproduces_true_texts(seed, tree):
     prompts, truths, drafts = LC.make_loop_case(seed)
     model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
-    gen, trace = OL.reference_loop(prompts, drafts, model, _cfg(), max_new_tokens=10 ** 6)
+    gen, trace = OL.reference_loop(prompts, drafts, model, _cfg(tree), max_new_tokens=10 ** 6)
+    if tree:  # tree blocks were proposed and walked
+        assert any(OA.TREE in s["modes"] for s in trace)
     for b, (g, t) in enumerate(zip(gen, truths)):
         if b % 4 == 3:   # repetition stop: the draft replaces the output
             assert g == drafts[b]
@@ -37,18 +41,19 @@ def test_oracle_loop_reproduces_true_texts(seed):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("seed,period", [(0, 1), (1, 1), (2, 3)])
-def test_device_loop_follows_oracle_loop(seed, period):
+@pytest.mark.parametrize("seed,period,tree", [(0, 1, False), (1, 1, False), (2, 3, False),
+                                              (3, 1, True), (4, 2, True)])
+def test_device_loop_follows_oracle_loop(seed, period, tree):
     from hsd_b200.loop import VerifyLoop
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
     dev = torch.device("cuda:0")
     prompts, truths, drafts = LC.make_loop_case(seed)
     model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
-    ref_gen, trace = OL.reference_loop(prompts, drafts, model, _cfg(), max_new_tokens=10 ** 6,
-                                       compact_period=period)
+    ref_gen, trace = OL.reference_loop(prompts, drafts, model, _cfg(tree),
+                                       max_new_tokens=10 ** 6, compact_period=period)
     loop = VerifyLoop(prompts, drafts, eos_token_id=LC.EOS, max_new_tokens=10 ** 6,
                       pad_token_id=LC.PAD, min_input_length=MIL, compact_period=period,
-                      device=dev)
+                      enable_tree_decode=tree, device=dev)
     for it, ref in enumerate(trace):
         ids, pos, mask = loop.inputs()
         np.testing.assert_array_equal(ids.cpu().numpy(), ref["input_ids"], err_msg=f"step {it}")
@@ -84,3 +89,18 @@ def test_batch_generate_returns_true_texts():
     assert gen == ref_gen
     assert decode_times == len(trace)
     assert len(timings) == 8 and timings[6] == decode_times - 1
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_continuation_tree_matches_oracle_trie(seed):
+    """hsd_b200.trie packs the same tree as the reference's KMP trie + BFS."""
+    from hsd_b200.trie import continuation_tree
+    from oracle import kmp as OK
+    rng = np.random.default_rng(seed)
+    draft = [int(x) for x in rng.integers(1, 6 + seed, int(rng.integers(5, 200)))]
+    gen = [int(x) for x in rng.integers(1, 6 + seed, int(rng.integers(1, 12)))]
+    depth = int(rng.integers(1, 16))
+    cap = int(rng.integers(1, 300))
+    window = gen[-min(10, len(gen)):]
+    trie, _ = OK.find_all_matches_kmp([draft], window, OK.compute_lps(window), depth)
+    assert continuation_tree(draft, window[-1], depth, cap) == OK.trie_bfs(trie, cap)
