@@ -35,7 +35,7 @@ import torch
 from . import _native as N
 from .accept import DOTS_SENTINEL, F, R, accept_kmp, make_config
 from .compaction import compact_bits, compact_kv, keep_indices
-from .plan import SEG_CAUSAL, SEG_SINGLE, SEG_TREE, PackedMask, pack_bits
+from .plan import SEG_CAUSAL, SEG_NONE, SEG_SINGLE, SEG_TREE, PackedMask, pack_bits
 from .trie import continuation_tree
 
 
@@ -212,11 +212,12 @@ class VerifyLoop:
         new_trees = [None] * self.nb
         for b in range(self.nb):
             if self.modes[b] == N.HSD_MODE_FINISHED:
+                new_kinds[b] = SEG_NONE   # no rows any more
                 continue
             r = res[b]
             self.new_tokens += int(r[R["increment"]])
             if r[R["finished"]]:
-                new_modes[b] = N.HSD_MODE_FINISHED
+                new_modes[b], new_kinds[b] = N.HSD_MODE_FINISHED, SEG_NONE
                 continue
             base = int(self.position_ids[int(r[R["pointer"]])]) + 1
             if r[R["match_count"]] == 1:
