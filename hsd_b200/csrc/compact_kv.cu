@@ -223,17 +223,28 @@ __global__ void __launch_bounds__(1024) keep_kernel(const uint64_t* live, int n_
   __shared__ int warp_sums[32];
   __shared__ int carry;
   __shared__ int first_moved;
+  __shared__ unsigned long long acc[1024];  // OR of the live rows, one chunk of words
   const int nw = (kv_len + 63) / 64;
   if (threadIdx.x == 0) {
     carry = 0;
     first_moved = 0x7fffffff;
   }
-  __syncthreads();
   for (int base = 0; base < nw; base += blockDim.x) {
+    // OR of the live rows over this chunk of words: all threads share the
+    // (row, word) pairs, so the loads are in flight together
+    const int cw = min(int(blockDim.x), nw - base);
+    acc[threadIdx.x] = 0ull;
+    __syncthreads();
+    for (int k = threadIdx.x; k < n_live * cw; k += blockDim.x) {
+      const int r = k / cw, wi = k - r * cw;
+      const uint64_t v = live[size_t(r) * live_stride + base + wi];
+      if (v) atomicOr(&acc[wi], static_cast<unsigned long long>(v));
+    }
+    __syncthreads();
     const int t = base + threadIdx.x;
     uint64_t w = 0;
     if (t < nw) {
-      for (int r = 0; r < n_live; ++r) w |= live[size_t(r) * live_stride + t];
+      w = acc[threadIdx.x];
       if (filter) w &= ~filter[t];
       const int rem = kv_len - 64 * t;
       if (rem < 64) w &= (1ull << rem) - 1ull;
@@ -259,15 +270,17 @@ __global__ void __launch_bounds__(1024) keep_kernel(const uint64_t* live, int n_
     __syncthreads();
     const int excl = carry + (warp_id() ? warp_sums[warp_id() - 1] : 0) + x - c;
     int pos = excl;
+    int moved = 0x7fffffff;  // col - pos never decreases: the first mismatch is the one
     uint64_t m = w;
     while (m) {
       const int b = __ffsll(static_cast<long long>(m)) - 1;
       const int col = 64 * t + b;
       keep_idx[pos] = col;
-      if (col != pos) atomicMin(&first_moved, pos);
+      if (col != pos && moved == 0x7fffffff) moved = pos;
       ++pos;
       m &= m - 1;
     }
+    if (moved != 0x7fffffff) atomicMin(&first_moved, moved);
     __syncthreads();
     if (threadIdx.x == blockDim.x - 1) carry = excl + c;
     __syncthreads();
@@ -279,23 +292,30 @@ __global__ void __launch_bounds__(1024) keep_kernel(const uint64_t* live, int n_
 }
 
 // out[r] bit i = in[r] bit keep_idx[i], i < n_keep; words past n_keep cleared.
+// One warp per output word: lane l fetches bits l and l + 32, two ballots
+// assemble the word.
 __global__ void compact_bits_kernel(const uint64_t* in, uint64_t* out, int n_rows, int stride,
                                     const int32_t* keep_idx, const int32_t* counts,
                                     int out_words) {
   const int n_keep = counts[0];
   const int total = n_rows * out_words;
-  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += gridDim.x * blockDim.x) {
+  const int lane = lane_id();
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int idx = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; idx < total; idx += warps) {
     const int r = idx / out_words, t = idx % out_words;
     const uint64_t* row = in + size_t(r) * stride;
-    uint64_t w = 0;
-    for (int b = 0; b < 64; ++b) {
-      const int i = 64 * t + b;
-      if (i >= n_keep) break;
-      const int src = keep_idx[i];
-      w |= ((row[src >> 6] >> (src & 63)) & 1ull) << b;
+    const int i0 = 64 * t + lane, i1 = i0 + 32;
+    bool b0 = false, b1 = false;
+    if (i0 < n_keep) {
+      const int src = keep_idx[i0];
+      b0 = (row[src >> 6] >> (src & 63)) & 1ull;
     }
-    out[size_t(r) * stride + t] = w;
+    if (i1 < n_keep) {
+      const int src = keep_idx[i1];
+      b1 = (row[src >> 6] >> (src & 63)) & 1ull;
+    }
+    const uint32_t lo = __ballot_sync(0xffffffffu, b0), hi = __ballot_sync(0xffffffffu, b1);
+    if (lane == 0) out[size_t(r) * stride + t] = (uint64_t(hi) << 32) | lo;
   }
 }
 
@@ -438,8 +458,8 @@ int hsd_compact_bits(const uint64_t* in_bits, uint64_t* out_bits, int32_t n_rows
     hsd_host::set_error("hsd_compact_bits: bad arguments (in-place remap is not supported)");
     return HSD_ERR_INVALID_ARG;
   }
-  const int total = n_rows * out_words;
-  const int grid = (total + 255) / 256 < 1184 ? (total + 255) / 256 : 1184;
+  const int total = n_rows * out_words;  // one warp per output word
+  const int grid = (total + 7) / 8 < 1184 ? (total + 7) / 8 : 1184;
   compact::compact_bits_kernel<<<grid > 0 ? grid : 1, 256, 0,
                                   reinterpret_cast<cudaStream_t>(stream)>>>(
       in_bits, out_bits, n_rows, stride, keep_idx, counts, out_words);
