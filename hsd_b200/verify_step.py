@@ -16,6 +16,8 @@ decoder GEMMs, which stay in the model:
 ``VerifyStep.run()`` launches all of it on one stream without a host sync.
 ``VerifyStep.run_from_host()`` is the end-to-end form: the step's inputs come
 from pinned host buffers and the per-block results go back to the host.
+Both capture into CUDA graphs (``VerifyStep.capture``): every buffer and
+launch argument is fixed, so a replay re-runs the step without host work.
 """
 from __future__ import annotations
 
@@ -156,21 +158,7 @@ class VerifyStep:
             C.byref(self.plan.struct), p(self.status), st), "hsd_build_plan_segments")
         mark("plan", 1)
         # 3. attention, every layer
-        scale = 1.0 / np.sqrt(self.d)
-        ql, kvl, hq, hkv, d = self.q_len, self.kv_len, self.hq, self.hkv, self.d
-        for l in range(self.L):
-            q = self.q[l]
-            k = self.cache[l, 0]
-            v = self.cache[l, 1]
-            if attn_events is not None:
-                attn_events[l][0].record(stream)
-            N.check(lib.hsd_verify_attention(
-                p(q), q.stride(1), q.stride(0), p(k), k.stride(1), k.stride(0), p(v), v.stride(1),
-                v.stride(0), p(self.out[l]), p(self.lse[l]), ql, kvl, hq, hkv, d, scale,
-                C.byref(self.plan.struct), C.c_void_p(self.ws.base), self.ws.nbytes,
-                p(self.status), st), "hsd_verify_attention")
-            if attn_events is not None:
-                attn_events[l][1].record(stream)
+        self.run_attention(stream, attn_events)
         # 4. acceptance + KMP
         mark("accept", 0)
         N.check(lib.hsd_accept_kmp(
@@ -195,6 +183,27 @@ class VerifyStep:
                                      p(self.keep_idx), p(self.counts), self.stride, st),
                 "hsd_compact_bits")
         mark("bits", 1)
+
+    def run_attention(self, stream=None, attn_events=None):
+        """The step's attention launches alone (every layer, current plan)."""
+        lib = N.load()
+        st = N.stream_handle(stream)
+        p = self._ptr
+        scale = 1.0 / np.sqrt(self.d)
+        ql, kvl, hq, hkv, d = self.q_len, self.kv_len, self.hq, self.hkv, self.d
+        for l in range(self.L):
+            q = self.q[l]
+            k = self.cache[l, 0]
+            v = self.cache[l, 1]
+            if attn_events is not None:
+                attn_events[l][0].record(stream)
+            N.check(lib.hsd_verify_attention(
+                p(q), q.stride(1), q.stride(0), p(k), k.stride(1), k.stride(0), p(v), v.stride(1),
+                v.stride(0), p(self.out[l]), p(self.lse[l]), ql, kvl, hq, hkv, d, scale,
+                C.byref(self.plan.struct), C.c_void_p(self.ws.base), self.ws.nbytes,
+                p(self.status), st), "hsd_verify_attention")
+            if attn_events is not None:
+                attn_events[l][1].record(stream)
 
     def compaction_bytes(self):
         """(bytes moved by the last compaction (read + write), rows moved, rows kept)."""
@@ -233,6 +242,23 @@ class VerifyStep:
         self.run(stream)
         h["results"].copy_(self.results, non_blocking=True)
         h["counts"].copy_(self.counts, non_blocking=True)
+
+    def capture(self, from_host=False, attention_only=False):
+        """A CUDA graph of one whole step (``run`` or ``run_from_host``, or
+        only its attention launches): the launches replay with no host work
+        between them.  Call :meth:`run` once before capturing (first-call
+        setup such as kernel attributes must not happen inside a capture)."""
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            if attention_only:
+                self.run_attention()
+            elif from_host:
+                self.run_from_host()
+            else:
+                self.run()
+        torch.cuda.synchronize(self.device)
+        return graph
 
     # ------------------------------------------------------------------
     def attention_flops(self):
