@@ -226,6 +226,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Launched with programmatic dependent launch: the setup above overlaps
+  // the previous kernel's tail; nothing global is read before this point.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t tmem = sm.tmem_base;
   volatile int* abort = &sm.abort;
   const int total = p.blk_prefix[p.n_qtiles] * per_tile;
@@ -856,7 +859,19 @@ extern "C" int hsd_verify_attention(const void* q, int64_t q_row_stride, int64_t
   // stream-K: one CTA per SM sharing the total work evenly; otherwise one CTA
   // per (query tile, head pair) item.
   const int grid = split ? W.grid : W.items;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  attn::verify_attn_kernel<<<grid, attn::kThreads, smem, st>>>(tq, tk, tv, p);
-  return hsd_host::cuda_check(cudaGetLastError(), "verify_attn_kernel launch");
+  // Programmatic dependent launch: the CTAs may start their setup while the
+  // previous kernel on the stream finishes (griddepcontrol.wait in the
+  // kernel holds every read of global memory until it has completed).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(attn::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return hsd_host::cuda_check(cudaLaunchKernelEx(&cfg, attn::verify_attn_kernel, tq, tk, tv, p),
+                              "verify_attn_kernel launch");
 }
