@@ -400,6 +400,7 @@ def run_ours(args):
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
+            cpu_reference_step(page, rows=128)  # first-call setup of eager FlexAttention
             t, parts = cpu_reference_step(page)
             line["cpu_baseline"] = {
                 "value": page.verified_tokens / t, "unit": "tokens/s",
