@@ -128,12 +128,13 @@ class VerifyStep:
     def _ptr(self, t):
         return C.c_void_p(t.data_ptr())
 
-    def run(self, stream=None, attn_events=None, phase_events=None):
+    def run(self, stream=None, attn_events=None, phase_events=None, layer_ready=None):
         """Launch one verification step on ``stream`` (no host sync).
 
         ``attn_events[l]`` (start, end) bracket layer l's attention call;
         ``phase_events`` (dict of name -> (start, end)) bracket the phases
-        append / plan / accept / keep / compact / bits.
+        append / plan / accept / keep / compact / bits; layer l's attention
+        waits for ``layer_ready[l]`` (an event) when given.
         """
         lib = N.load()
         st = N.stream_handle(stream)
@@ -158,7 +159,7 @@ class VerifyStep:
             C.byref(self.plan.struct), p(self.status), st), "hsd_build_plan_segments")
         mark("plan", 1)
         # 3. attention, every layer
-        self.run_attention(stream, attn_events)
+        self.run_attention(stream, attn_events, layer_ready)
         # 4. acceptance + KMP
         mark("accept", 0)
         N.check(lib.hsd_accept_kmp(
@@ -184,10 +185,11 @@ class VerifyStep:
                 "hsd_compact_bits")
         mark("bits", 1)
 
-    def run_attention(self, stream=None, attn_events=None):
+    def run_attention(self, stream=None, attn_events=None, layer_ready=None):
         """The step's attention launches alone (every layer, current plan)."""
         lib = N.load()
         st = N.stream_handle(stream)
+        ts = stream if stream is not None else torch.cuda.current_stream()
         p = self._ptr
         scale = 1.0 / np.sqrt(self.d)
         ql, kvl, hq, hkv, d = self.q_len, self.kv_len, self.hq, self.hkv, self.d
@@ -195,6 +197,8 @@ class VerifyStep:
             q = self.q[l]
             k = self.cache[l, 0]
             v = self.cache[l, 1]
+            if layer_ready is not None:
+                ts.wait_event(layer_ready[l])
             if attn_events is not None:
                 attn_events[l][0].record(stream)
             N.check(lib.hsd_verify_attention(
@@ -233,15 +237,33 @@ class VerifyStep:
         return sum(h[k].numel() * h[k].element_size() for k in ("results", "counts"))
 
     def run_from_host(self, stream=None):
-        """End-to-end step: pinned host inputs -> device step -> results to host."""
+        """End-to-end step: pinned host inputs -> device step -> results to host.
+
+        The new K/V rows and token ids are copied on the compute stream (the
+        KV append needs all of them); Q, three quarters of the bytes, goes
+        layer by layer on a copy stream, each layer's attention waiting only
+        for its own Q, so the copies overlap the step's kernels.
+        """
         h = self.host_buffers()
-        self.q.copy_(h["q"], non_blocking=True)
-        self.new_kv.copy_(h["new_kv"], non_blocking=True)
-        self.input_ids.copy_(h["input_ids"], non_blocking=True)
-        self.next_ids.copy_(h["next_ids"], non_blocking=True)
-        self.run(stream)
-        h["results"].copy_(self.results, non_blocking=True)
-        h["counts"].copy_(self.counts, non_blocking=True)
+        cs = stream if stream is not None else torch.cuda.current_stream()
+        if getattr(self, "_copy_stream", None) is None:
+            self._copy_stream = torch.cuda.Stream(device=self.device)
+            self._q_ready = [torch.cuda.Event() for _ in range(self.L)]
+        xs = self._copy_stream
+        xs.wait_stream(cs)  # the previous step no longer reads q
+        with torch.cuda.stream(xs):
+            for l in range(self.L):
+                self.q[l].copy_(h["q"][l], non_blocking=True)
+                self._q_ready[l].record(xs)
+        with torch.cuda.stream(cs):
+            self.new_kv.copy_(h["new_kv"], non_blocking=True)
+            self.input_ids.copy_(h["input_ids"], non_blocking=True)
+            self.next_ids.copy_(h["next_ids"], non_blocking=True)
+        self.run(cs, layer_ready=self._q_ready)
+        cs.wait_stream(xs)
+        with torch.cuda.stream(cs):
+            h["results"].copy_(self.results, non_blocking=True)
+            h["counts"].copy_(self.counts, non_blocking=True)
 
     def capture(self, from_host=False, attention_only=False):
         """A CUDA graph of one whole step (``run`` or ``run_from_host``, or

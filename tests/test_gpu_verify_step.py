@@ -1,0 +1,116 @@
+"""GPU parity of a whole verification step (``VerifyStep``) against the oracle.
+
+One step of a small packed region page runs through the device path (KV
+append, tile plan, attention on every layer, acceptance + KMP, keep indices,
+in-place compaction, visibility remap) and is checked against the oracle's
+restatement of the same iteration: per-block pointer / increment / finished
+and the kept columns bit-exactly, the compacted caches bit-exactly against
+``index_select`` of the appended caches, attention within the tolerance of
+the attention tests.  The end-to-end form (pinned host buffers, Q copied
+layer by layer on a copy stream) and its CUDA-graph capture must give the
+same results as the device-resident form.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import accept as OA
+from oracle import attention as OAtt
+from oracle import compact as OC
+from oracle import masks as OM
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+
+
+@pytest.fixture(scope="module")
+def page():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    from hsd_b200 import _native
+    from hsd_b200 import workloads as W
+    _native.load()
+    return W.stage1_regions(seed=5, prefix=640, groups=3, drafts_per_group=2)
+
+
+def _step(page, seed=0):
+    from hsd_b200.verify_step import VerifyStep
+    return VerifyStep(page, device="cuda:0", seed=seed)
+
+
+def _oracle(page):
+    from hsd_b200.workloads import segment_dicts
+    allowed = OM.segments_to_allowed(page.q_len, page.kv_len, segment_dicts(page))
+    cfg = OA.StepConfig(pad_token_id=-1, eos_token_ids=(2**31 - 1,), tight_pack=True)
+    filt = np.zeros(page.kv_len, bool)
+    base = page.kv_len - page.q_len
+    nxt, ids = page.next_ids.tolist(), page.input_ids.tolist()
+    rows = []
+    for sg in page.segments:
+        st = OA.BlockState(mode=OA.SPEC, gen=list(sg.gen), draft=list(sg.draft), mws=3,
+                           matches_len=1, valid_count=sg.q_len)
+        ptr, _, inc, fin = OA.accept_block(st, sg.q_start, sg.q_start + sg.q_len, nxt, ids,
+                                           cfg, filt, base, lambda r: allowed[r], False)
+        rows.append((ptr, inc, int(bool(fin))))
+    active = [p for p, _, f in rows if not f]
+    keep = OC.keep_columns(allowed, active, filt)
+    return allowed, rows, OC.keep_indices(keep)
+
+
+def test_step_matches_oracle(page):
+    from hsd_b200.accept import R
+    s = _step(page)
+    appended = s.cache.clone()
+    appended[:, :, :, s.prefix:s.prefix + s.q_len] = s.new_kv
+    q = s.q.clone()
+    s.run()
+    torch.cuda.synchronize()
+    allowed, rows, idx = _oracle(page)
+
+    res = s.results.cpu().numpy()
+    got = [(int(r[R["pointer"]]), int(r[R["increment"]]), int(r[R["finished"]])) for r in res]
+    assert got == rows
+
+    n_keep, first = (int(x) for x in s.counts.cpu().tolist())
+    assert n_keep == len(idx)
+    moved = np.nonzero(idx != np.arange(len(idx)))[0]
+    assert first == (int(moved[0]) if len(moved) else n_keep)
+    it = torch.as_tensor(idx, device=appended.device)
+    assert torch.equal(s.cache[:, :, :, :n_keep], appended.index_select(3, it))
+
+    mask = torch.as_tensor(allowed)
+    for l in (0, page.layers - 1):
+        ref, _ = OAtt.attention_fp32(q[l].cpu(), appended[l, 0].cpu(), appended[l, 1].cpu(),
+                                     mask)
+        err = (s.out[l].float().cpu() - ref).abs()
+        assert err.max().item() <= MAX_ABS and err.mean().item() <= MEAN_ABS
+
+
+def _state(s):
+    torch.cuda.synchronize()
+    return [t.clone() for t in (s.results, s.counts, s.cache, s.out, s.lse, s.vis_next)]
+
+
+def test_from_host_and_graph_match_device_form(page):
+    a = _step(page)
+    a.run()
+    a.run()
+    want = _state(a)
+
+    b = _step(page)
+    b.run_from_host()
+    b.run_from_host()
+    h = b.host_buffers()
+    torch.cuda.synchronize()
+    assert torch.equal(h["results"], b.results.cpu())
+    assert torch.equal(h["counts"], b.counts.cpu())
+    for x, y in zip(want, _state(b)):
+        assert torch.equal(x, y)
+
+    c = _step(page)
+    c.run_from_host()
+    g = c.capture(from_host=True)
+    g.replay()
+    for x, y in zip(want, _state(c)):
+        assert torch.equal(x, y)
+    del g
