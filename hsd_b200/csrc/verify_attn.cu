@@ -687,28 +687,10 @@ using namespace hsd;
 
 namespace {
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn get_encode() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
-  return fn;
-}
-
 // [heads][rows][128] bf16 at element strides (row, head); box 64 x 128 rows x 1 head.
 int make_map(CUtensorMap* map, const void* base, int rows, int heads, int64_t row_stride,
              int64_t head_stride, const char* what) {
-  EncodeTiledFn enc = get_encode();
+  hsd_host::EncodeTiledFn enc = hsd_host::tensor_map_encoder();
   if (!enc) {
     hsd_host::set_error("cuTensorMapEncodeTiled unavailable");
     return HSD_ERR_CUDA;

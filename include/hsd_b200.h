@@ -265,6 +265,28 @@ int hsd_accept_kmp(const hsd_accept_config_t *cfg, hsd_block_t *blocks,
                    uint64_t *out_kv_bits, uint64_t *filter_bits, int32_t *status,
                    hsd_stream_t stream);
 
+/* ---- (5) next tokens: fused lm_head + argmax ------------------------------ */
+
+/* Workspace of hsd_lm_head_argmax: 8 bytes per row + 256, 256-byte aligned. */
+size_t hsd_lm_head_argmax_workspace_bytes(int32_t q_len);
+
+/* Next token of every packed row: argmax over the vocabulary of
+ * hidden[q_len, hidden_dim] . weight[vocab, hidden_dim]^T (bf16 in, fp32
+ * accumulation), each logit rounded to bf16 as the logits tensor holds it,
+ * ties to the lowest id.  Replaces `logits = lm_head(hidden)` followed by
+ * `logits.argmax(dim=-1)` (D:1057-1064) without writing the logits.  ids32
+ * and/or ids64 receive the ids (one may be NULL); max_logit (nullable) the
+ * maximal logit per row.  NaN logits never win (torch's argmax would return
+ * a NaN's index).  The workspace must be zero-filled before its first use;
+ * each call leaves it ready for the next (after an error status, zero it
+ * again), and calls sharing one must not overlap in time.  Pointers 16-byte
+ * aligned, row strides (elements) >= hidden_dim and multiples of 8. */
+int hsd_lm_head_argmax(const void *hidden, int64_t hidden_row_stride, const void *weight,
+                       int64_t weight_row_stride, int32_t q_len, int32_t vocab,
+                       int32_t hidden_dim, int32_t *ids32, int64_t *ids64, float *max_logit,
+                       void *workspace, size_t workspace_bytes, int32_t *status,
+                       hsd_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

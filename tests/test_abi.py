@@ -98,3 +98,22 @@ def test_other_entry_points_reject_null_arguments():
     assert lib.hsd_build_plan_segments(None, 0, None, None, 0, None, C.byref(plan),
                                        None, None) != 0
     assert lib.hsd_build_plan_dense(None, 0, C.byref(plan), None, None) != 0
+
+
+def test_lm_head_argmax_host_checks():
+    lib = N.load()
+    assert lib.hsd_lm_head_argmax_workspace_bytes(0) == 0
+    assert lib.hsd_lm_head_argmax_workspace_bytes(2176) == 2176 * 8 + 256
+    # no id output / unaligned pointer / stride below hidden_dim: rejected on the host
+    assert lib.hsd_lm_head_argmax(C.c_void_p(256), 1536, C.c_void_p(256), 1536, 4, 100, 1536,
+                                  None, None, None, None, 0, None, None) != 0
+    assert b"bad arguments" in lib.hsd_last_error()
+    assert lib.hsd_lm_head_argmax(C.c_void_p(8), 1536, C.c_void_p(256), 1536, 4, 100, 1536,
+                                  C.c_void_p(256), None, None, None, 0, None, None) != 0
+    assert lib.hsd_lm_head_argmax(C.c_void_p(256), 1000, C.c_void_p(256), 1536, 4, 100, 1536,
+                                  C.c_void_p(256), None, None, None, 0, None, None) != 0
+    # too small a workspace
+    assert lib.hsd_lm_head_argmax(C.c_void_p(256), 1536, C.c_void_p(256), 1536, 4, 100, 1536,
+                                  C.c_void_p(256), None, None, C.c_void_p(256), 64, None,
+                                  None) != 0
+    assert b"workspace" in lib.hsd_last_error()
