@@ -237,6 +237,49 @@ def run_reference(args):
 
 
 # ---------------------------------------------------------------- GPU side
+def measure_next_tokens(page, dev, steps, warmup, seed=0):
+    """Fused lm_head + argmax on the page's packed rows (hidden = Hq x head
+    dim: 1536, the dots.ocr decoder's, on the stage-1 workload; the
+    151,936-token vocabulary), against the reference's two ops on the same
+    device: ``F.linear`` (cuBLAS bf16, fp32 accumulation, bf16 logits)
+    then ``argmax(-1)``.  The weight (467 MB) exceeds L2, so no flush."""
+    import torch
+
+    from hsd_b200.lm_head import lm_head_argmax
+    from hsd_b200.workloads import VOCAB
+
+    q, hd = page.q_len, page.hq * page.head_dim
+    g = torch.Generator(device=dev).manual_seed(1000 + seed)
+    h = torch.randn(q, hd, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn(VOCAB, hd, generator=g, device=dev) / hd ** 0.5).to(torch.bfloat16)
+    out = torch.empty(q, dtype=torch.int64, device=dev)
+    n = max(5, min(steps, 50))
+
+    def timed(fn):
+        for _ in range(max(3, warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    ours_ms = timed(lambda: lm_head_argmax(h, w, out=out))
+    ref_ms = timed(lambda: torch.nn.functional.linear(h, w).argmax(-1))
+    agree = float((out == torch.nn.functional.linear(h, w).argmax(-1)).float().mean())
+    flops = 2.0 * q * VOCAB * hd
+    del h, w
+    return {"kernel": "lm_head_argmax_kernel", "rows": q, "hidden": hd, "vocab": VOCAB,
+            "launches": n, "ms": ours_ms, "tflops": flops / (ours_ms * 1e-3) / 1e12,
+            "torch_linear_argmax_ms": ref_ms, "speedup_vs_torch": ref_ms / ours_ms,
+            "ids_agree_with_torch": agree,
+            "logits_bytes_not_written": q * VOCAB * 2}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -351,6 +394,8 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
 
+    next_tokens = measure_next_tokens(page, dev, args.steps, args.warmup, seed=rank)
+
     tokens = float(page.verified_tokens)
     stats = torch.tensor([ms, e2e_ms, tokens], dtype=torch.float64, device=dev)
     if world > 1:
@@ -398,6 +443,8 @@ def run_ours(args):
                            / peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])},
             "gpu_launches": args.steps * step.kernel_launches_per_step,
             "clocks": clocks,
+            "next_tokens": dict(next_tokens, peak_tflops=peak,
+                                frac=next_tokens["tflops"] / peak),
         }
         if world == 1 and not args.no_cpu_baseline:
             cpu_reference_step(page, rows=128)  # first-call setup of eager FlexAttention
