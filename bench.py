@@ -280,6 +280,78 @@ def measure_next_tokens(page, dev, steps, warmup, seed=0):
             "logits_bytes_not_written": q * VOCAB * 2}
 
 
+def measure_rope_append(page, dev, steps, warmup, seed=0):
+    """Fused RoPE + cache update of one step's new rows on every layer,
+    against the reference's ops on the same device: transformers'
+    ``apply_rotary_pos_emb`` on the query / key states and ``torch.cat`` of
+    key and value states onto the layer cache (DynamicCache.update).  q / k /
+    v are column slices of one fused projection output; the cache holds the
+    page prefix and receives the step's rows after it."""
+    import torch
+    from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
+
+    from hsd_b200.rope import rope_append
+
+    n, hq, hkv, L = page.q_len, page.hq, page.hkv, page.layers
+    g = torch.Generator(device=dev).manual_seed(2000 + seed)
+    qkv = torch.randn(L, n, (hq + 2 * hkv) * 128, generator=g, device=dev).to(torch.bfloat16)
+    pos = torch.arange(page.prefix, page.prefix + n, device=dev).float()
+    inv = 1.0 / 1e6 ** (torch.arange(0, 128, 2, device=dev).float() / 128)
+    emb = torch.cat([pos[:, None] * inv, pos[:, None] * inv], dim=-1)
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    kc = torch.zeros(L, hkv, page.kv_len, 128, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    prev_k = torch.randn(L, 1, hkv, page.prefix, 128, generator=g, device=dev).to(torch.bfloat16)
+    prev_v = torch.randn_like(prev_k)
+    a, b = hq * 128, (hq + hkv) * 128
+    n_iter = max(5, min(steps, 50))
+
+    def ours():
+        for l in range(L):
+            rope_append(qkv[l, :, :a], qkv[l, :, a:b], qkv[l, :, b:], cos, sin, kc[l], vc[l],
+                        page.prefix)
+
+    def ref():
+        for l in range(L):
+            q4 = qkv[l, :, :a].reshape(1, n, hq, 128).transpose(1, 2)
+            k4 = qkv[l, :, a:b].reshape(1, n, hkv, 128).transpose(1, 2)
+            v4 = qkv[l, :, b:].reshape(1, n, hkv, 128).transpose(1, 2)
+            qe, ke = apply_rotary_pos_emb(q4, k4, cos[None], sin[None])
+            torch.cat([prev_k[l], ke], dim=-2)
+            torch.cat([prev_v[l], v4], dim=-2)
+
+    def timed(fn):
+        # both paths as CUDA graphs of their per-layer launches, so the
+        # device time is measured rather than Python's per-call overhead
+        fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        for _ in range(max(3, warmup)):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n_iter):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del graph
+        return e0.elapsed_time(e1) / n_iter
+
+    ours_ms, ref_ms = timed(ours), timed(ref)
+    per_row = hq * 256 * 2 + hkv * 256 * 2 * 2 + 2 * 256  # q r/w, k and v r/w, cos + sin
+    algo = n * per_row
+    return {"kernel": "rope_append_kernel", "rows": n, "layers": L, "launches_per_step": L,
+            "timing": "CUDA graph of the 28 per-layer launches (both paths)",
+            "ms_all_layers": ours_ms, "us_per_launch": ours_ms * 1e3 / L,
+            "bytes_per_launch": algo,
+            "achieved_gbs": algo / (ours_ms * 1e-3 / L) / 1e9,
+            "torch_rope_cat_ms_all_layers": ref_ms, "speedup_vs_torch": ref_ms / ours_ms}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -395,6 +467,7 @@ def run_ours(args):
     e2e_ms = e0.elapsed_time(e1) / args.steps
 
     next_tokens = measure_next_tokens(page, dev, args.steps, args.warmup, seed=rank)
+    rope = measure_rope_append(page, dev, args.steps, args.warmup, seed=rank)
 
     tokens = float(page.verified_tokens)
     stats = torch.tensor([ms, e2e_ms, tokens], dtype=torch.float64, device=dev)
@@ -445,6 +518,9 @@ def run_ours(args):
             "clocks": clocks,
             "next_tokens": dict(next_tokens, peak_tflops=peak,
                                 frac=next_tokens["tflops"] / peak),
+            "rope_append": dict(rope, peak_gbs=peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]),
+                                frac=rope["achieved_gbs"]
+                                / peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
         }
         if world == 1 and not args.no_cpu_baseline:
             cpu_reference_step(page, rows=128)  # first-call setup of eager FlexAttention

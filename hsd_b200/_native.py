@@ -88,6 +88,9 @@ SIGNATURES = [
     ("hsd_compact_bits", C.c_int, [_P, _P, _I32, _I32, _P, _P, _I32, _P]),
     ("hsd_accept_kmp", C.c_int,
      [C.POINTER(AcceptConfig), _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    ("hsd_rope_append", C.c_int,
+     [_P, _I64, _P, _P, _I64, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _I64,
+      _I32, _P]),
     ("hsd_lm_head_argmax_workspace_bytes", _SZ, [_I32]),
     ("hsd_lm_head_argmax", C.c_int,
      [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _SZ, _P, _P]),

@@ -247,6 +247,25 @@ int hsd_compact_bits(const uint64_t *in_bits, uint64_t *out_bits, int32_t n_rows
                      int32_t stride, const int32_t *keep_idx, const int32_t *counts,
                      int32_t out_words, hsd_stream_t stream);
 
+/* Rotary position embedding + cache update of one layer's new rows, one
+ * launch.  Replaces transformers' apply_rotary_pos_emb on the query and key
+ * states (D:345-346) and the DynamicCache.update torch.cat (D:348-351).
+ * q: [n_rows][num_q_heads][128] bf16 at q_row_stride (the q_proj output),
+ * rotated in place; k, v: [n_rows][num_kv_heads][128] at kv_row_stride (read
+ * only); cos_emb, sin_emb: [n_rows][128] bf16 at cs_row_stride (the model's
+ * position embeddings).  Rotated k rows and v rows go to rows
+ * [dst_row0, dst_row0 + n_rows) of the caches (head h at
+ * cache + h * head_stride, rows at cache_row_stride).  Arithmetic as torch's
+ * bf16 ops: y = bf16(bf16(x * cos) + bf16(rotate_half(x) * sin)), so the
+ * result is bit-identical.  num_q_heads may be 0 (keys and values only).
+ * All strides in elements, multiples of 8; pointers 16-byte aligned. */
+int hsd_rope_append(void *q, int64_t q_row_stride, const void *k, const void *v,
+                    int64_t kv_row_stride, const void *cos_emb, const void *sin_emb,
+                    int64_t cs_row_stride, int32_t n_rows, int32_t num_q_heads,
+                    int32_t num_kv_heads, int32_t head_dim, void *k_cache,
+                    int64_t k_cache_head_stride, void *v_cache, int64_t v_cache_head_stride,
+                    int64_t cache_row_stride, int32_t dst_row0, hsd_stream_t stream);
+
 /* ---- (3) acceptance + KMP re-alignment ----------------------------------- */
 
 /* One warp per block: acceptance by mode (D:1107-1293, H:1633-1858 at

@@ -117,3 +117,20 @@ def test_lm_head_argmax_host_checks():
                                   C.c_void_p(256), None, None, C.c_void_p(256), 64, None,
                                   None) != 0
     assert b"workspace" in lib.hsd_last_error()
+
+
+def test_rope_append_host_checks():
+    lib = N.load()
+    a = C.c_void_p(256)
+    # head_dim other than 128
+    assert lib.hsd_rope_append(a, 1536, a, a, 256, a, a, 128, 4, 12, 2, 64, a, 4096, a, 4096,
+                               128, 0, None) == N.HSD_OK + 2
+    # unaligned key pointer, then a row stride too small for the heads
+    assert lib.hsd_rope_append(a, 1536, C.c_void_p(258), a, 256, a, a, 128, 4, 12, 2, 128, a,
+                               4096, a, 4096, 128, 0, None) != 0
+    assert lib.hsd_rope_append(a, 1000, a, a, 256, a, a, 128, 4, 12, 2, 128, a, 4096, a, 4096,
+                               128, 0, None) != 0
+    assert b"bad arguments" in lib.hsd_last_error()
+    # zero rows: nothing to do, no launch
+    assert lib.hsd_rope_append(a, 1536, a, a, 256, a, a, 128, 0, 12, 2, 128, a, 4096, a, 4096,
+                               128, 0, None) == 0
