@@ -20,7 +20,11 @@ The target model stays outside: :meth:`VerifyLoop.inputs` gives the packed
 tile plan is what :func:`hsd_b200.attention.flex_attention_forward`
 consumes), and :meth:`VerifyLoop.step` takes the model's argmax per packed
 row.  With ``enable_tree_decode`` a block without exactly one KMP match
-proposes its draft's continuation tree (:mod:`hsd_b200.trie`, D:1488-1543).
+proposes its draft's continuation tree (D:1488-1543), built and packed on the
+device for all such blocks in one launch (:mod:`hsd_b200.trie`); the tree's
+node arrays feed the next acceptance kernel and its ancestor rows the next
+mask without a host copy, and only tokens and depths come back to pack the
+input.
 Not driven by this loop: tight packing (HSD_TIGHT_PACK) and the page block's
 tokenizer-driven parsers.
 """
@@ -36,7 +40,7 @@ from . import _native as N
 from .accept import DOTS_SENTINEL, F, R, accept_kmp, make_config
 from .compaction import compact_bits, compact_kv, keep_indices
 from .plan import SEG_CAUSAL, SEG_NONE, SEG_SINGLE, SEG_TREE, PackedMask, pack_bits
-from .trie import continuation_tree
+from .trie import continuation_trees
 
 
 class VerifyLoop:
@@ -93,7 +97,8 @@ class VerifyLoop:
         self.q_start = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
         self.q_len = np.asarray(lens, dtype=np.int64)
         self.kinds = [SEG_CAUSAL] * self.nb
-        self.trees = [None] * self.nb                # (tokens, parents) of TREE blocks
+        self.trees = None                            # device trees of this step's TREE blocks
+        self.tree_slot = [-1] * self.nb              # row of block b in self.trees
         self.modes = [N.HSD_MODE_NORMAL] * self.nb   # D:978
         # non-pad rows per block (the reference counts them while
         # block_valid_counts is None, D:1108-1111)
@@ -117,6 +122,8 @@ class VerifyLoop:
             blocks[b, F["mws"]] = self.mws0
             blocks[b, F["seg"]] = b
             doff += len(self.drafts[b])
+        self.d_draft_off = torch.from_numpy(blocks[:, F["draft_off"]].copy()).to(dev)
+        self.d_draft_len = torch.from_numpy(blocks[:, F["draft_len"]].copy()).to(dev)
         self.blocks = torch.from_numpy(blocks).to(dev)
         self.draft_pool = torch.tensor(sum(self.drafts, []) or [0], dtype=torch.int32, device=dev)
         self.gen_pool = torch.zeros(self.nb * cap, dtype=torch.int32, device=dev)
@@ -141,22 +148,18 @@ class VerifyLoop:
                 segs[b, :3] = (qs, ql, self.kinds[b])
                 row_seg[qs:qs + ql] = b
                 if self.kinds[b] == SEG_TREE:
-                    # node i sees itself and its ancestors (D:1506-1533); pad rows nothing
+                    # node i sees itself and its ancestors (D:1506-1533), rows
+                    # from the tree kernel; pad rows see nothing
                     tw = (ql + 63) // 64
-                    anc = np.zeros((ql, tw * 64), dtype=bool)
-                    parents = self.trees[b][1]
-                    for i in range(len(parents)):
-                        a = i
-                        while a >= 0:
-                            anc[i, a] = True
-                            a = parents[a]
-                    tree_rows.append(pack_bits(anc).reshape(-1))
+                    i = self.tree_slot[b]
+                    n = int(self.valid[b])
+                    rows = torch.zeros((ql, tw), dtype=torch.int64, device=self.device)
+                    w = min(tw, self.trees.anc.shape[2])
+                    rows[:n, :w] = self.trees.anc[i, :n, :w]
+                    tree_rows.append(rows.reshape(-1))
                     segs[b, 3], segs[b, 4] = tree_off, tw
                     tree_off += ql * tw
-            tree_bits = None
-            if tree_rows:
-                tree_bits = torch.from_numpy(np.concatenate(tree_rows).view(np.int64)).to(
-                    self.device)
+            tree_bits = torch.cat(tree_rows) if tree_rows else None
             self._mask = PackedMask.from_bits(q, self.kv_len, segs, row_seg, self.seg_bits,
                                               self.device, tree_bits)
         ids = torch.from_numpy(self.input_ids.astype(np.int32)).to(self.device)
@@ -182,18 +185,18 @@ class VerifyLoop:
         self.blocks[:, F["q_start"]] = upd[:, 1]
         self.blocks[:, F["q_len"]] = upd[:, 2]
         self.blocks[:, F["valid_count"]] = upd[:, 3]
-        tree_tok, tree_par, toff = [], [], np.zeros(self.nb, dtype=np.int32)
+        toff = np.zeros(self.nb, dtype=np.int32)
         tnodes = np.zeros(self.nb, dtype=np.int32)
-        for b in range(self.nb):
-            if self.modes[b] == N.HSD_MODE_TREE:
-                toff[b], tnodes[b] = len(tree_tok), len(self.trees[b][0])
-                tree_tok += self.trees[b][0]
-                tree_par += self.trees[b][1]
-        if tree_tok:
+        d_tok = d_par = torch.zeros(1, dtype=torch.int32, device=dev)
+        if self.trees is not None:
+            # this step's tree blocks read their nodes straight from the tree kernel's rows
+            for b in range(self.nb):
+                if self.modes[b] == N.HSD_MODE_TREE:
+                    toff[b] = self.tree_slot[b] * self.trees.cap
+                    tnodes[b] = self.valid[b]
             self.blocks[:, F["tree_off"]] = torch.from_numpy(toff).to(dev)
             self.blocks[:, F["tree_nodes"]] = torch.from_numpy(tnodes).to(dev)
-        d_tok = torch.tensor(tree_tok or [0], dtype=torch.int32, device=dev)
-        d_par = torch.tensor(tree_par or [0], dtype=torch.int32, device=dev)
+            d_tok, d_par = self.trees.tokens.reshape(-1), self.trees.parents.reshape(-1)
         self.filter.zero_()
         self.out_bits.zero_()
         cfg = make_config(self.nb, kv, q, self.stride, self.eos, self.mws0, self.mws_ub,
@@ -206,10 +209,26 @@ class VerifyLoop:
         res = self.results.cpu().numpy()
         self._check()
 
+        # continuation trees of the blocks without exactly one match, one launch
+        want = [b for b in range(self.nb)
+                if self.tree_decode and self.modes[b] != N.HSD_MODE_FINISHED
+                and not res[b][R["finished"]] and res[b][R["match_count"]] != 1]
+        new_trees, new_slot, host_trees = None, [-1] * self.nb, {}
+        if want:
+            idx = torch.tensor(want, dtype=torch.long, device=dev)
+            new_trees = continuation_trees(
+                self.draft_pool, self.d_draft_off[idx].contiguous(),
+                self.d_draft_len[idx].contiguous(),
+                self.results[idx, R["next_token"]].contiguous(), self.tree_depth,
+                self.tree_cap, status=self.status)
+            for i, (b, tree) in enumerate(zip(want, new_trees.host())):
+                host_trees[b] = tree
+                new_slot[b] = i
+            self._check()
+
         # next inputs (D:1421-1565) from the result rows
         new_ids, new_pos, new_lens = [], [], [0] * self.nb
         new_modes, new_valid, new_kinds = list(self.modes), [0] * self.nb, list(self.kinds)
-        new_trees = [None] * self.nb
         for b in range(self.nb):
             if self.modes[b] == N.HSD_MODE_FINISHED:
                 new_kinds[b] = SEG_NONE   # no rows any more
@@ -227,18 +246,14 @@ class VerifyLoop:
                 new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_SPEC, SEG_CAUSAL, n
                 pos = list(range(base, base + len(toks)))
             else:
-                tree = None
-                if self.tree_decode:
-                    tree = continuation_tree(self.drafts[b], int(r[R["next_token"]]),
-                                             self.tree_depth, self.tree_cap)
+                tree = host_trees.get(b)
                 if tree is not None and len(tree[0]) > 1:    # D:1488-1543
-                    tokens, depths, parents = tree
+                    tokens, depths, _ = tree
                     n = len(tokens)
                     pad_n = math.ceil(n / self.mil) * self.mil - n
                     toks = list(tokens) + [self.pad] * pad_n
                     pos = [d + base for d in depths] + [0] * pad_n
                     new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_TREE, SEG_TREE, n
-                    new_trees[b] = (list(tokens), list(parents))
                 else:                                        # D:1544-1565
                     toks = [int(r[R["next_token"]])] + [self.pad] * (self.mil - 1)
                     pos = [base] + [0] * (self.mil - 1)
@@ -290,7 +305,7 @@ class VerifyLoop:
         self.q_len = np.asarray(new_lens, dtype=np.int64)
         self.q_start = ends - self.q_len
         self.modes, self.valid, self.kinds = new_modes, new_valid, new_kinds
-        self.trees = new_trees
+        self.trees, self.tree_slot = new_trees, new_slot
         self.kv_len = kv + int(self.input_ids.size)
         if self.kv_len > self.kv_cap:
             raise N.HSDError(f"KV columns {self.kv_len} exceed the loop's capacity {self.kv_cap}")

@@ -284,6 +284,23 @@ int hsd_accept_kmp(const hsd_accept_config_t *cfg, hsd_block_t *blocks,
                    uint64_t *out_kv_bits, uint64_t *filter_bits, int32_t *status,
                    hsd_stream_t stream);
 
+/* Continuation tries of tree decoding, one CTA per tree.  Tree i: the draft
+ * draft_pool[draft_off[i] .. + draft_len[i]) and the root token
+ * last_tokens[i] (the match window's last token).  After every draft
+ * position p holding the root token the next min(max_depth, len - 1 - p)
+ * draft tokens are inserted (kmp_search's trie, D:573-586; children in
+ * insertion order) and the trie is packed breadth-first, at most cap nodes
+ * (D:1488-1543).  Outputs, row i at i * cap: tokens, depths, parents (-1
+ * for the root) and counts[i] nodes; anc_bits[i][node][ceil(cap / 64)]: the
+ * node and its ancestors, the tree's attention-mask rows (D:1506-1533).
+ * cap <= 1024; more than 2048 root occurrences in one draft sets
+ * HSD_DEV_CAPACITY and counts[i] = 0. */
+int hsd_continuation_trees(const int32_t *draft_pool, const int32_t *draft_off,
+                           const int32_t *draft_len, const int32_t *last_tokens,
+                           int32_t n_trees, int32_t max_depth, int32_t cap, int32_t *tokens,
+                           int32_t *depths, int32_t *parents, int32_t *counts,
+                           uint64_t *anc_bits, int32_t *status, hsd_stream_t stream);
+
 /* ---- (5) next tokens: fused lm_head + argmax ------------------------------ */
 
 /* Workspace of hsd_lm_head_argmax: 8 bytes per row + 256, 256-byte aligned. */

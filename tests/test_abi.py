@@ -134,3 +134,14 @@ def test_rope_append_host_checks():
     # zero rows: nothing to do, no launch
     assert lib.hsd_rope_append(a, 1536, a, a, 256, a, a, 128, 0, 12, 2, 128, a, 4096, a, 4096,
                                128, 0, None) == 0
+
+
+def test_continuation_trees_host_checks():
+    lib = N.load()
+    a = C.c_void_p(256)
+    args = [a, a, a, a, 3, 15]
+    assert lib.hsd_continuation_trees(*args, 0, a, a, a, a, a, None, None) != 0      # cap 0
+    assert lib.hsd_continuation_trees(*args, 1025, a, a, a, a, a, None, None) != 0   # cap > 1024
+    assert b"cap" in lib.hsd_last_error()
+    assert lib.hsd_continuation_trees(None, None, None, None, 0, 15, 256, None, None, None, None,
+                                      None, None, None) == 0                        # nothing to do

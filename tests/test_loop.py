@@ -89,18 +89,3 @@ def test_batch_generate_returns_true_texts():
     assert gen == ref_gen
     assert decode_times == len(trace)
     assert len(timings) == 8 and timings[6] == decode_times - 1
-
-
-@pytest.mark.parametrize("seed", range(12))
-def test_continuation_tree_matches_oracle_trie(seed):
-    """hsd_b200.trie packs the same tree as the reference's KMP trie + BFS."""
-    from hsd_b200.trie import continuation_tree
-    from oracle import kmp as OK
-    rng = np.random.default_rng(seed)
-    draft = [int(x) for x in rng.integers(1, 6 + seed, int(rng.integers(5, 200)))]
-    gen = [int(x) for x in rng.integers(1, 6 + seed, int(rng.integers(1, 12)))]
-    depth = int(rng.integers(1, 16))
-    cap = int(rng.integers(1, 300))
-    window = gen[-min(10, len(gen)):]
-    trie, _ = OK.find_all_matches_kmp([draft], window, OK.compute_lps(window), depth)
-    assert continuation_tree(draft, window[-1], depth, cap) == OK.trie_bfs(trie, cap)
