@@ -352,6 +352,48 @@ def measure_rope_append(page, dev, steps, warmup, seed=0):
             "torch_rope_cat_ms_all_layers": ref_ms, "speedup_vs_torch": ref_ms / ours_ms}
 
 
+def measure_trees(page, dev, steps, warmup, depth=15, cap=256):
+    """Continuation trees of every block of the page in one launch (root =
+    the block's last generated token), against the oracle's restatement of
+    the reference's host code (kmp_search's trie insertion + BFS packing,
+    D:573-586, D:1488-1543) on one host core."""
+    import torch
+
+    from hsd_b200.trie import continuation_trees
+    from oracle import kmp as OK
+
+    drafts = [list(map(int, sg.draft)) for sg in page.segments]
+    roots = [int(sg.gen[-1]) if len(sg.gen) else int(sg.draft[0]) for sg in page.segments]
+    off = np.cumsum([0] + [len(d) for d in drafts[:-1]]).tolist()
+    t = lambda x: torch.tensor(x, dtype=torch.int32, device=dev)
+    pool, d_off, d_len, d_root = t(sum(drafts, [])), t(off), t([len(d) for d in drafts]), \
+        t(roots)
+    n = max(5, min(steps, 100))
+    for _ in range(max(3, warmup)):
+        continuation_trees(pool, d_off, d_len, d_root, depth, cap)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        trees = continuation_trees(pool, d_off, d_len, d_root, depth, cap)
+    e1.record()
+    torch.cuda.synchronize()
+    dev_ms = e0.elapsed_time(e1) / n
+    got = trees.host()
+    t0 = time.perf_counter()
+    want = []
+    for d, r in zip(drafts, roots):
+        trie, _ = OK.find_all_matches_kmp([d], [r], OK.compute_lps([r]), depth)
+        want.append(OK.trie_bfs(trie, cap))
+    cpu_ms = (time.perf_counter() - t0) * 1e3
+    same = all(g == (list(w[0]), list(w[1]), list(w[2])) for g, w in zip(got, want))
+    return {"kernel": "trie_kernel", "trees": len(drafts), "depth": depth, "cap": cap,
+            "nodes": int(sum(len(g[0]) for g in got)), "ms": dev_ms,
+            "host_python_ms": cpu_ms, "equal_to_oracle": same,
+            "timing": "CUDA events around back-to-back launches (includes the launch)"}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -468,6 +510,7 @@ def run_ours(args):
 
     next_tokens = measure_next_tokens(page, dev, args.steps, args.warmup, seed=rank)
     rope = measure_rope_append(page, dev, args.steps, args.warmup, seed=rank)
+    trees = measure_trees(page, dev, args.steps, args.warmup)
 
     tokens = float(page.verified_tokens)
     stats = torch.tensor([ms, e2e_ms, tokens], dtype=torch.float64, device=dev)
@@ -518,6 +561,7 @@ def run_ours(args):
             "clocks": clocks,
             "next_tokens": dict(next_tokens, peak_tflops=peak,
                                 frac=next_tokens["tflops"] / peak),
+            "trees": trees,
             "rope_append": dict(rope, peak_gbs=peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]),
                                 frac=rope["achieved_gbs"]
                                 / peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
