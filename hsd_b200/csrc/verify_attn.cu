@@ -411,20 +411,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int h = pc.h0 + s;
       const uint32_t* list = p.blk_list + size_t(qt) * p.n_kv128;
       float m = -INFINITY, l = 0.f;
-      for (int j = pc.b0; j < pc.b1 && ok; ++j) {
-        const uint32_t e = list[j];
+      // Mask words of a block: absent half = 0, full half = ~0, partial half =
+      // this row's word.  Block j + 1's list entry and words are fetched
+      // during block j, so no global-load latency sits on the block chain.
+      const uint64_t* mrow = p.mask_words + size_t(qt) * p.n_kv64 * 128 + r;
+      auto load_words = [&](uint32_t e, uint64_t (&wd)[2]) {
         const int kb = int(e & 0xFFFFFFu);
-        // mask words: absent half = 0, full half = ~0, partial half = its row word
-        uint32_t mw[4];
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
-          const bool present = (e >> (24 + 2 * hf)) & 1u;
-          const bool partial = (e >> (25 + 2 * hf)) & 1u;
-          uint64_t wd = present ? ~0ull : 0ull;
-          if (partial) wd = p.mask_words[(size_t(qt) * p.n_kv64 + 2 * kb + hf) * 128 + r];
-          mw[2 * hf] = uint32_t(wd);
-          mw[2 * hf + 1] = uint32_t(wd >> 32);
+          wd[hf] = ((e >> (24 + 2 * hf)) & 1u) ? ~0ull : 0ull;
+          if ((e >> (25 + 2 * hf)) & 1u) wd[hf] = mrow[size_t(2 * kb + hf) * 128];
         }
+      };
+      uint32_t e_next = pc.b0 < pc.b1 ? list[pc.b0] : 0u;
+      uint64_t wd_next[2];
+      load_words(e_next, wd_next);
+      for (int j = pc.b0; j < pc.b1 && ok; ++j) {
+        uint32_t mw[4] = {uint32_t(wd_next[0]), uint32_t(wd_next[0] >> 32), uint32_t(wd_next[1]),
+                          uint32_t(wd_next[1] >> 32)};
+        if (j + 1 < pc.b1) e_next = list[j + 1];
         ok = __all_sync(0xffffffffu, mbar_wait(&sm.bar_s_full[s], uint32_t(gs) & 1u, abort,
                                                p.status, 0x300 + s));
         if (!ok) break;
@@ -498,6 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                  p.status, 0x312 + s));
           if (!ok) break;
         }
+        if (j + 1 < pc.b1) load_words(e_next, wd_next);
         // When both slots are active their exponential phases take turns on
         // the MUFU (slot 0 first): each slot's max / load / wait phases then
         // run under the other slot's exponentials instead of in lockstep.
