@@ -160,17 +160,6 @@ __device__ __forceinline__ void umma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, u
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
-// D[tmem] (+)= A[tmem] * B[smem desc]: A (M x 16 bf16) is read from tensor
-// memory, one row per lane, two bf16 per 32-bit column (lower k in the low half).
-__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                             uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
-}
-
 // Arrive on `bar` once every tcgen05 async operation this thread issued so
 // far has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -233,14 +222,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 // the loaded values after the wait.
 __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" : HSD_RW32(r)::"memory");
-}
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, "
-      "%10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, "
-      "%27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      HSD_IN32(r)
-      : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -351,12 +332,6 @@ __device__ __forceinline__ void fence_acq_rel_gpu() {
   asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 
-// Orders this thread's generic-proxy view of global memory before its later
-// async-proxy (bulk copy) reads of it.
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
 // Untiled bulk copy global -> this CTA's shared memory, completion counted in
 // bytes on `bar` (16-byte aligned addresses, size a multiple of 16).
 __device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint32_t bytes,
@@ -366,13 +341,6 @@ __device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint3
       ::"r"(smem_u32(dst_smem)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes),
       "r"(smem_u32(bar))
       : "memory");
-}
-
-__device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t (&v)[4]) {
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
-               : "r"(addr)
-               : "memory");
 }
 
 // Bounded wait until *flag == value (another CTA of the same launch sets it

@@ -184,10 +184,6 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_smem, uint3
   }
 }
 
-__device__ __forceinline__ void slot_barrier(int s) {
-  asm volatile("bar.sync %0, 128;" ::"r"(1 + s) : "memory");
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
     verify_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
