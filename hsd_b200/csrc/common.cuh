@@ -328,8 +328,36 @@ __device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t* p) {
   return v;
 }
 
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void fence_acq_rel_gpu() {
   asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
+// 3-D tiled bulk tensor store shared -> global (rows past the tensor's
+// extent are not written), tracked by this thread's bulk async-group.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0,
+                                             int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until every committed bulk store of this thread has read its shared memory.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until every committed bulk store of this thread has completed.
+__device__ __forceinline__ void bulk_wait_group0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // Untiled bulk copy global -> this CTA's shared memory, completion counted in
@@ -345,17 +373,19 @@ __device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint3
 
 // Bounded wait until *flag == value (another CTA of the same launch sets it
 // with st_release_u32), polling with relaxed loads: the caller issues
-// fence_acq_rel_gpu() after its last flag before reading the flagged data.
+// fence_acq_rel_gpu() after its last flag before reading the flagged data, or
+// polls with acquire loads (acquire = true) and needs no fence.
 // Gives up like mbar_wait: on abort, on another error in status after
 // kSlowCheckNs, or after kWaitLimitNs (HSD_DEV_TIMEOUT | where).
 __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t value,
-                                          volatile int* abort, int32_t* status, int32_t where) {
-  if (ld_relaxed_u32(flag) == value) return true;
+                                          volatile int* abort, int32_t* status, int32_t where,
+                                          bool acquire = false) {
+  if ((acquire ? ld_acquire_u32(flag) : ld_relaxed_u32(flag)) == value) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
-      if (ld_relaxed_u32(flag) == value) return true;
+      if ((acquire ? ld_acquire_u32(flag) : ld_relaxed_u32(flag)) == value) return true;
     if (*abort) return false;
     const uint64_t dt = globaltimer_ns() - t0;
     if (dt < kSlowCheckNs) continue;

@@ -85,6 +85,8 @@ struct __align__(1024) Smem {
   uint64_t bar_o_free[NSLOT];
   uint64_t bar_mufu[NSLOT];  // exponential phases alternate between the slots
   uint64_t bar_final[NSLOT];
+  uint64_t bar_ostage[NSLOT];  // the slot's O rows are staged in its P buffer
+  uint64_t bar_ofree[NSLOT];   // their bulk stores have read the buffer
   uint32_t tmem_base;
   int abort;
 };
@@ -187,7 +189,8 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_smem, uint3
 __global__ void __launch_bounds__(kThreads, 1)
     verify_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v, const Params p) {
+                       const __grid_constant__ CUtensorMap tm_v,
+                       const __grid_constant__ CUtensorMap tm_o, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                       ~uintptr_t(1023));
@@ -211,7 +214,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.bar_o_free[i], 128);
       mbar_init(&sm.bar_mufu[i], 128);
     }
-    for (int i = 0; i < NSLOT; ++i) mbar_init(&sm.bar_final[i], 1);
+    for (int i = 0; i < NSLOT; ++i) {
+      mbar_init(&sm.bar_final[i], 1);
+      mbar_init(&sm.bar_ostage[i], 128);
+      mbar_init(&sm.bar_ofree[i], 1);
+    }
     sm.abort = 0;
     fence_barrier_init();
   }
@@ -396,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t t_s = tmem + lane_off + s * 256;
     const uint32_t t_o = t_s + 128;
     int gs = 0;  // blocks this slot has processed (barrier parity)
+    int fo = 0;  // final outputs this slot has stored (barrier parity)
     int hs = 0;  // blocks with both slots active (exponential-phase handshakes)
     bool ok = true;
     int w = w0;
@@ -605,48 +613,73 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = blockIdx.x + 1; k <= khi && ok; ++k) {
           if (range_start(k + 1, total, G) == range_start(k, total, G)) continue;  // empty
           const uint32_t* rec = p.partials + (size_t(k) * NSLOT + s) * kRecWords;
+          // acquire poll: the record reads below are ordered after the flag
           ok = wait_flag(p.flags + (size_t(k) * NSLOT + s) * 4 + quarter, gen + 1u, abort,
-                         p.status, 0x330 + s);
+                         p.status, 0x330 + s, true);
           if (!ok) break;
-          fence_acq_rel_gpu();
+          // (m, l) and all 16 chunks in one round of loads; a row the later
+          // piece saw nothing of (l = 0) leaves O, m and l as they are
           const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec + 128 * 64) + r);
-          if (ml.y > 0.f) {
-            const float nm = fmaxf(m, ml.x);
-            const float a = ex2_approx(m - nm);  // 0 when this row had nothing yet (m = -inf)
-            const float b = ex2_approx(ml.x - nm) * ml.y;
-            const int4* rec4 = reinterpret_cast<const int4*>(rec);
+          const int4* rec4 = reinterpret_cast<const int4*>(rec);
+          int4 v[16];
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-              const int4 v = __ldcg(rec4 + c * 128 + r);
-              const uint32_t wv[4] = {uint32_t(v.x), uint32_t(v.y), uint32_t(v.z), uint32_t(v.w)};
+          for (int c = 0; c < 16; ++c) v[c] = __ldcg(rec4 + c * 128 + r);
+          const bool use = ml.y > 0.f;
+          const float nm = use ? fmaxf(m, ml.x) : m;
+          const float a = use ? ex2_approx(m - nm) : 1.f;  // 0 when this row had nothing yet
+          const float b = use ? ex2_approx(ml.x - nm) * ml.y : 0.f;
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                o[8 * c + 2 * i] = o[8 * c + 2 * i] * a + __uint_as_float(wv[i] << 16) * b;
-                o[8 * c + 2 * i + 1] =
-                    o[8 * c + 2 * i + 1] * a + __uint_as_float(wv[i] & 0xffff0000u) * b;
-              }
+          for (int c = 0; c < 16; ++c) {
+            const uint32_t wv[4] = {uint32_t(v[c].x), uint32_t(v[c].y), uint32_t(v[c].z),
+                                    uint32_t(v[c].w)};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              o[8 * c + 2 * i] = o[8 * c + 2 * i] * a + __uint_as_float(wv[i] << 16) * b;
+              o[8 * c + 2 * i + 1] =
+                  o[8 * c + 2 * i + 1] * a + __uint_as_float(wv[i] & 0xffff0000u) * b;
             }
-            l = l * a + b;
-            m = nm;
           }
+          l = l * a + b;
+          m = nm;
         }
         if (!ok) break;
       }
-      // ---- final output of the item
+      // ---- final output of the item: O / l rows staged in this slot's P
+      // buffer (free: the last PV has completed) in the 128-byte-swizzled TMA
+      // layout, then two bulk tensor stores of 64 columns x 128 rows (rows
+      // past q_len are not written).  The buffer is free again for the next
+      // piece's P once the stores have read it.
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
-      if (q < p.q_len) {
-        int4* dst = reinterpret_cast<int4*>(p.out + (size_t(q) * p.hq + h) * HD);
+      {
+        const uint32_t orow = smem_u32(sm.pb[s]) + uint32_t(r) * 128u;
 #pragma unroll
         for (int v = 0; v < 16; ++v)
-          dst[v] = make_int4(int(pack_bf16x2(o[8 * v] * inv, o[8 * v + 1] * inv)),
-                             int(pack_bf16x2(o[8 * v + 2] * inv, o[8 * v + 3] * inv)),
-                             int(pack_bf16x2(o[8 * v + 4] * inv, o[8 * v + 5] * inv)),
-                             int(pack_bf16x2(o[8 * v + 6] * inv, o[8 * v + 7] * inv)));
-        if (p.lse)
-          p.lse[size_t(h) * p.q_len + q] =
-              (l > 0.f) ? (m + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
+          st_shared_v4(orow + uint32_t((v >> 3) * SUB_BYTES) + (uint32_t((v & 7) ^ (r & 7)) << 4),
+                       pack_bf16x2(o[8 * v] * inv, o[8 * v + 1] * inv),
+                       pack_bf16x2(o[8 * v + 2] * inv, o[8 * v + 3] * inv),
+                       pack_bf16x2(o[8 * v + 4] * inv, o[8 * v + 5] * inv),
+                       pack_bf16x2(o[8 * v + 6] * inv, o[8 * v + 7] * inv));
+        fence_async_shared();
+        mbar_arrive(&sm.bar_ostage[s]);
+        if (r == 0) {
+          if (mbar_wait(&sm.bar_ostage[s], uint32_t(fo) & 1u, abort, p.status, 0x340 + s)) {
+            tma_store_3d(&tm_o, sm.pb[s], 0, qt * BM, h);
+            tma_store_3d(&tm_o, sm.pb[s] + SUB_BYTES, 64, qt * BM, h);
+            bulk_commit_group();
+            bulk_wait_group_read0();
+          }
+          mbar_arrive(&sm.bar_ofree[s]);  // also after an abort, so no thread waits long
+        }
+        ok = __all_sync(0xffffffffu, mbar_wait(&sm.bar_ofree[s], uint32_t(fo) & 1u, abort,
+                                               p.status, 0x342 + s));
+        ++fo;
+        if (!ok) break;
       }
+      if (q < p.q_len && p.lse)
+        p.lse[size_t(h) * p.q_len + q] =
+            (l > 0.f) ? (m + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
     }
+    bulk_wait_group0();  // this thread's output stores (if any) have completed
     // query tiles without any visible block: all their rows are fully masked
     if (ok) {
       const int tid = threadIdx.x;  // 0..255
@@ -799,6 +832,9 @@ extern "C" int hsd_verify_attention(const void* q, int64_t q_row_stride, int64_t
   int rc = make_map(&tq, q, q_len, num_q_heads, q_row_stride, q_head_stride, "q");
   if (!rc) rc = make_map(&tk, k, kv_len, num_kv_heads, k_row_stride, k_head_stride, "k");
   if (!rc) rc = make_map(&tv, v, kv_len, num_kv_heads, v_row_stride, v_head_stride, "v");
+  CUtensorMap to;
+  if (!rc)
+    rc = make_map(&to, out, q_len, num_q_heads, int64_t(num_q_heads) * attn::HD, attn::HD, "out");
   if (rc) return rc;
   attn::Params p;
   p.out = static_cast<__nv_bfloat16*>(out);
@@ -856,6 +892,6 @@ extern "C" int hsd_verify_attention(const void* q, int64_t q_row_stride, int64_t
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return hsd_host::cuda_check(cudaLaunchKernelEx(&cfg, attn::verify_attn_kernel, tq, tk, tv, p),
+  return hsd_host::cuda_check(cudaLaunchKernelEx(&cfg, attn::verify_attn_kernel, tq, tk, tv, to, p),
                               "verify_attn_kernel launch");
 }
