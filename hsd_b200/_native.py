@@ -93,6 +93,7 @@ SIGNATURES = [
       _I32, _P]),
     ("hsd_continuation_trees", C.c_int,
      [_P, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P]),
+    ("hsd_selftest_bounded_wait", C.c_int, [_P, _P, _P]),
     ("hsd_lm_head_argmax_workspace_bytes", _SZ, [_I32]),
     ("hsd_lm_head_argmax", C.c_int,
      [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _SZ, _P, _P]),

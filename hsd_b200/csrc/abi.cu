@@ -117,3 +117,29 @@ int hsd_plan_init(void* workspace, size_t bytes, int32_t q_len, int32_t kv_len,
 }
 
 }  // extern "C"
+
+namespace {
+
+// One thread waits for *flag == 1 with the library's bounded wait; nothing
+// sets the flag, so the wait gives up after hsd::kWaitLimitNs and records
+// HSD_DEV_TIMEOUT | where in the status word.
+__global__ void selftest_wait_kernel(const uint32_t* flag, int32_t* status, int32_t where) {
+  __shared__ int abort;
+  if (threadIdx.x == 0) {
+    abort = 0;
+    hsd::wait_flag(flag, 1u, &abort, status, where);
+  }
+}
+
+}  // namespace
+
+extern "C" int hsd_selftest_bounded_wait(const uint32_t* flag, int32_t* status,
+                                         hsd_stream_t stream) {
+  if (!flag || !status) {
+    hsd_host::set_error("hsd_selftest_bounded_wait: flag and status are required");
+    return HSD_ERR_INVALID_ARG;
+  }
+  selftest_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flag, status,
+                                                                              0x7F0);
+  return hsd_host::cuda_check(cudaGetLastError(), "selftest_wait_kernel launch");
+}

@@ -135,6 +135,14 @@ typedef struct {
 const char *hsd_version(void);
 const char *hsd_last_error(void);
 
+/* Self-test of the device-side failure path: one thread waits for
+ * *flag == 1 (a device word nothing sets) with the same bounded wait every
+ * kernel of this library uses, gives up after 1 s and writes
+ * HSD_DEV_TIMEOUT | 0x7F0 into *status; the context stays usable.  Shows on
+ * a device that a wait which cannot finish ends in an error code, not a
+ * hang. */
+int hsd_selftest_bounded_wait(const uint32_t *flag, int32_t *status, hsd_stream_t stream);
+
 /* ---- (4) packing metadata ---------------------------------------------- */
 
 /* Bytes of device workspace a plan for (q_len, kv_len) needs. */
