@@ -46,12 +46,33 @@ def shard_pages(costs, world: int):
     return [sorted(s) for s in shards]
 
 
+def run_shard(pages, fn):
+    """Verify this rank's pages one after another, as the reference's
+    per-image loop does (hsd/hunyuan_ocr_pipeline/run_hunyuan_ocr_hsd.py
+    RH:264-280): a page whose ``fn(page)`` raises is recorded as failed (its
+    result is ``None``, its message kept) and the next page runs.
+
+    Returns ``(results {page: 1-D int tensor or None}, errors {page: str})``.
+    """
+    results, errors = {}, {}
+    for i in pages:
+        try:
+            results[i] = torch.as_tensor(fn(i), dtype=torch.int64).reshape(-1)
+        except Exception as e:  # noqa: BLE001 -- any failure of one page
+            results[i] = None
+            errors[i] = f"{type(e).__name__}: {e}"
+    return results, errors
+
+
 def gather_page_results(local: dict, n_pages: int, dst: int = 0, device=None):
-    """Gather ``{page_index: 1-D int tensor}`` from every rank to ``dst``.
+    """Gather ``{page_index: 1-D int tensor or None}`` from every rank to ``dst``.
 
     Variable-length results travel as (lengths, padded buffer): one gather of
-    the per-page lengths, then one of the padded token buffers.  Returns the
-    full ``{page_index: tensor}`` on ``dst`` and ``None`` elsewhere.
+    the per-page lengths, then one of the padded token buffers; a failed page
+    (``None``) travels as length -2 and comes back as ``None``.  Returns the
+    full ``{page_index: tensor or None}`` on ``dst`` and ``None`` elsewhere;
+    a page that no rank reported raises on ``dst``.  Collectives that a dead
+    rank never joins end with the process group's timeout error.
     """
     world = dist.get_world_size()
     rank = dist.get_rank()
@@ -64,13 +85,14 @@ def gather_page_results(local: dict, n_pages: int, dst: int = 0, device=None):
     lens = torch.full((max_n, 2), -1, dtype=torch.int64, device=device)
     for j, i in enumerate(idx):
         lens[j, 0] = i
-        lens[j, 1] = local[i].numel()
+        lens[j, 1] = -2 if local[i] is None else local[i].numel()
     all_lens = [torch.zeros_like(lens) for _ in range(world)]
     dist.all_gather(all_lens, lens)
     max_len = max(1, int(max(t[:, 1].max().item() for t in all_lens)))
     buf = torch.zeros((max_n, max_len), dtype=torch.int64, device=device)
     for j, i in enumerate(idx):
-        buf[j, :local[i].numel()] = local[i].to(device=device, dtype=torch.int64)
+        if local[i] is not None:
+            buf[j, :local[i].numel()] = local[i].to(device=device, dtype=torch.int64)
     all_buf = [torch.zeros_like(buf) for _ in range(world)]
     dist.all_gather(all_buf, buf)
     if rank != dst:
@@ -80,7 +102,7 @@ def gather_page_results(local: dict, n_pages: int, dst: int = 0, device=None):
         for j in range(max_n):
             page, n = int(lens_r[j, 0]), int(lens_r[j, 1])
             if page >= 0:
-                out[page] = buf_r[j, :n].clone()
+                out[page] = None if n == -2 else buf_r[j, :n].clone()
     missing = set(range(n_pages)) - set(out)
     if missing:
         raise RuntimeError(f"pages without results after the gather: {sorted(missing)[:8]}")

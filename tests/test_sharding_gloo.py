@@ -1,6 +1,7 @@
 """Page sharding and the rank-0 result gather, on CPU ranks over gloo."""
 import os
 import socket
+import time
 
 import pytest
 import torch
@@ -77,3 +78,73 @@ def test_gather_to_rank0_over_gloo(world):
     assert sorted(got) == list(range(n_pages))
     for i in range(n_pages):
         assert got[i] == [1000 * i + t for t in range(i % 7 + 1)]
+
+
+def _worker_failures(rank, world, port, n_pages, q):
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=20))
+    try:
+        mine = S.shard_pages([1] * n_pages, world)[rank]
+
+        def verify(i):
+            if i % 4 == 3:
+                raise RuntimeError(f"page {i} could not be verified")
+            return list(range(i + 1))
+
+        local, errors = S.run_shard(mine, verify)
+        out = S.gather_page_results(local, n_pages, dst=0)
+        q.put((rank, None if out is None else {k: (None if v is None else v.tolist())
+                                               for k, v in out.items()}, sorted(errors)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_failed_pages_are_reported_and_the_rest_gathered():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port, world, n_pages = _free_port(), 2, 10
+    procs = [ctx.Process(target=_worker_failures, args=(r, world, port, n_pages, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted([q.get(timeout=120) for _ in range(world)], key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    got = results[0][1]
+    assert sorted(got) == list(range(n_pages))
+    for i in range(n_pages):
+        assert got[i] == (None if i % 4 == 3 else list(range(i + 1)))
+    assert sorted(results[0][2] + results[1][2]) == [3, 7]
+
+
+def _worker_dead_rank(rank, world, port, q):
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(0)  # leaves between steps, never joins the gather
+    t0 = time.time()
+    try:
+        S.gather_page_results({0: torch.arange(3)}, 2, dst=0)
+        q.put(("no error", time.time() - t0))
+    except Exception as e:  # noqa: BLE001
+        q.put((type(e).__name__, time.time() - t0))
+
+
+def test_dead_rank_ends_the_gather_with_an_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_dead_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    kind, dt = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert kind != "no error" and dt < 60
