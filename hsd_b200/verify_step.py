@@ -120,6 +120,7 @@ class VerifyStep:
         self.row_bytes = d * 2
         self.period = period
         self._host = None
+        self._side = None  # second stream for the step's independent launches
         self.attn_launches_per_step = L
         # append 1 + plan 2 + attention L + accept 1 + keep 1 + compact 1 + bits 1
         self.kernel_launches_per_step = 1 + 2 + L + 4
@@ -135,22 +136,37 @@ class VerifyStep:
         ``phase_events`` (dict of name -> (start, end)) bracket the phases
         append / plan / accept / keep / compact / bits; layer l's attention
         waits for ``layer_ready[l]`` (an event) when given.
+
+        Independent launches run on a second stream: the KV append beside
+        the tile plan (both feed the attention), the visibility-row remap
+        beside the compaction (both follow the keep indices).  With
+        ``phase_events`` every phase runs in order on ``stream``, so each
+        pair of events brackets one phase alone.
         """
         lib = N.load()
-        st = N.stream_handle(stream)
+        main = stream if stream is not None else torch.cuda.current_stream()
+        st = N.stream_handle(main)
         p = self._ptr
         ev = phase_events or {}
+        concurrent = not ev
+        if concurrent and self._side is None:
+            self._side = torch.cuda.Stream(device=self.device)
+        side = self._side if concurrent else main
+        sst = N.stream_handle(side)
 
         def mark(name, i):
             if name in ev:
-                ev[name][i].record(stream)
-        # 1. KV append (the model's cache update)
+                ev[name][i].record(main)
+        # 1. KV append (the model's cache update), beside the plan
+        if concurrent:
+            side.wait_stream(main)
         mark("append", 0)
         N.check(lib.hsd_kv_append(p(self.planes), p(self.new_planes), self.planes.numel(),
-                                  self.row_bytes, self.prefix, self.q_len, st), "hsd_kv_append")
+                                  self.row_bytes, self.prefix, self.q_len, sst), "hsd_kv_append")
         mark("append", 1)
-        self.filter.zero_()
-        self.blocks.copy_(self.blocks0)
+        with torch.cuda.stream(main):
+            self.filter.zero_()
+            self.blocks.copy_(self.blocks0)
         mark("plan", 0)
         # 2. tile plan
         m = self.mask
@@ -158,8 +174,10 @@ class VerifyStep:
             p(m.segs), m.n_segs, p(m.row_seg), p(m.kv_bits), m.stride, p(m.tree_bits),
             C.byref(self.plan.struct), p(self.status), st), "hsd_build_plan_segments")
         mark("plan", 1)
+        if concurrent:
+            main.wait_stream(side)
         # 3. attention, every layer
-        self.run_attention(stream, attn_events, layer_ready)
+        self.run_attention(main, attn_events, layer_ready)
         # 4. acceptance + KMP
         mark("accept", 0)
         N.check(lib.hsd_accept_kmp(
@@ -174,6 +192,8 @@ class VerifyStep:
                                      self.kv_len, p(self.keep_bits), p(self.keep_idx),
                                      p(self.counts), st), "hsd_keep_indices")
         mark("keep", 1)
+        if concurrent:
+            side.wait_stream(main)
         mark("compact", 0)
         N.check(lib.hsd_compact_kv(p(self.planes), self.planes.numel(), self.row_bytes,
                                    p(self.keep_idx), -1, p(self.counts), p(self.status), st),
@@ -181,9 +201,11 @@ class VerifyStep:
         mark("compact", 1)
         mark("bits", 0)
         N.check(lib.hsd_compact_bits(p(self.vis), p(self.vis_next), self.n_blocks, self.stride,
-                                     p(self.keep_idx), p(self.counts), self.stride, st),
+                                     p(self.keep_idx), p(self.counts), self.stride, sst),
                 "hsd_compact_bits")
         mark("bits", 1)
+        if concurrent:
+            main.wait_stream(side)
 
     def run_attention(self, stream=None, attn_events=None, layer_ready=None):
         """The step's attention launches alone (every layer, current plan)."""
