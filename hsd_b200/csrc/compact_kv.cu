@@ -97,7 +97,7 @@ constexpr int kIdxCache = 8192;  // staged keep indices (32 KB); the rest read f
 //
 // The copy engine keeps far more bytes in flight per SM than 16-byte register
 // loads, so one CTA per plane streams close to HBM speed.  Waves of destination rows
-// [d0, d1) alternate between two shared-memory buffers: the sources of a wave
+// [d0, d1) go round a ring of shared-memory buffers: the sources of a wave
 // are fetched as runs of consecutive rows (at most 32 rows per run, found
 // with one warp ballot per 32 destinations) completing on the buffer's
 // mbarrier, then the whole wave goes back with one contiguous bulk store.  The
@@ -107,8 +107,13 @@ constexpr int kIdxCache = 8192;  // staged keep indices (32 KB); the rest read f
 // every earlier wave).  Before a buffer is refilled, the store that read it
 // must have finished reading shared memory.
 constexpr int kBulkThreads = 256;
-constexpr int kBulkBuf = 96 * 1024;  // bytes per staging buffer (two buffers)
-constexpr int kBulkSmem = 2 * kBulkBuf + kIdxCache * 4 + 64;
+#ifndef HSD_COMPACT_NBUF
+#define HSD_COMPACT_NBUF 4
+#endif
+constexpr int kBulkNBuf = HSD_COMPACT_NBUF;            // staging buffers (a ring)
+constexpr int kBulkData = 192 * 1024;                  // bytes of all staging buffers
+constexpr int kBulkBuf = kBulkData / kBulkNBuf / 256 * 256;  // bytes per buffer
+constexpr int kBulkSmem = kBulkNBuf * kBulkBuf + kIdxCache * 4 + 8 * (kBulkNBuf + 1);
 
 
 __device__ __forceinline__ void bulk_store(void* dst, const void* src_smem, uint32_t bytes) {
@@ -121,6 +126,10 @@ __device__ __forceinline__ void bulk_store(void* dst, const void* src_smem, uint
 __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+// Every committed bulk store but the most recent one has read shared memory.
+__device__ __forceinline__ void bulk_wait_read_but_last() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -131,9 +140,9 @@ __global__ void __launch_bounds__(kBulkThreads, 1) compact_plane_bulk_kernel(
     const int32_t* __restrict__ keep_idx, int n_keep_host, const int32_t* counts,
     int32_t* status) {
   extern __shared__ __align__(128) unsigned char smem[];
-  int32_t* s_idx = reinterpret_cast<int32_t*>(smem + 2 * kBulkBuf);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * kBulkBuf + kIdxCache * 4);
-  volatile int* abort = reinterpret_cast<volatile int*>(bar + 2);
+  int32_t* s_idx = reinterpret_cast<int32_t*>(smem + kBulkNBuf * kBulkBuf);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kBulkNBuf * kBulkBuf + kIdxCache * 4);
+  volatile int* abort = reinterpret_cast<volatile int*>(bar + kBulkNBuf);
   const int plane = blockIdx.x;
   const int n_keep = counts ? counts[0] : n_keep_host;
   const int first = counts ? counts[1] : 0;
@@ -146,8 +155,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) compact_plane_bulk_kernel(
   const int n_moved = n_keep - first;
   const int n_cached = n_moved < kIdxCache ? n_moved : kIdxCache;
   if (threadIdx.x == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    for (int i = 0; i < kBulkNBuf; ++i) mbar_init(&bar[i], 1);
     *abort = 0;
     fence_barrier_init();
   }
@@ -156,16 +164,21 @@ __global__ void __launch_bounds__(kBulkThreads, 1) compact_plane_bulk_kernel(
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int rows_per_wave = kBulkBuf / row_bytes;
   const int n_waves = (n_moved + rows_per_wave - 1) / rows_per_wave;
-  // Loads of wave wv+1 are issued before wave wv is waited for, so two waves
-  // of loads are in flight; wave wv+1's sources lie above every row wave wv
-  // stores, and its buffer was last read by the store of wave wv-1.
+  // Waves go round kBulkNBuf buffers with the loads of up to kBulkNBuf - 1
+  // waves in flight.  Wave wv's store is issued once its loads have landed
+  // (the loads of every earlier wave have landed before); a later wave's
+  // sources lie above every row an earlier wave stores, so its loads may be
+  // in flight during those stores.  A buffer is refilled once the store that
+  // last read it has read it.
   int issued = 0;
   auto issue_wave = [&](int wv) {
-    const int b = wv & 1;
+    const int b = wv % kBulkNBuf;
     const int d0 = first + wv * rows_per_wave;
     const int d1 = d0 + rows_per_wave < n_keep ? d0 + rows_per_wave : n_keep;
     if (threadIdx.x == 0) {
-      bulk_wait_read_all();  // the store that last read buffer b is done reading it
+      // buffer b was last read by the store of wave wv - kBulkNBuf, issued
+      // before the most recent store (wave wv - kBulkNBuf + 1, or none yet)
+      bulk_wait_read_but_last();
       mbar_arrive_expect_tx(&bar[b], uint32_t(d1 - d0) * uint32_t(row_bytes));
     }
     __syncthreads();
@@ -188,20 +201,18 @@ __global__ void __launch_bounds__(kBulkThreads, 1) compact_plane_bulk_kernel(
     }
     issued = wv + 1;
   };
-  issue_wave(0);
+  for (int x = 0; x < kBulkNBuf - 1 && x < n_waves; ++x) issue_wave(x);
   for (int wv = 0; wv < n_waves; ++wv) {
-    if (wv + 1 < n_waves) issue_wave(wv + 1);
-    const int b = wv & 1;
-    const uint32_t parity = uint32_t(wv >> 1) & 1u;
+    const int b = wv % kBulkNBuf;
+    const uint32_t parity = uint32_t(wv / kBulkNBuf) & 1u;
     const int d0 = first + wv * rows_per_wave;
     const int d1 = d0 + rows_per_wave < n_keep ? d0 + rows_per_wave : n_keep;
     if (threadIdx.x == 0) {
       if (!mbar_wait(&bar[b], parity, abort, status, 0x500 + b, false)) {
-        // loads of this wave (and of the next, if issued) are still in
-        // flight: let them land before the CTA's shared memory goes away
-        mbar_wait(&bar[b], parity, abort, nullptr, 0, false);
-        if (issued > wv + 1)
-          mbar_wait(&bar[b ^ 1], uint32_t((wv + 1) >> 1) & 1u, abort, nullptr, 0, false);
+        // loads still in flight (this wave's and the ones issued after it)
+        // land before the CTA's shared memory goes away
+        for (int x = wv; x < issued; ++x)
+          mbar_wait(&bar[x % kBulkNBuf], uint32_t(x / kBulkNBuf) & 1u, abort, nullptr, 0, false);
         *abort = 1;
       } else {
         bulk_store(base + size_t(d0) * row_bytes, smem + size_t(b) * kBulkBuf,
@@ -210,6 +221,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) compact_plane_bulk_kernel(
     }
     __syncthreads();
     if (*abort) break;
+    if (wv + kBulkNBuf - 1 < n_waves) issue_wave(wv + kBulkNBuf - 1);
   }
   if (threadIdx.x == 0) bulk_wait_all();
 }
@@ -374,9 +386,8 @@ int hsd_compact_kv(const uint64_t* plane_ptrs, int32_t n_planes, int32_t row_byt
     return HSD_ERR_INVALID_ARG;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  static_assert(compact::kThreads * compact::kVec * 16 <= compact::kBulkBuf,
-                "every accepted row fits a bulk staging buffer");
-  if (n_planes >= kPlaneCtaMinPlanes) {
+  // the bulk kernel stages whole rows; larger rows take the cluster kernel
+  if (n_planes >= kPlaneCtaMinPlanes && row_bytes <= compact::kBulkBuf) {
     int dev = 0;
     int rc = hsd_host::cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
     if (rc) return rc;
