@@ -346,14 +346,15 @@ __global__ void __launch_bounds__(256) append_kernel(const uint64_t* __restrict_
   const int4* src = reinterpret_cast<const int4*>(src_planes[plane]);
   int4* dst = reinterpret_cast<int4*>(reinterpret_cast<char*>(dst_planes[plane]) +
                                       size_t(dst_row0) * row_bytes);
+  // eight 16-byte loads in flight per thread, then their stores
+  constexpr int kU = 8;
   size_t v = v0 + threadIdx.x;
-  for (; v + 3 * blockDim.x < v1; v += 4 * blockDim.x) {
-    const int4 a = __ldcs(src + v), b = __ldcs(src + v + blockDim.x),
-               c = __ldcs(src + v + 2 * blockDim.x), d = __ldcs(src + v + 3 * blockDim.x);
-    dst[v] = a;
-    dst[v + blockDim.x] = b;
-    dst[v + 2 * blockDim.x] = c;
-    dst[v + 3 * blockDim.x] = d;
+  for (; v + (kU - 1) * blockDim.x < v1; v += kU * blockDim.x) {
+    int4 t[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) t[u] = __ldcs(src + v + u * blockDim.x);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) dst[v + u * blockDim.x] = t[u];
   }
   for (; v < v1; v += blockDim.x) dst[v] = __ldcs(src + v);
 }
@@ -441,7 +442,7 @@ int hsd_kv_append(const uint64_t* dst_planes, const uint64_t* src_planes, int32_
   }
   if (n_rows == 0) return HSD_OK;
   const int64_t nvec = int64_t(n_rows) * (row_bytes >> 4);
-  int chunks = int((nvec + 4095) / 4096);  // ~64 KB per CTA
+  int chunks = int((nvec + 8191) / 8192);  // ~128 KB per CTA
   if (chunks < 1) chunks = 1;
   compact::append_kernel<<<n_planes * chunks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       dst_planes, src_planes, n_planes, row_bytes, dst_row0, n_rows, chunks);
