@@ -96,8 +96,14 @@ struct FilterOp {
   int16_t path[kMaxPath];
 };
 
+// Dynamic shared memory: the blocks' FilterOps, then the filter words.
+__host__ __device__ __forceinline__ size_t filter_smem_offset(int n_blocks) {
+  return (size_t(n_blocks) * sizeof(FilterOp) + 15) & ~size_t(15);
+}
+
 // One CTA.  Phase 1: warp w handles blocks w, w + nwarps, ... in parallel.
-// Phase 2: warp 0 applies every block's filter operation in block order.
+// Phase 2: warp 0 applies every block's filter operation in block order, on
+// a shared-memory copy of the filter words written back once at the end.
 __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
   extern __shared__ uint8_t smem_raw[];
   FilterOp* ops = reinterpret_cast<FilterOp*>(smem_raw);
@@ -309,27 +315,31 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
   __syncthreads();
   if (warp_id() != 0) return;
   // Phase 2: replay the filter operations in block order.
+  uint64_t* filt = reinterpret_cast<uint64_t*>(smem_raw + filter_smem_offset(cfg.n_blocks));
+  for (int w = lane; w < nwords; w += 32) filt[w] = p.filter_bits[w];
+  __syncwarp();
   for (int b = 0; b < cfg.n_blocks; ++b) {
     const FilterOp& op = ops[b];
     if (op.kind == 1) {
-      or_range(p.filter_bits, op.lo, op.hi, lane, false);
+      or_range(filt, op.lo, op.hi, lane, false);
     } else if (op.kind == 2) {
       if (lane == 0)
         for (int k = 0; k < op.n_path; ++k) {
           const int c = op.lo + op.path[k];
-          p.filter_bits[c >> 6] |= 1ull << (c & 63);
+          filt[c >> 6] |= 1ull << (c & 63);
         }
       __syncwarp();
       for (int w = (op.lo >> 6) + lane; w <= (op.hi >> 6); w += 32)
-        p.filter_bits[w] ^= word_range(w, op.lo, op.hi);
+        filt[w] ^= word_range(w, op.lo, op.hi);
     }
     __syncwarp();
     if (op.finished) {
       const uint64_t* vis = p.out_kv_bits + size_t(b) * stride;
-      for (int w = lane; w < nwords; w += 32) p.filter_bits[w] |= vis[w];
+      for (int w = lane; w < nwords; w += 32) filt[w] |= vis[w];
     }
     __syncwarp();
   }
+  for (int w = lane; w < nwords; w += 32) p.filter_bits[w] = filt[w];
 }
 
 }  // namespace acc
@@ -338,6 +348,9 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
 using namespace hsd;
 
 static constexpr int kMaxBlocks = 1024;
+static constexpr size_t kMaxSmem = 200 * 1024;  // FilterOps + filter words
+static constexpr int kMaxDevices = 64;
+static bool g_attr_set[kMaxDevices] = {};
 
 extern "C" int hsd_accept_kmp(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
                               hsd_block_result_t* results, const int32_t* next_ids,
@@ -372,12 +385,28 @@ extern "C" int hsd_accept_kmp(const hsd_accept_config_t* cfg, hsd_block_t* block
     return HSD_ERR_TOO_LARGE;
   }
   const int warps = cfg->n_blocks < 32 ? cfg->n_blocks : 32;
-  const size_t smem = size_t(cfg->n_blocks) * sizeof(acc::FilterOp);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(acc::accept_kmp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         int(kMaxBlocks * sizeof(acc::FilterOp)));
-    attr = true;
+  const size_t smem = acc::filter_smem_offset(cfg->n_blocks) +
+                      size_t((cfg->kv_len + 63) / 64) * sizeof(uint64_t);
+  if (smem > kMaxSmem) {
+    hsd_host::set_error("hsd_accept_kmp: %d blocks over %d KV columns need %zu bytes of "
+                        "shared memory (at most %zu)",
+                        cfg->n_blocks, cfg->kv_len, smem, kMaxSmem);
+    return HSD_ERR_TOO_LARGE;
+  }
+  int dev = 0;
+  int rc = hsd_host::cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= kMaxDevices) {
+    hsd_host::set_error("hsd_accept_kmp: device ordinal %d >= %d", dev, kMaxDevices);
+    return HSD_ERR_UNSUPPORTED;
+  }
+  if (!g_attr_set[dev]) {
+    rc = hsd_host::cuda_check(
+        cudaFuncSetAttribute(acc::accept_kmp_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxSmem)),
+        "cudaFuncSetAttribute(accept_kmp_kernel)");
+    if (rc) return rc;
+    g_attr_set[dev] = true;
   }
   acc::accept_kmp_kernel<<<1, warps * 32, smem, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   return hsd_host::cuda_check(cudaGetLastError(), "accept_kmp_kernel launch");
