@@ -10,7 +10,7 @@
 // only wrote rows < w0.  Within a wave every source is read before any
 // destination is written.  Two launch shapes:
 //  * many planes (>= kPlaneCtaMinPlanes): one CTA per plane moving rows with
-//    the bulk-copy engine through two shared-memory buffers
+//    the bulk-copy engine through a ring of shared-memory buffers
 //    (compact_plane_bulk_kernel);
 //  * few planes: a thread-block cluster per plane staging a wave in
 //    registers, the cluster's hardware barrier separating the read and write
