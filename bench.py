@@ -556,11 +556,13 @@ def run_ours(args):
                            "achieved_gbs": comp_bytes / (breakdown["compact"] * 1e-3) / 1e9,
                            "peak_gbs": peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]),
                            "frac": comp_bytes / (breakdown["compact"] * 1e-3) / 1e9
-                           / peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])},
+                           / peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]),
+                           "traffic": profile_traffic("compact_kv_stage1_regions")},
             "gpu_launches": args.steps * step.kernel_launches_per_step,
             "clocks": clocks,
             "next_tokens": dict(next_tokens, peak_tflops=peak,
-                                frac=next_tokens["tflops"] / peak),
+                                frac=next_tokens["tflops"] / peak,
+                                traffic=profile_traffic("lm_head_argmax_stage1_rows")),
             "trees": trees,
             "rope_append": dict(rope, peak_gbs=peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]),
                                 frac=rope["achieved_gbs"]
