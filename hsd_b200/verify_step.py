@@ -33,18 +33,23 @@ from .plan import PackedMask, TilePlan, pack_bits
 
 
 class VerifyStep:
-    def __init__(self, page, device="cuda", seed=0, period=1):
+    def __init__(self, page, device="cuda", seed=0, period=1, device_rng=False):
+        """Device buffers of one page's step.  The synthetic Q / K / V come
+        from a CPU generator seeded with ``seed`` (the same on every machine),
+        or, with ``device_rng``, from a generator on the device (fast when
+        many pages are built)."""
         self.page = page
         self.device = torch.device(device)
         dev = self.device
         L, hq, hkv, d = page.layers, page.hq, page.hkv, page.head_dim
         self.L, self.hq, self.hkv, self.d = L, hq, hkv, d
         self.q_len, self.kv_len, self.prefix = page.q_len, page.kv_len, page.prefix
-        g = torch.Generator(device="cpu").manual_seed(seed)
+        gdev = dev if device_rng else torch.device("cpu")
+        g = torch.Generator(device=gdev).manual_seed(seed)
         s = 1.0 / np.sqrt(d)
 
         def rnd(*shape):
-            return (torch.randn(*shape, generator=g) * s).to(torch.bfloat16)
+            return (torch.randn(*shape, generator=g, device=gdev) * s).to(torch.bfloat16)
 
         # step inputs (device-resident for run(); mirrored in pinned host memory
         # for run_from_host())
