@@ -550,6 +550,13 @@ def run_ours(args):
                     "h2d_bytes_per_step": step.h2d_bytes(),
                     "d2h_bytes_per_step": step.d2h_bytes()},
             "breakdown_ms_per_step": breakdown,
+            "latency_bound": {
+                "accept_kmp_us": breakdown["accept"] * 1e3,
+                "blocks": step.n_blocks,
+                "blocks_per_s": step.n_blocks / (breakdown["accept"] * 1e-3),
+                "plan_us": breakdown["plan"] * 1e3,
+                "query_tiles": int(step.plan.struct.n_qtiles),
+                "segments_per_s": len(page.segments) / (breakdown["plan"] * 1e-3)},
             "compaction": {"bound": "hbm", "bytes_per_launch": comp_bytes,
                            "rows_moved": comp_moved, "rows_kept": comp_kept,
                            "planes": int(step.planes.numel()),
