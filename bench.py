@@ -394,6 +394,47 @@ def measure_trees(page, dev, steps, warmup, depth=15, cap=256):
             "timing": "CUDA events around back-to-back launches (includes the launch)"}
 
 
+def measure_loop(page, dev, iters=30):
+    """The verification loop's own cost per iteration: ``VerifyLoop.inputs``
+    + ``step`` (device tile plan, acceptance + KMP, keep / compaction rule, the
+    8-int result rows to the host and the host packing of the next inputs),
+    on the page's drafts with 64-token seeded prompts.  The target model is
+    replaced by a stand-in on the device (each packed row predicts the next
+    packed input token, so a speculative block accepts its whole draft
+    slice); its time is excluded."""
+    import torch
+
+    from hsd_b200.loop import VerifyLoop
+    from hsd_b200.workloads import EOS_ID
+
+    rng = np.random.default_rng(7)
+    drafts = [list(map(int, sg.draft)) for sg in page.segments]
+    prompts = [[int(x) for x in rng.integers(1, 150000, 64)] for _ in drafts]
+    loop = VerifyLoop(prompts, drafts, eos_token_id=EOS_ID, max_new_tokens=10 ** 7,
+                      kv_capacity=65536, device=dev)
+    times, rows, tokens = [], [], []
+    for _ in range(iters + 3):
+        t0 = time.perf_counter()
+        ids, pos, mask = loop.inputs()
+        nxt = torch.roll(ids, -1)                 # the stand-in target model
+        before = loop.new_tokens
+        more = loop.step(nxt)
+        torch.cuda.synchronize(dev)
+        times.append(time.perf_counter() - t0)
+        rows.append(int(ids.numel()))
+        tokens.append(loop.new_tokens - before)
+        if not more:
+            break
+    t, r, k = times[3:], rows[3:], tokens[3:]   # first iterations: setup, allocation
+    if not t:
+        return None
+    return {"blocks": len(drafts), "iterations": len(t),
+            "ms_per_iteration": 1e3 * sum(t) / len(t),
+            "packed_rows_per_iteration": sum(r) / len(r),
+            "new_tokens_per_iteration": sum(k) / len(k),
+            "timing": "host wall clock around inputs() + step(), device synchronised"}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -511,6 +552,7 @@ def run_ours(args):
     next_tokens = measure_next_tokens(page, dev, args.steps, args.warmup, seed=rank)
     rope = measure_rope_append(page, dev, args.steps, args.warmup, seed=rank)
     trees = measure_trees(page, dev, args.steps, args.warmup)
+    loop_cost = measure_loop(page, dev)
 
     tokens = float(page.verified_tokens)
     stats = torch.tensor([ms, e2e_ms, tokens], dtype=torch.float64, device=dev)
@@ -571,6 +613,7 @@ def run_ours(args):
                                 frac=next_tokens["tflops"] / peak,
                                 traffic=profile_traffic("lm_head_argmax_stage1_rows")),
             "trees": trees,
+            "loop": loop_cost,
             "rope_append": dict(rope, peak_gbs=peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]),
                                 frac=rope["achieved_gbs"]
                                 / peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
