@@ -1,12 +1,12 @@
 // Verification attention whose stream-K scratch lives in a static device
 // array instead of a caller-allocated workspace.
 //
-// For callers that cannot allocate device memory at the point of the call:
-// code running under a CUDA graph capture (cudaMalloc is not capturable), a
-// serving loop that must not go through an allocator between steps, or a
-// host binding that has no device allocator of its own.  The kernels and the
-// schedule are those of hsd_verify_attention; only where the scratch comes
-// from differs.
+// For callers that cannot allocate device memory where they call it: a
+// binding in another language that has no device allocator of its own, or a
+// serving loop that keeps every allocation at start-up and must not reach an
+// allocator (or pay for cudaMalloc's implicit synchronisation) between steps.
+// The kernels and the schedule are those of hsd_verify_attention; only where
+// the scratch comes from differs.
 //
 // Setup: the first call on each device (that device current) looks up the
 // array's device address with cudaGetSymbolAddress and caches it; this may
@@ -16,12 +16,15 @@
 // Limits: the scratch holds kStaticScratchBytes (20 MiB), enough for the
 // stream-K schedule on devices of up to 310 SMs (each SM's CTA needs a 33 KB
 // partial record per head slot and 32 bytes of flags).  A call whose scratch
-// need exceeds it returns HSD_ERR_TOO_LARGE and launches nothing.  The
-// scratch starts zero-filled (static storage), which its flags and launch
-// generation need, and every call leaves it ready for the next.  There is
-// one scratch per device, so calls on one device must not overlap in time --
-// issue them on one stream (or order them with events); two concurrent calls
-// race on the partial records and corrupt each other's output.
+// need exceeds it returns HSD_ERR_TOO_LARGE and launches nothing.  The array
+// keeps whatever the last call left in it, so every call first clears, on
+// its stream, the part that must start at zero (the ready flags and the
+// launch counters, a few KB; cudaMemsetAsync allocates nothing): a call never
+// depends on an earlier one, not even on one that stopped on an error.  The
+// partial records need no clearing -- each is written before it is read.
+// There is one scratch per device, so calls on one device must not overlap
+// in time -- issue them on one stream (or order them with events); two
+// overlapping calls race on the scratch and corrupt each other's output.
 #include <mutex>
 
 #include "common.cuh"
@@ -86,7 +89,14 @@ extern "C" int hsd_verify_attention_static_scratch(
     return HSD_ERR_TOO_LARGE;
   }
   void* scratch = nullptr;
-  const int rc = scratch_for_current_device(&scratch);
+  int rc = scratch_for_current_device(&scratch);
+  if (rc) return rc;
+  // the flags and launch counters start at zero on every call
+  const size_t flags = hsd_host::attention_flags_offset(q_len, num_q_heads, num_kv_heads);
+  rc = hsd_host::cuda_check(
+      cudaMemsetAsync(static_cast<unsigned char*>(scratch) + flags, 0, need - flags,
+                      reinterpret_cast<cudaStream_t>(stream)),
+      "cudaMemsetAsync(static attention scratch flags)");
   if (rc) return rc;
   return hsd_verify_attention(q, q_row_stride, q_head_stride, k, k_row_stride, k_head_stride, v,
                               v_row_stride, v_head_stride, out, lse, q_len, kv_len, num_q_heads,

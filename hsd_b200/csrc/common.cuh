@@ -413,4 +413,8 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 // The driver's cuTensorMapEncodeTiled, or nullptr when it is unavailable.
 EncodeTiledFn tensor_map_encoder();
+// Byte offset, in the attention's stream-K scratch, of the ready flags and
+// launch counters that follow the partial records (they run to the end of
+// hsd_attention_workspace_bytes()).
+size_t attention_flags_offset(int32_t q_len, int32_t num_q_heads, int32_t num_kv_heads);
 }  // namespace hsd_host

@@ -786,6 +786,12 @@ bool g_attr_set[kMaxDevices] = {};
 
 }  // namespace
 
+namespace hsd_host {
+size_t attention_flags_offset(int32_t q_len, int32_t num_q_heads, int32_t num_kv_heads) {
+  return ws_layout(q_len, num_q_heads, num_kv_heads).flags;
+}
+}  // namespace hsd_host
+
 extern "C" size_t hsd_attention_workspace_bytes(int32_t q_len, int32_t num_q_heads,
                                                 int32_t num_kv_heads) {
   if (q_len <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads)

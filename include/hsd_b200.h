@@ -202,14 +202,15 @@ int hsd_verify_attention(const void *q, int64_t q_row_stride, int64_t q_head_str
  * call).  hsd_verify_attention with the stream-K scratch taken from a static
  * device array of hsd_attention_static_scratch_bytes() bytes (20 MiB, enough
  * for devices of up to 310 SMs) instead of a caller workspace, so the call
- * allocates nothing: for callers under a CUDA graph capture, or that must not
- * reach an allocator between serving steps.  The first call on each device
- * (that device current) looks up the array's address -- make it before any
- * stream capture.  A scratch need above the array's size returns
- * HSD_ERR_TOO_LARGE.  The array starts zero-filled (static storage) and each
- * call leaves it ready for the next.  One scratch per device: calls on one device must not overlap in time (one
- * stream, or ordered by events), or they race on it.  Other arguments as
- * hsd_verify_attention. */
+ * allocates nothing: for bindings without a device allocator of their own,
+ * and for serving loops that must not reach an allocator between steps.  The
+ * first call on each device (that device current) looks up the array's
+ * address -- make it before any stream capture.  A scratch need above the
+ * array's size returns HSD_ERR_TOO_LARGE.  The array keeps the last call's
+ * contents; each call first clears the flags and counters that must start at
+ * zero (a few KB, on its stream).  One scratch per device: calls on one
+ * device must not overlap on the GPU (one stream, or ordered by events), or
+ * they race on it.  Other arguments as hsd_verify_attention. */
 size_t hsd_attention_static_scratch_bytes(void);
 int hsd_verify_attention_static_scratch(const void *q, int64_t q_row_stride,
                                         int64_t q_head_stride, const void *k,

@@ -3,8 +3,10 @@
 ``hsd_verify_attention_static_scratch`` runs the stream-K attention with its
 scratch in a static device array; it must give the same output as
 ``hsd_verify_attention`` with a caller workspace, on consecutive calls (the
-scratch is reused without being cleared).  Collected last so that it also runs
-after every other GPU test in the same process; it passes alone as well.
+array keeps what the previous call left; each call clears the flags and
+counters that must start at zero).  It is for callers that cannot allocate
+device memory themselves.  Collected last so that it also runs after every
+other GPU test in the same process; it passes alone as well.
 """
 import ctypes
 import math
