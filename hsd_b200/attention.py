@@ -97,7 +97,12 @@ def verify_attention(q, k, v, plan: TilePlan, scale=None, out=None, lse=None,
 
 
 def plan_for(attention_mask, q_len, kv_len):
-    """Tile plan for whatever mask object the caller passed."""
+    """Tile plan for whatever mask object the caller passed.
+
+    A dense mask tensor is converted once and the plan reused while the same
+    tensor object comes back (every layer of one step), as D:83-106 reuses
+    its BlockMask; like there, a mask changed in place between calls keeps
+    its old plan, so pass a new tensor (or a PackedMask) for a new step."""
     if isinstance(attention_mask, TilePlan):
         return attention_mask
     if isinstance(attention_mask, PackedMask):
