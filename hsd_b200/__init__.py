@@ -7,9 +7,18 @@ hand-written CUDA kernels behind a C ABI (``include/hsd_b200.h``,
 ``libhsd_b200.so``):
 
 1. packed block-sparse verification attention (tcgen05 + TMEM + TMA),
-2. in-place KV-cache compaction,
+2. in-place KV-cache compaction and the KV append,
 3. warp-per-block acceptance fused with KMP re-alignment,
-4. on-device packing metadata (tile plans from segment descriptors).
+4. on-device packing metadata (tile plans from segment descriptors),
+5. next tokens: the lm_head GEMM fused with the argmax (no logits written),
+6. rotary embedding fused with the cache update,
+7. tree decoding's continuation tries, built and packed on the device.
+
+Python entry points: ``attention.flex_attention_forward`` (the HF attention
+hook), ``loop.VerifyLoop`` / ``loop.batch_generate`` (the verification
+loop), ``verify_step.VerifyStep`` (one fixed page's step, as benchmarked),
+``lm_head.lm_head_argmax``, ``rope.rope_append``, ``trie.continuation_trees``
+and ``sharding`` (pages over the GPUs of a node).
 
 There is no CPU fallback: importing a kernel wrapper without the compiled
 library raises ``HSDNativeError``.
