@@ -89,3 +89,56 @@ def test_batch_generate_returns_true_texts():
     assert gen == ref_gen
     assert decode_times == len(trace)
     assert len(timings) == 8 and timings[6] == decode_times - 1
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("seed,period,tree", [(0, 1, False), (2, 3, False), (3, 1, True)])
+def test_registered_caches_follow_the_loops_columns(seed, period, tree):
+    """A model's K/V caches registered with the loop (``kv_planes``) are
+    compacted in place with its columns: every row of every plane encodes
+    the token of its KV column (and the plane's index), and after every
+    step's compaction the rows in front of the new ones still spell the
+    loop's ``kv_tokens`` exactly."""
+    from hsd_b200.compaction import plane_pointers
+    from hsd_b200.loop import VerifyLoop
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    dev = torch.device("cuda:0")
+    prompts, truths, drafts = LC.make_loop_case(seed)
+    model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
+    ref_gen, _ = OL.reference_loop(prompts, drafts, model, _cfg(tree), max_new_tokens=10 ** 6,
+                                   compact_period=period)
+    cap = 4096
+    caches = [torch.zeros(2, cap, 128, dtype=torch.bfloat16, device=dev) for _ in range(4)]
+    planes = plane_pointers(caches, device=dev)
+    n_planes = 2 * len(caches)
+    loop = VerifyLoop(prompts, drafts, eos_token_id=LC.EOS, max_new_tokens=10 ** 6,
+                      pad_token_id=LC.PAD, min_input_length=MIL, compact_period=period,
+                      enable_tree_decode=tree, kv_planes=planes, row_bytes=256,
+                      kv_capacity=cap, device=dev)
+    plane_id = torch.arange(n_planes, device=dev, dtype=torch.float32).view(4, 2, 1)
+
+    def check(n, tokens):
+        for t, c in enumerate(caches):
+            rows = c[:, :n, :3].float()                         # [2, n, 3]
+            got = (rows[..., 0] * 256 + rows[..., 1]).long()
+            assert torch.equal(got, tokens.long().expand(2, n)), (t, n)
+            assert torch.equal(rows[..., 2], plane_id[t].expand(2, n))
+
+    for it in range(1000):
+        ids, pos, mask = loop.inputs()
+        kv_tokens = loop.kv_tokens
+        total, q = kv_tokens.numel(), ids.numel()
+        check(total - q, kv_tokens[:total - q])
+        # the model's cache update: rows of the step's new columns
+        vals = torch.zeros(q, 128, dtype=torch.float32, device=dev)
+        vals[:, 0] = (ids // 256).float()
+        vals[:, 1] = (ids % 256).float()
+        for t, c in enumerate(caches):
+            for h in range(2):
+                vals[:, 2] = float(plane_id[t, h, 0])
+                c[h, total - q:total] = vals.to(torch.bfloat16)
+        allowed = mask.plan().dense_allowed()
+        nxt = model(ids.cpu().numpy(), pos.cpu().numpy(), allowed, kv_tokens.cpu().numpy())
+        if not loop.step(torch.from_numpy(nxt).to(dev)):
+            break
+    assert loop.generated() == ref_gen
