@@ -55,6 +55,32 @@ def test_compact_matches_index_select(dev, layers, hkv, kv, dead, first):
         assert torch.equal(v[:, :, :n_keep].cpu(), rv)
 
 
+@pytest.mark.parametrize("n_planes,row_bytes,kv,dead,first", [
+    (64, 256, 12000, 0.1, 50),      # > 8192 moved rows: indices past the staged cache
+    (80, 512, 3000, 0.3, 200),      # 512-byte rows (head dim 256), bulk kernel
+    (70, 64 * 1024, 40, 0.4, 1),    # rows larger than a staging buffer: cluster kernel
+    (4, 1024, 2000, 0.5, 10),       # few planes: cluster kernel
+])
+def test_compact_row_sizes_and_long_moves(dev, n_planes, row_bytes, kv, dead, first):
+    """Planes of raw rows of any 16-byte multiple move like index_select,
+    whichever kernel the plane count and row size pick."""
+    from hsd_b200.compaction import compact_kv, keep_indices
+    rng = np.random.default_rng(n_planes + row_bytes + kv)
+    keep = random_keep(kv, rng, dead, first)
+    data = torch.randint(0, 256, (n_planes, kv, row_bytes), dtype=torch.uint8, device=dev)
+    ref = data[:, torch.as_tensor(OC.keep_indices(keep), device=dev)].clone()
+    live = torch.from_numpy(_pack(keep)).to(dev)[None]
+    _, keep_idx, counts = keep_indices(live, None, kv)
+    planes = torch.tensor([data[i].data_ptr() for i in range(n_planes)], dtype=torch.int64,
+                          device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    compact_kv(planes, row_bytes, keep_idx, counts=counts, status=status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    n_keep = int(keep.sum())
+    assert torch.equal(data[:, :n_keep], ref)
+
+
 def _pack(b):
     from hsd_b200.plan import pack_bits
     return pack_bits(b).view(np.int64)
