@@ -615,6 +615,7 @@ def run_ours(args):
             "trees": trees,
             "loop": loop_cost,
             "rope_append": dict(rope, peak_gbs=peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]),
+                                traffic=profile_traffic("rope_append_stage1_rows"),
                                 frac=rope["achieved_gbs"]
                                 / peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
         }
