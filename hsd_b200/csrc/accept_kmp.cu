@@ -11,7 +11,8 @@
 // The KMP scan of the reference (compute_lps / kmp_search, D:543-604) reports
 // every occurrence of the window in the draft; the warp tests all candidate
 // starts at once, which yields the same set (and so the same count and first
-// start).  The continuation trie for tree mode is built by the host.
+// start).  The continuation tries for tree mode come packed as input
+// (hsd_continuation_trees builds them on the device).
 #include "common.cuh"
 
 namespace hsd {
@@ -84,41 +85,46 @@ __device__ void count_matches(const int32_t* text, int n, const int32_t* pat, in
   }
 }
 
-// Filter-bit operation a block applies, replayed in block order by phase 2
-// (the reference mutates one shared filter mask block after block; a tree
-// block *inverts* its column range, so order matters when ranges overlap).
-constexpr int kMaxPath = 64;
-struct FilterOp {
-  int32_t kind;  // 0 none, 1 OR [lo, hi], 2 tree: set path, then invert [lo, hi]
-  int32_t lo, hi;
-  int32_t finished;  // OR the block's visibility row afterwards
-  int32_t n_path;
-  int16_t path[kMaxPath];
+// The reference updates one filter mask block after block: a speculative
+// block sets its rejected columns (D:1196-1200), a tree block sets its walked
+// path and then inverts its column range (D:1266-1286), a finished block ORs
+// in its pointer row's visibility (D:1299-1319).  Setting bits commutes with
+// setting bits, so the rejected columns and tree paths go straight into a
+// shared-memory copy of the filter (atomics on masked words: neighbours may
+// share a word).  Only the inversions and the finished rows depend on the
+// block order (a row may reach another block's columns); each block records
+// those two as a FilterRec and one thread per filter word replays them in
+// block order at the end.
+struct FilterRec {
+  int32_t lo, hi;    // inverted columns [lo, hi] (none if lo > hi)
+  int32_t finished;  // OR the block's visibility row
 };
 
-// Dynamic shared memory: the blocks' FilterOps, then the filter words.
-__host__ __device__ __forceinline__ size_t filter_smem_offset(int n_blocks) {
-  return (size_t(n_blocks) * sizeof(FilterOp) + 15) & ~size_t(15);
+__host__ __device__ __forceinline__ size_t filter_rec_offset(int nwords) {
+  return (size_t(nwords) * sizeof(uint64_t) + 15) & ~size_t(15);
 }
 
-// One CTA.  Phase 1: warp w handles blocks w, w + nwarps, ... in parallel.
-// Phase 2: warp 0 applies every block's filter operation in block order, on
-// a shared-memory copy of the filter words written back once at the end.
+__device__ __forceinline__ void filter_or(unsigned long long* f, int lo, int hi, int lane) {
+  if (lo > hi) return;
+  for (int w = (lo >> 6) + lane; w <= (hi >> 6); w += 32) atomicOr(f + w, word_range(w, lo, hi));
+}
+
+// One CTA; warp w handles blocks w, w + nwarps, ... in parallel.  Dynamic
+// shared memory: the filter words, then one FilterRec per block.
 __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
   extern __shared__ uint8_t smem_raw[];
-  FilterOp* ops = reinterpret_cast<FilterOp*>(smem_raw);
+  unsigned long long* filt = reinterpret_cast<unsigned long long*>(smem_raw);
   const int lane = lane_id();
   const int nwarps = blockDim.x >> 5;
   const hsd_accept_config_t& cfg = p.cfg;
   const int stride = cfg.kv_words_stride;
   const int nwords = (cfg.kv_len + 63) / 64;
   const int kvb = cfg.kv_base;
+  FilterRec* recs = reinterpret_cast<FilterRec*>(smem_raw + filter_rec_offset(nwords));
+  for (int w = threadIdx.x; w < nwords; w += blockDim.x) filt[w] = p.filter_bits[w];
+  __syncthreads();
   for (int b = warp_id(); b < cfg.n_blocks; b += nwarps) {
-    FilterOp op;
-    op.kind = 0;
-    op.lo = op.hi = 0;
-    op.finished = 0;
-    op.n_path = 0;
+    if (lane == 0) recs[b] = FilterRec{1, 0, 0};
     hsd_block_t blk = p.blocks[b];
     hsd_block_result_t res;
     res.finished = 0;
@@ -134,10 +140,7 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
       uint64_t* dead = p.out_kv_bits + size_t(b) * stride;
       for (int w = lane; w < nwords; w += 32) dead[w] = 0;
       res.finished = 3;
-      if (lane == 0) {
-        p.results[b] = res;
-        ops[b] = op;
-      }
+      if (lane == 0) p.results[b] = res;
       continue;
     }
     const int bs = blk.q_start, blen = blk.q_len;
@@ -183,9 +186,7 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
         inc = diff + 1;
         if (diff != blen - 1) {
           ptr = bs + diff;
-          op.kind = 1;
-          op.lo = kvb + bs + diff + 1;
-          op.hi = kvb + bs + blen - 1;
+          filter_or(filt, kvb + bs + diff + 1, kvb + bs + blen - 1, lane);  // rejected rows
         }
         or_range(vis, kvb + bs, kvb + ptr, lane, false);
       }
@@ -198,13 +199,14 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
       if (glen + n > blk.gen_cap) {
         bad = true;
       } else {
-        if (lane == 0) gen[glen] = decode;
+        if (lane == 0) {
+          gen[glen] = decode;
+          // the visited path (root first) is kept: set here, inverted below
+          const int c = kvb + bs;
+          atomicOr(filt + (c >> 6), 1ull << (c & 63));
+          vis[c >> 6] |= 1ull << (c & 63);
+        }
         glen += 1;
-        op.kind = 2;
-        op.lo = kvb + bs;
-        op.hi = kvb + bs + blen - 1;
-        op.path[0] = 0;
-        op.n_path = 1;
         for (int guard = 0; guard < n; ++guard) {
           int child = -1;
           for (int base = node + 1; base < n; base += 32) {
@@ -217,33 +219,30 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
             }
           }
           if (child < 0) break;
-          if (op.n_path >= kMaxPath) {
-            bad = true;
-            break;
-          }
           node = child;
           decode = p.next_ids[bs + child];
-          if (lane == 0) gen[glen] = decode;
+          if (lane == 0) {
+            gen[glen] = decode;
+            const int c = kvb + bs + child;
+            atomicOr(filt + (c >> 6), 1ull << (c & 63));
+            vis[c >> 6] |= 1ull << (c & 63);
+          }
           glen += 1;
           ++walked;
-          op.path[op.n_path++] = int16_t(child);
         }
         ptr = bs + node;
         nxt = decode;
         inc = 1 + walked;
-        if (lane == 0)
-          for (int k = 0; k < op.n_path; ++k) {
-            const int c = kvb + bs + op.path[k];
-            vis[c >> 6] |= 1ull << (c & 63);
-          }
+        if (lane == 0) {  // unvisited nodes filtered: the range is inverted
+          recs[b].lo = kvb + bs;
+          recs[b].hi = kvb + bs + blen - 1;
+        }
       }
     } else {
       bad = true;
     }
     if (bad) {
       report(p.status, HSD_DEV_CAPACITY | 1);
-      op.kind = 0;
-      if (lane == 0) ops[b] = op;
       continue;
     }
     __syncwarp();
@@ -255,8 +254,8 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
     res.pointer = ptr;
     res.next_token = nxt;
 
-    // EOS stop (D:1299-1305) and repetition stop (D:1306-1319); their
-    // filter update (the pointer row) is applied in phase 2.
+    // EOS stop (D:1299-1305) and repetition stop (D:1306-1319); the block's
+    // visibility row joins the filter.
     const bool page_block = (blk.flags & 1) != 0;
     int finished = 0;
     if (is_eos(cfg, gen[glen - 1])) {
@@ -282,7 +281,7 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
     }
     __syncwarp();
     if (finished) {
-      op.finished = 1;
+      if (lane == 0) recs[b].finished = 1;
       blk.mode = HSD_MODE_FINISHED;
     } else if (!page_block) {
       // KMP re-alignment (D:1321-1336)
@@ -309,37 +308,20 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
     if (lane == 0) {
       p.results[b] = res;
       p.blocks[b] = blk;
-      ops[b] = op;
     }
   }
   __syncthreads();
-  if (warp_id() != 0) return;
-  // Phase 2: replay the filter operations in block order.
-  uint64_t* filt = reinterpret_cast<uint64_t*>(smem_raw + filter_smem_offset(cfg.n_blocks));
-  for (int w = lane; w < nwords; w += 32) filt[w] = p.filter_bits[w];
-  __syncwarp();
-  for (int b = 0; b < cfg.n_blocks; ++b) {
-    const FilterOp& op = ops[b];
-    if (op.kind == 1) {
-      or_range(filt, op.lo, op.hi, lane, false);
-    } else if (op.kind == 2) {
-      if (lane == 0)
-        for (int k = 0; k < op.n_path; ++k) {
-          const int c = op.lo + op.path[k];
-          filt[c >> 6] |= 1ull << (c & 63);
-        }
-      __syncwarp();
-      for (int w = (op.lo >> 6) + lane; w <= (op.hi >> 6); w += 32)
-        filt[w] ^= word_range(w, op.lo, op.hi);
+  // Order-dependent updates, per word in block order (the visibility rows
+  // are complete: every warp passed the barrier after writing its own).
+  for (int w = threadIdx.x; w < nwords; w += blockDim.x) {
+    uint64_t v = filt[w];
+    for (int b = 0; b < cfg.n_blocks; ++b) {
+      const FilterRec r = recs[b];
+      if (r.lo <= r.hi && (r.lo >> 6) <= w && w <= (r.hi >> 6)) v ^= word_range(w, r.lo, r.hi);
+      if (r.finished) v |= p.out_kv_bits[size_t(b) * stride + w];
     }
-    __syncwarp();
-    if (op.finished) {
-      const uint64_t* vis = p.out_kv_bits + size_t(b) * stride;
-      for (int w = lane; w < nwords; w += 32) filt[w] |= vis[w];
-    }
-    __syncwarp();
+    p.filter_bits[w] = v;
   }
-  for (int w = lane; w < nwords; w += 32) p.filter_bits[w] = filt[w];
 }
 
 }  // namespace acc
@@ -348,7 +330,7 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
 using namespace hsd;
 
 static constexpr int kMaxBlocks = 1024;
-static constexpr size_t kMaxSmem = 200 * 1024;  // FilterOps + filter words
+static constexpr size_t kMaxSmem = 200 * 1024;  // filter words + FilterRecs
 static constexpr int kMaxDevices = 64;
 static bool g_attr_set[kMaxDevices] = {};
 
@@ -385,8 +367,8 @@ extern "C" int hsd_accept_kmp(const hsd_accept_config_t* cfg, hsd_block_t* block
     return HSD_ERR_TOO_LARGE;
   }
   const int warps = cfg->n_blocks < 32 ? cfg->n_blocks : 32;
-  const size_t smem = acc::filter_smem_offset(cfg->n_blocks) +
-                      size_t((cfg->kv_len + 63) / 64) * sizeof(uint64_t);
+  const size_t smem = acc::filter_rec_offset((cfg->kv_len + 63) / 64) +
+                      size_t(cfg->n_blocks) * sizeof(acc::FilterRec);
   if (smem > kMaxSmem) {
     hsd_host::set_error("hsd_accept_kmp: %d blocks over %d KV columns need %zu bytes of "
                         "shared memory (at most %zu)",
