@@ -64,6 +64,11 @@ class AcceptConfig(C.Structure):
         [("eos_ids", C.c_int32 * 8)]
 
 
+class AcceptLogits(C.Structure):
+    _fields_ = [("max_logit", C.c_void_p), ("probe_logit", C.c_void_p),
+                ("spec_thresh", C.c_float), ("tree_thresh", C.c_float)]
+
+
 # (name, restype, argtypes) of every entry point include/hsd_b200.h declares.
 _P, _I32, _I64, _F, _SZ = C.c_void_p, C.c_int32, C.c_int64, C.c_float, C.c_size_t
 SIGNATURES = [
@@ -88,6 +93,9 @@ SIGNATURES = [
     ("hsd_compact_bits", C.c_int, [_P, _P, _I32, _I32, _P, _P, _I32, _P]),
     ("hsd_accept_kmp", C.c_int,
      [C.POINTER(AcceptConfig), _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    ("hsd_accept_kmp_logits", C.c_int,
+     [C.POINTER(AcceptConfig), _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+      C.POINTER(AcceptLogits), _P, _P]),
     ("hsd_rope_append", C.c_int,
      [_P, _I64, _P, _P, _I64, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _I64,
       _I32, _P]),
@@ -97,6 +105,8 @@ SIGNATURES = [
     ("hsd_lm_head_argmax_workspace_bytes", _SZ, [_I32]),
     ("hsd_lm_head_argmax", C.c_int,
      [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _SZ, _P, _P]),
+    ("hsd_probe_logits", C.c_int,
+     [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _P, _I32, _P, _P, _P]),
 ]
 
 _lib = None

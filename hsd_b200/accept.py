@@ -3,8 +3,10 @@
 One kernel launch per verification step handles every packed block with one
 warp each: the reference's per-block Python loop body
 (hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py D:1103-1336) at the default
-exact-match thresholds.  Block state lives in an int32 tensor with the field
-order of ``hsd_block_t``; results come back as ``hsd_block_result_t`` rows.
+exact-match thresholds, and with ``logits`` the logit-ratio rules below them
+(HSD_SPEC_THRESH / HSD_TREE_THRESH < 1, D:1147-1174, D:1228-1266).  Block
+state lives in an int32 tensor with the field order of ``hsd_block_t``;
+results come back as ``hsd_block_result_t`` rows.
 """
 from __future__ import annotations
 
@@ -21,6 +23,8 @@ R = {name: i for i, name in enumerate(RESULT_FIELDS)}
 
 DOTS_SENTINEL = 20993     # D:1306
 HUNYUAN_SENTINEL = 41153  # H:1873
+FLAG_PAGE_BLOCK = 1       # hsd_block_t.flags: no repetition stop, no token KMP
+FLAG_TEXT_MODE = 2        # parser.text_mode (D:1229): tree logit-ratio fallback on
 
 
 def make_config(n_blocks, kv_len, q_len, words_stride, eos_ids, match_window_size=3,
@@ -46,11 +50,14 @@ def make_config(n_blocks, kv_len, q_len, words_stride, eos_ids, match_window_siz
 
 def accept_kmp(cfg, blocks, next_ids, input_ids, gen_pool, draft_pool, seg_kv_bits,
                out_kv_bits, filter_bits, tree_tokens=None, tree_parents=None, results=None,
-               status=None, stream=None):
+               status=None, stream=None, logits=None):
     """Launch the acceptance kernel; all tensors are device int32 / int64.
 
     ``blocks``: int32 ``[n_blocks, 16]`` (updated in place);
-    returns ``results`` int32 ``[n_blocks, 8]``.
+    returns ``results`` int32 ``[n_blocks, 8]``.  ``logits = (max_logit,
+    probe_logit, spec_thresh, tree_thresh)`` (float32 ``[Q]`` tensors, see
+    ``hsd_accept_logits_t``) turns on the logit-ratio rules for thresholds
+    below 1.
     """
     lib = N.load()
     if results is None:
@@ -59,10 +66,22 @@ def accept_kmp(cfg, blocks, next_ids, input_ids, gen_pool, draft_pool, seg_kv_bi
     dummy = None
     if tree_tokens is None or tree_parents is None:
         dummy = torch.zeros(1, dtype=torch.int32, device=blocks.device)
-    N.check(lib.hsd_accept_kmp(
-        C.byref(cfg), N.ptr(blocks), N.ptr(results), N.ptr(next_ids), N.ptr(input_ids),
-        N.ptr(gen_pool), N.ptr(draft_pool), N.ptr(tree_tokens if tree_tokens is not None else dummy),
-        N.ptr(tree_parents if tree_parents is not None else dummy), N.ptr(seg_kv_bits),
-        N.ptr(out_kv_bits), N.ptr(filter_bits), N.ptr(status), N.stream_handle(stream)),
-        "hsd_accept_kmp")
+    args = (C.byref(cfg), N.ptr(blocks), N.ptr(results), N.ptr(next_ids), N.ptr(input_ids),
+            N.ptr(gen_pool), N.ptr(draft_pool),
+            N.ptr(tree_tokens if tree_tokens is not None else dummy),
+            N.ptr(tree_parents if tree_parents is not None else dummy), N.ptr(seg_kv_bits),
+            N.ptr(out_kv_bits), N.ptr(filter_bits))
+    if logits is None:
+        N.check(lib.hsd_accept_kmp(*args, N.ptr(status), N.stream_handle(stream)),
+                "hsd_accept_kmp")
+        return results
+    max_logit, probe_logit, spec_thresh, tree_thresh = logits
+    for t in (max_logit, probe_logit):
+        if t is not None and (t.dtype != torch.float32 or not t.is_contiguous()
+                              or t.numel() < input_ids.numel()):
+            raise ValueError("max_logit / probe_logit: contiguous float32, one per packed row")
+    lg = N.AcceptLogits(N.ptr(max_logit), N.ptr(probe_logit), float(spec_thresh),
+                        float(tree_thresh))
+    N.check(lib.hsd_accept_kmp_logits(*args, C.byref(lg), N.ptr(status),
+                                      N.stream_handle(stream)), "hsd_accept_kmp_logits")
     return results

@@ -1,11 +1,10 @@
 // (3) Draft-target acceptance fused with KMP re-alignment: one warp per block.
 //
-// Restates, at HSD_SPEC_THRESH / HSD_TREE_THRESH >= 1 (exact match), the
-// per-block body of the reference's verification loop
+// Restates the per-block body of the reference's verification loop
 // (hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py):
 //   normal 1-token step                 D:1107-1124
-//   speculative longest accepted prefix D:1126-1213
-//   tree walk                           D:1215-1293
+//   speculative longest accepted prefix D:1126-1213 (logit ratio D:1147-1174)
+//   tree walk                           D:1215-1293 (logit ratio D:1228-1238, D:1256-1266)
 //   EOS and repetition stop             D:1299-1319
 //   KMP re-alignment (token mode)       D:1321-1336, window D:1121-1124
 // The KMP scan of the reference (compute_lps / kmp_search, D:543-604) reports
@@ -32,7 +31,66 @@ struct Params {
   uint64_t* out_kv_bits;
   uint64_t* filter_bits;
   int32_t* status;
+  // logit-ratio acceptance (off at the default thresholds >= 1)
+  const float* max_logit;
+  const float* probe_logit;
+  float spec_thresh, tree_thresh;  // rounded to bf16
+  int32_t spec_ratio, tree_ratio;
 };
+
+// torch's bf16 quotient: the float32 quotient rounded to bf16 (D:1171, D:1233).
+__device__ __forceinline__ float logit_ratio(float num, float den) {
+  return __bfloat162float(__float2bfloat16_rn(__fdiv_rn(num, den)));
+}
+
+// A speculative row that missed the exact match passes when the draft
+// token's logit over the row's maximal logit reaches the threshold and the
+// maximal logit is positive (D:1163-1174).
+__device__ __forceinline__ bool spec_ratio_pass(const Params& p, int row) {
+  if (!p.spec_ratio) return false;
+  const float pred = p.max_logit[row];
+  return pred > 0.f && logit_ratio(p.probe_logit[row], pred) >= p.spec_thresh;
+}
+
+// Tree walk fallback (D:1228-1238, D:1256-1266): when the target's token
+// `decode` is not a child of `node`, the child with the first maximal ratio
+// logits[row, child] / logits[row, decode] (torch.argmax; a NaN ratio counts
+// as maximal) replaces it, if any ratio reaches the threshold.  Children are
+// the packed nodes with parent `node`, in BFS (insertion) order.
+__device__ int tree_ratio_fallback(const Params& p, int bs, int node, int decode,
+                                   const int32_t* tok, const int32_t* par, int n, int lane) {
+  for (int base = node + 1; base < n; base += 32) {
+    const int c = base + lane;
+    if (__any_sync(0xffffffffu, c < n && par[c] == node && tok[c] == decode)) return decode;
+  }
+  const float den = p.max_logit[bs + node];
+  bool pass = false;
+  int nan_c = -1, best_c = -1;
+  float best = 0.f;
+  for (int base = node + 1; base < n; base += 32) {
+    const int c = base + lane;
+    const bool kid = c < n && par[c] == node;
+    const float r = kid ? logit_ratio(p.probe_logit[bs + c], den) : 0.f;
+    pass |= __any_sync(0xffffffffu, kid && r >= p.tree_thresh);
+    const uint32_t nb = __ballot_sync(0xffffffffu, kid && isnan(r));
+    if (nan_c < 0 && nb) nan_c = base + __ffs(nb) - 1;
+    if (kid && !isnan(r) && (best_c < 0 || r > best)) {
+      best = r;
+      best_c = c;
+    }
+  }
+  if (!pass) return decode;
+  if (nan_c >= 0) return tok[nan_c];
+  for (int off = 16; off; off >>= 1) {  // maximal ratio, lowest index among equals
+    const float ob = __shfl_xor_sync(0xffffffffu, best, off);
+    const int oc = __shfl_xor_sync(0xffffffffu, best_c, off);
+    if (oc >= 0 && (best_c < 0 || ob > best || (ob == best && oc < best_c))) {
+      best = ob;
+      best_c = oc;
+    }
+  }
+  return tok[best_c];
+}
 
 
 __device__ __forceinline__ uint64_t word_range(int w, int lo, int hi) {  // [lo, hi]
@@ -169,7 +227,8 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
       int diff = blen - 1;
       for (int base = 0; base < blen - 1; base += 32) {
         const int i = base + lane;
-        const bool miss = (i < blen - 1) && (p.next_ids[bs + i] != p.input_ids[bs + i + 1]);
+        const bool miss = (i < blen - 1) && (p.next_ids[bs + i] != p.input_ids[bs + i + 1]) &&
+                          !spec_ratio_pass(p, bs + i);
         const uint32_t bal = __ballot_sync(0xffffffffu, miss);
         if (bal) {
           diff = base + __ffs(bal) - 1;
@@ -194,11 +253,13 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
       const int32_t* tok = p.tree_tokens + blk.tree_off;
       const int32_t* par = p.tree_parents + blk.tree_off;
       const int n = min(blk.tree_nodes, blen);
+      const bool ratio = p.tree_ratio && (blk.flags & 2);
       int decode = p.next_ids[bs];
       int node = 0, walked = 0;
       if (glen + n > blk.gen_cap) {
         bad = true;
       } else {
+        if (ratio) decode = tree_ratio_fallback(p, bs, 0, decode, tok, par, n, lane);
         if (lane == 0) {
           gen[glen] = decode;
           // the visited path (root first) is kept: set here, inverted below
@@ -221,6 +282,7 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
           if (child < 0) break;
           node = child;
           decode = p.next_ids[bs + child];
+          if (ratio) decode = tree_ratio_fallback(p, bs, child, decode, tok, par, n, lane);
           if (lane == 0) {
             gen[glen] = decode;
             const int c = kvb + bs + child;
@@ -231,7 +293,7 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
           ++walked;
         }
         ptr = bs + node;
-        nxt = decode;
+        nxt = p.next_ids[bs + node];  // next_token_int = group[new_index] (D:1292)
         inc = 1 + walked;
         if (lane == 0) {  // unvisited nodes filtered: the range is inverted
           recs[b].lo = kvb + bs;
@@ -334,13 +396,13 @@ static constexpr size_t kMaxSmem = 200 * 1024;  // filter words + FilterRecs
 static constexpr int kMaxDevices = 64;
 static bool g_attr_set[kMaxDevices] = {};
 
-extern "C" int hsd_accept_kmp(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
-                              hsd_block_result_t* results, const int32_t* next_ids,
-                              const int32_t* input_ids, int32_t* gen_pool,
-                              const int32_t* draft_pool, const int32_t* tree_tokens,
-                              const int32_t* tree_parents, const uint64_t* seg_kv_bits,
-                              uint64_t* out_kv_bits, uint64_t* filter_bits, int32_t* status,
-                              hsd_stream_t stream) {
+static int accept_launch(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
+                         hsd_block_result_t* results, const int32_t* next_ids,
+                         const int32_t* input_ids, int32_t* gen_pool, const int32_t* draft_pool,
+                         const int32_t* tree_tokens, const int32_t* tree_parents,
+                         const uint64_t* seg_kv_bits, uint64_t* out_kv_bits,
+                         uint64_t* filter_bits, const hsd_accept_logits_t* logits,
+                         int32_t* status, hsd_stream_t stream) {
   if (!cfg || cfg->n_blocks <= 0 || !blocks || !results || !next_ids || !input_ids ||
       !gen_pool || !draft_pool || !seg_kv_bits || !out_kv_bits || !filter_bits ||
       cfg->kv_words_stride < (cfg->kv_len + 63) / 64 || cfg->n_eos < 0 || cfg->n_eos > 8 ||
@@ -348,7 +410,21 @@ extern "C" int hsd_accept_kmp(const hsd_accept_config_t* cfg, hsd_block_t* block
     hsd_host::set_error("hsd_accept_kmp: bad arguments");
     return HSD_ERR_INVALID_ARG;
   }
+  const bool spec_ratio = logits && logits->spec_thresh < 1.0f;
+  const bool tree_ratio = logits && logits->tree_thresh < 1.0f;
+  if ((spec_ratio || tree_ratio) && (!logits->max_logit || !logits->probe_logit)) {
+    hsd_host::set_error("hsd_accept_kmp_logits: a threshold below 1 needs max_logit and "
+                        "probe_logit");
+    return HSD_ERR_INVALID_ARG;
+  }
   acc::Params p;
+  p.max_logit = logits ? logits->max_logit : nullptr;
+  p.probe_logit = logits ? logits->probe_logit : nullptr;
+  p.spec_ratio = spec_ratio;
+  p.tree_ratio = tree_ratio;
+  // the reference compares bf16 ratios with the threshold rounded to bf16
+  p.spec_thresh = spec_ratio ? __bfloat162float(__float2bfloat16_rn(logits->spec_thresh)) : 1.f;
+  p.tree_thresh = tree_ratio ? __bfloat162float(__float2bfloat16_rn(logits->tree_thresh)) : 1.f;
   p.cfg = *cfg;
   p.blocks = blocks;
   p.results = results;
@@ -392,4 +468,29 @@ extern "C" int hsd_accept_kmp(const hsd_accept_config_t* cfg, hsd_block_t* block
   }
   acc::accept_kmp_kernel<<<1, warps * 32, smem, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   return hsd_host::cuda_check(cudaGetLastError(), "accept_kmp_kernel launch");
+}
+
+extern "C" int hsd_accept_kmp(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
+                              hsd_block_result_t* results, const int32_t* next_ids,
+                              const int32_t* input_ids, int32_t* gen_pool,
+                              const int32_t* draft_pool, const int32_t* tree_tokens,
+                              const int32_t* tree_parents, const uint64_t* seg_kv_bits,
+                              uint64_t* out_kv_bits, uint64_t* filter_bits, int32_t* status,
+                              hsd_stream_t stream) {
+  return accept_launch(cfg, blocks, results, next_ids, input_ids, gen_pool, draft_pool,
+                       tree_tokens, tree_parents, seg_kv_bits, out_kv_bits, filter_bits, nullptr,
+                       status, stream);
+}
+
+extern "C" int hsd_accept_kmp_logits(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
+                                     hsd_block_result_t* results, const int32_t* next_ids,
+                                     const int32_t* input_ids, int32_t* gen_pool,
+                                     const int32_t* draft_pool, const int32_t* tree_tokens,
+                                     const int32_t* tree_parents, const uint64_t* seg_kv_bits,
+                                     uint64_t* out_kv_bits, uint64_t* filter_bits,
+                                     const hsd_accept_logits_t* logits, int32_t* status,
+                                     hsd_stream_t stream) {
+  return accept_launch(cfg, blocks, results, next_ids, input_ids, gen_pool, draft_pool,
+                       tree_tokens, tree_parents, seg_kv_bits, out_kv_bits, filter_bits, logits,
+                       status, stream);
 }

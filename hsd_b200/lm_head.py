@@ -71,3 +71,37 @@ def lm_head_argmax(hidden, weight, *, out=None, out_int32=None, max_logit=None, 
         N.ptr(out), N.ptr(max_logit), C.c_void_p(base), nbytes, N.ptr(status),
         N.stream_handle()), "hsd_lm_head_argmax")
     return out
+
+
+def probe_logits(hidden, weight, rows, toks, *, out=None, status=None):
+    """Single bf16 logits ``logits[rows[k], toks[k]]`` as float32, without
+    the logits tensor: ``hidden[rows[k]] . weight[toks[k]]`` with fp32
+    accumulation rounded to bf16 (``hsd_probe_logits``); ``toks[k] < 0``
+    gives 0.  These are the entries the logit-ratio acceptance reads
+    (D:1167-1168, D:1231-1232); :meth:`hsd_b200.loop.VerifyLoop.logit_probes`
+    lists them for a step.  ``rows`` / ``toks``: int32 device tensors.
+    """
+    if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("probe_logits: hidden and weight must be bf16")
+    hd = hidden.shape[-1]
+    if weight.dim() != 2 or weight.shape[1] != hd:
+        raise ValueError(f"probe_logits: weight {tuple(weight.shape)} vs hidden dim {hd}")
+    h2 = hidden.reshape(-1, hd)
+    if h2.stride(-1) != 1:
+        h2 = h2.contiguous()
+    w = weight if weight.stride(-1) == 1 else weight.contiguous()
+    n = rows.numel()
+    if toks.numel() != n or rows.dtype != torch.int32 or toks.dtype != torch.int32:
+        raise ValueError("probe_logits: rows and toks int32 of one length")
+    rows, toks = rows.contiguous(), toks.contiguous()
+    if out is None:
+        out = torch.empty(n, dtype=torch.float32, device=hidden.device)
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=hidden.device)
+    if n == 0:
+        return out
+    N.check(N.load().hsd_probe_logits(
+        N.ptr(h2), h2.stride(0), N.ptr(w), w.stride(0), h2.shape[0], w.shape[0], hd,
+        N.ptr(rows), N.ptr(toks), n, N.ptr(out), N.ptr(status), N.stream_handle()),
+        "hsd_probe_logits")
+    return out

@@ -24,7 +24,10 @@ proposes its draft's continuation tree (D:1488-1543), built and packed on the
 device for all such blocks in one launch (:mod:`hsd_b200.trie`); the tree's
 node arrays feed the next acceptance kernel and its ancestor rows the next
 mask without a host copy, and only tokens and depths come back to pack the
-input.
+input.  Below the default thresholds (``spec_thresh`` / ``tree_thresh`` < 1,
+HSD_SPEC_THRESH / HSD_TREE_THRESH, D:970-971) the logit-ratio rules apply:
+:meth:`VerifyLoop.logit_probes` lists the logits they read, and
+:meth:`VerifyLoop.step` takes them with the maximal logit per row.
 Not driven by this loop: tight packing (HSD_TIGHT_PACK) and the page block's
 tokenizer-driven parsers.
 """
@@ -37,7 +40,7 @@ import numpy as np
 import torch
 
 from . import _native as N
-from .accept import DOTS_SENTINEL, F, R, accept_kmp, make_config
+from .accept import DOTS_SENTINEL, FLAG_TEXT_MODE, F, R, accept_kmp, make_config
 from .compaction import compact_bits, compact_kv, keep_indices
 from .plan import SEG_CAUSAL, SEG_NONE, SEG_SINGLE, SEG_TREE, PackedMask, pack_bits
 from .trie import continuation_trees
@@ -60,7 +63,7 @@ class VerifyLoop:
                  max_spec_len=0, compact_period=1, enable_tree_decode=False,
                  max_tree_depth=15, max_tree_len=256,
                  repeat_sentinel=DOTS_SENTINEL, kv_planes=None, row_bytes=0,
-                 kv_capacity=None, device="cuda"):
+                 kv_capacity=None, spec_thresh=1.0, tree_thresh=1.0, device="cuda"):
         if len(prompts) != len(drafts) or not prompts:
             raise ValueError("one draft per prompt, at least one block")
         self.device = torch.device(device)
@@ -80,6 +83,8 @@ class VerifyLoop:
                          else int(max_tree_len))
         self.period = int(compact_period)
         self.sentinel = int(repeat_sentinel)
+        self.spec_thresh, self.tree_thresh = float(spec_thresh), float(tree_thresh)
+        self.ratio = self.spec_thresh < 1.0 or self.tree_thresh < 1.0
         self.kv_planes, self.row_bytes = kv_planes, int(row_bytes)
         self.drafts = [list(map(int, d)) for d in drafts]
         lens = [len(p) for p in prompts]
@@ -99,6 +104,7 @@ class VerifyLoop:
         self.kinds = [SEG_CAUSAL] * self.nb
         self.trees = None                            # device trees of this step's TREE blocks
         self.tree_slot = [-1] * self.nb              # row of block b in self.trees
+        self.tree_parents = [None] * self.nb         # host parents of block b's tree
         self.modes = [N.HSD_MODE_NORMAL] * self.nb   # D:978
         # non-pad rows per block (the reference counts them while
         # block_valid_counts is None, D:1108-1111)
@@ -166,14 +172,45 @@ class VerifyLoop:
         pos = torch.from_numpy(self.position_ids).to(self.device)
         return ids, pos, self._mask
 
-    def step(self, next_ids):
+    def logit_probes(self):
+        """``(rows, toks)``, int32 device ``[Q]``: the logits
+        ``logits[rows[r], toks[r]]`` the logit-ratio rules read this step,
+        one per packed row (``toks[r] = -1``: none).  A speculative block's
+        row r probes its draft token ``input_ids[r + 1]`` (D:1166-1167); a
+        tree block's node c (row bs + c) probes its own token at its
+        parent's row, ``logits[bs + parent(c), token(c)]`` (D:1231, D:1259).
+        :func:`hsd_b200.lm_head.probe_logits` computes them from the final
+        hidden states."""
+        q = int(self.input_ids.size)
+        rows = np.arange(q, dtype=np.int32)
+        toks = np.full(q, -1, dtype=np.int32)
+        for b in range(self.nb):
+            qs, ql = int(self.q_start[b]), int(self.q_len[b])
+            if self.modes[b] == N.HSD_MODE_SPEC and ql > 1:
+                toks[qs:qs + ql - 1] = self.input_ids[qs + 1:qs + ql]
+            elif self.modes[b] == N.HSD_MODE_TREE and self.tree_parents[b] is not None:
+                n = int(self.valid[b])
+                par = np.asarray(self.tree_parents[b][:n], dtype=np.int32)
+                rows[qs + 1:qs + n] = qs + par[1:]
+                toks[qs + 1:qs + n] = self.input_ids[qs + 1:qs + n]
+        return (torch.from_numpy(rows).to(self.device), torch.from_numpy(toks).to(self.device))
+
+    def step(self, next_ids, max_logit=None, probe_logit=None, text_mode=None):
         """Consume the target argmax of every packed row; prepare the next step.
 
-        Returns False once generation is finished (every block finished or
-        ``max_new_tokens`` generated, D:1589-1591).
+        With thresholds below 1, ``max_logit`` (float32 ``[Q]``, the maximal
+        bf16 logit per row: :func:`hsd_b200.lm_head.lm_head_argmax`'s
+        ``max_logit``) and ``probe_logit`` (float32 ``[Q]``, the logits
+        :meth:`logit_probes` lists) feed the logit-ratio rules, and
+        ``text_mode[b]`` (the page parser's ``text_mode``, D:1229; default
+        False) enables the tree fallback for block b.  Returns False once
+        generation is finished (every block finished or ``max_new_tokens``
+        generated, D:1589-1591).
         """
         if self.done:
             raise RuntimeError("the loop has finished")
+        if self.ratio and (max_logit is None or probe_logit is None):
+            raise ValueError("thresholds below 1 need max_logit and probe_logit")
         dev = self.device
         self.decode_times += 1
         q = int(self.input_ids.size)
@@ -185,6 +222,11 @@ class VerifyLoop:
         self.blocks[:, F["q_start"]] = upd[:, 1]
         self.blocks[:, F["q_len"]] = upd[:, 2]
         self.blocks[:, F["valid_count"]] = upd[:, 3]
+        if text_mode is not None:
+            flags = np.asarray([FLAG_TEXT_MODE if t else 0 for t in text_mode], dtype=np.int32)
+            if flags.size != self.nb:
+                raise ValueError("text_mode: one flag per block")
+            self.blocks[:, F["flags"]] = torch.from_numpy(flags).to(dev)
         toff = np.zeros(self.nb, dtype=np.int32)
         tnodes = np.zeros(self.nb, dtype=np.int32)
         d_tok = d_par = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -205,7 +247,9 @@ class VerifyLoop:
         accept_kmp(cfg, self.blocks, next_ids.to(torch.int32), ids, self.gen_pool,
                    self.draft_pool, self.seg_bits, self.out_bits, self.filter,
                    tree_tokens=d_tok, tree_parents=d_par, results=self.results,
-                   status=self.status)
+                   status=self.status,
+                   logits=(max_logit, probe_logit, self.spec_thresh, self.tree_thresh)
+                   if self.ratio else None)
         res = self.results.cpu().numpy()
         self._check()
 
@@ -229,6 +273,7 @@ class VerifyLoop:
         # next inputs (D:1421-1565) from the result rows
         new_ids, new_pos, new_lens = [], [], [0] * self.nb
         new_modes, new_valid, new_kinds = list(self.modes), [0] * self.nb, list(self.kinds)
+        new_parents = [None] * self.nb
         for b in range(self.nb):
             if self.modes[b] == N.HSD_MODE_FINISHED:
                 new_kinds[b] = SEG_NONE   # no rows any more
@@ -248,7 +293,7 @@ class VerifyLoop:
             else:
                 tree = host_trees.get(b)
                 if tree is not None and len(tree[0]) > 1:    # D:1488-1543
-                    tokens, depths, _ = tree
+                    tokens, depths, new_parents[b] = tree
                     n = len(tokens)
                     pad_n = math.ceil(n / self.mil) * self.mil - n
                     toks = list(tokens) + [self.pad] * pad_n
@@ -305,7 +350,7 @@ class VerifyLoop:
         self.q_len = np.asarray(new_lens, dtype=np.int64)
         self.q_start = ends - self.q_len
         self.modes, self.valid, self.kinds = new_modes, new_valid, new_kinds
-        self.trees, self.tree_slot = new_trees, new_slot
+        self.trees, self.tree_slot, self.tree_parents = new_trees, new_slot, new_parents
         self.kv_len = kv + int(self.input_ids.size)
         if self.kv_len > self.kv_cap:
             raise N.HSDError(f"KV columns {self.kv_len} exceed the loop's capacity {self.kv_cap}")
@@ -332,6 +377,11 @@ def batch_generate(model_fn, prompts, drafts, *, eos_token_id, max_new_tokens, *
     mask, kv_tokens) -> next_ids`` (the target forward + argmax per packed
     row; ``mask`` is the step's :class:`PackedMask`, ``kv_tokens`` the token
     of every KV column, which a model holding its own cache can ignore).
+    Below the default thresholds (``spec_thresh`` / ``tree_thresh`` < 1)
+    the call is ``model_fn(..., probes=(rows, toks)) -> (next_ids,
+    max_logit, probe_logit)`` with the probes of
+    :meth:`VerifyLoop.logit_probes`, optionally followed by ``text_mode``
+    (one flag per block).
 
     Returns the reference's result shape (D:1801-1810): ``(generated_tokens,
     decode_times, (forward_s, outside_forward_s, 0.0, 0.0, first_forward_s,
@@ -345,10 +395,13 @@ def batch_generate(model_fn, prompts, drafts, *, eos_token_id, max_new_tokens, *
         ids, pos, mask = loop.inputs()
         torch.cuda.synchronize(loop.device)
         t0 = time.perf_counter()
-        nxt = model_fn(ids, pos, mask, loop.kv_tokens)
+        if loop.ratio:
+            out = model_fn(ids, pos, mask, loop.kv_tokens, probes=loop.logit_probes())
+        else:
+            out = (model_fn(ids, pos, mask, loop.kv_tokens),)
         torch.cuda.synchronize(loop.device)
         t1 = time.perf_counter()
-        more = loop.step(nxt)
+        more = loop.step(*out)
         t2 = time.perf_counter()
         t_fwd += t1 - t0
         t_out += t2 - t1

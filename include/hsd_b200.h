@@ -103,7 +103,9 @@ typedef struct {
   int32_t tree_off;    /* HSD_MODE_TREE: packed BFS nodes at tree_tokens/parents[tree_off..] */
   int32_t tree_nodes;
   int32_t seg;         /* row of seg_kv_bits holding this block's KV visibility */
-  int32_t flags;       /* bit 0: page block (no repetition stop, no token KMP) */
+  int32_t flags;       /* bit 0: page block (no repetition stop, no token KMP);
+                          bit 1: text mode (parser.text_mode, D:1229), enables the
+                          tree logit-ratio fallback */
   int32_t reserved;
 } hsd_block_t;
 
@@ -130,6 +132,28 @@ typedef struct {
   int32_t n_eos;
   int32_t eos_ids[8];
 } hsd_accept_config_t;
+
+/* Inputs of the logit-ratio acceptance the reference applies below
+ * HSD_SPEC_THRESH / HSD_TREE_THRESH = 1 (D:970-971).  Ratios are bf16
+ * quotients (float32 quotient rounded to bf16) compared with the threshold
+ * rounded to bf16, as torch does on the bf16 logits tensor. */
+typedef struct {
+  /* [q_len] logits[r, next_ids[r]]: each packed row's maximal logit (bf16
+   * value; hsd_lm_head_argmax's max_logit) */
+  const float *max_logit;
+  /* [q_len] per packed row r: in a speculative block logits[r, input_ids[r + 1]];
+   * for node c >= 1 of a tree block starting at row bs,
+   * logits[bs + parent(c), token(c)] (row bs + c); hsd_probe_logits computes them */
+  const float *probe_logit;
+  /* < 1: a speculative row that misses also passes when
+   * probe_logit / max_logit >= thresh and max_logit > 0 (D:1147-1174) */
+  float spec_thresh;
+  /* < 1: in text-mode blocks (flags bit 1), a tree node whose target token is
+   * no child moves to the child of first maximal ratio
+   * probe_logit(child) / max_logit(node) if one reaches thresh (D:1228-1238,
+   * D:1256-1266) */
+  float tree_thresh;
+} hsd_accept_logits_t;
 
 /* ---- library ---------------------------------------------------------- */
 const char *hsd_version(void);
@@ -293,6 +317,20 @@ int hsd_accept_kmp(const hsd_accept_config_t *cfg, hsd_block_t *blocks,
                    uint64_t *out_kv_bits, uint64_t *filter_bits, int32_t *status,
                    hsd_stream_t stream);
 
+/* hsd_accept_kmp with the logit-ratio rules (thresholds below 1; at 1 or
+ * above, or logits == NULL, it equals hsd_accept_kmp).  A tree block's
+ * result next_token stays next_ids of its last walked row
+ * (next_token_int = group[new_index], D:1292); its generated token is the
+ * fallback's choice. */
+int hsd_accept_kmp_logits(const hsd_accept_config_t *cfg, hsd_block_t *blocks,
+                          hsd_block_result_t *results, const int32_t *next_ids,
+                          const int32_t *input_ids, int32_t *gen_pool,
+                          const int32_t *draft_pool, const int32_t *tree_tokens,
+                          const int32_t *tree_parents, const uint64_t *seg_kv_bits,
+                          uint64_t *out_kv_bits, uint64_t *filter_bits,
+                          const hsd_accept_logits_t *logits, int32_t *status,
+                          hsd_stream_t stream);
+
 /* Continuation tries of tree decoding, one CTA per tree.  Tree i: the draft
  * draft_pool[draft_off[i] .. + draft_len[i]) and the root token
  * last_tokens[i] (the match window's last token).  After every draft
@@ -331,6 +369,18 @@ int hsd_lm_head_argmax(const void *hidden, int64_t hidden_row_stride, const void
                        int32_t hidden_dim, int32_t *ids32, int64_t *ids64, float *max_logit,
                        void *workspace, size_t workspace_bytes, int32_t *status,
                        hsd_stream_t stream);
+
+/* Single logits of the logit-ratio acceptance: out[k] = logits[rows[k],
+ * toks[k]] = hidden[rows[k]] . weight[toks[k]] (bf16 in, fp32 accumulation,
+ * rounded to bf16 and returned as float), the entries the reference reads
+ * from the logits tensor (D:1167-1168, D:1231-1232); toks[k] < 0 gives 0.
+ * A row outside [0, q_len) or a token >= vocab writes NaN and sets
+ * HSD_DEV_BAD_INDEX.  One warp per entry; rows 16-byte aligned, strides
+ * (elements) multiples of 8, hidden_dim a multiple of 8. */
+int hsd_probe_logits(const void *hidden, int64_t hidden_row_stride, const void *weight,
+                     int64_t weight_row_stride, int32_t q_len, int32_t vocab,
+                     int32_t hidden_dim, const int32_t *rows, const int32_t *toks, int32_t n,
+                     float *out, int32_t *status, hsd_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -4,8 +4,12 @@ Restates the token-level parts of one iteration of the reference's
 ``batch_generate`` loop (hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py):
 
 * normal mode 1-token step (D:1107-1124)
-* speculative exact-match acceptance at ``HSD_SPEC_THRESH >= 1`` (D:1126-1213)
-* tree-walk acceptance at ``HSD_TREE_THRESH >= 1`` (D:1215-1293)
+* speculative acceptance (D:1126-1213): exact match, and below
+  ``HSD_SPEC_THRESH`` < 1 the logit-ratio test from the first miss on
+  (D:1147-1174)
+* tree-walk acceptance (D:1215-1293), with the logit-ratio fallback among a
+  node's children below ``HSD_TREE_THRESH`` < 1 in text mode (D:1228-1238,
+  D:1256-1266)
 * EOS and repetition stop (D:1299-1319)
 * KMP re-alignment of non-page blocks (D:1321-1336, D:1417-1419)
 * next block input: speculative slice, BFS tree, or normal (D:1421-1567)
@@ -37,6 +41,7 @@ class BlockState:
     valid_count: int | None = None               # block_valid_counts[b]
     tree_tokens: list | None = None              # packed BFS tree (tree mode)
     tree_parents: list | None = None
+    text_mode: bool = False                      # parser.text_mode (D:1229, D:1257)
 
 
 @dataclass
@@ -52,6 +57,46 @@ class StepConfig:
     tight_pack: bool = False       # HSD_TIGHT_PACK (D:52)
     enable_tree_decode: bool = False
     repeat_sentinel: int = 20993   # dots (D:1306); HunYuan uses 41153 (H:1873)
+    spec_thresh: float = 1.0       # HSD_SPEC_THRESH (D:971)
+    tree_thresh: float = 1.0       # HSD_TREE_THRESH (D:970)
+
+
+def bf16_f32(x):
+    """float32 -> nearest bf16 (ties to even, the float -> bfloat16
+    conversion torch applies to every bf16 result), returned as float32."""
+    a = np.atleast_1d(np.asarray(x, dtype=np.float32)).copy()
+    u = a.view(np.uint32)
+    nan = np.isnan(a)
+    r = (u + (((u >> 16) & 1) + np.uint32(0x7FFF))) & np.uint32(0xFFFF0000)
+    out = np.where(nan, a, r.view(np.float32))
+    return out if np.ndim(x) else out[0]
+
+
+def logit_ratio(num, den):
+    """``num / den`` of two bf16 logits as torch computes a bf16 quotient:
+    the float32 quotient rounded to bf16 (D:1171, D:1233)."""
+    with np.errstate(divide="ignore", invalid="ignore"):
+        return bf16_f32(np.float32(num) / np.float32(den))
+
+
+def ratio_passes(num, den, thresh):
+    """``(num / den) >= thresh`` on bf16 tensors: torch compares in bf16,
+    so the Python float threshold is rounded to bf16 first (0.9 -> 0.8984375)."""
+    return bool(logit_ratio(num, den) >= bf16_f32(thresh))
+
+
+def tree_ratio_fallback(node, tokens, parents, max_logit, probe_logit):
+    """The ratios a tree walk's fallback compares when the target's token is
+    not a child of ``node`` (D:1228-1238, D:1256-1266): ``logits[row, child
+    token] / logits[row, decode]`` over the node's children in insertion
+    (BFS) order, ``row`` being the node's packed row.  ``probe_logit[c]``
+    (indexed from the block's first row) holds ``logits[row of c's parent,
+    token c]``; ``max_logit``, the row's maximal logit, is ``logits[row,
+    decode]``.  Returns ``(children, ratios)``, or None without children."""
+    kids = [c for c in range(node + 1, len(tokens)) if parents[c] == node]
+    if not kids:
+        return None
+    return kids, [logit_ratio(probe_logit[c], max_logit) for c in kids]
 
 
 def _valid_length(st, input_list, bs, be, pad):
@@ -68,7 +113,7 @@ def _window_update(st, cfg, increment):
 
 
 def accept_block(st, bs, be, next_list, input_list, cfg, filt, kv_base,
-                 allowed_row_fn, is_page_block):
+                 allowed_row_fn, is_page_block, logits=None):
     """Acceptance for one block; mutates ``st`` and ``filt``.
 
     Returns ``(pointer, next_token, increment, finished_reason)`` where
@@ -76,7 +121,12 @@ def accept_block(st, bs, be, next_list, input_list, cfg, filt, kv_base,
     block's last accepted token, ``finished_reason`` is 0 (running),
     1 (EOS) or 2 (repetition stop).  ``filt`` is the step's bool filter over
     KV columns; ``allowed_row_fn(row)`` gives the bool visibility of a query
-    row (the mask row the EOS rule ORs in, D:1300-1302).
+    row (the mask row the EOS rule ORs in, D:1300-1302).  ``logits =
+    (max_logit, probe_logit)``, per packed row, feeds the logit-ratio rules
+    when a threshold is below 1: ``max_logit[r] = logits[r, next[r]]``; for a
+    speculative row ``probe_logit[r] = logits[r, input[r + 1]]``, for tree
+    node c of a block starting at bs ``probe_logit[bs + c] = logits[bs +
+    parent(c), token(c)]``.
     """
     pad = cfg.pad_token_id
     mode = st.mode
@@ -94,6 +144,13 @@ def accept_block(st, bs, be, next_list, input_list, cfg, filt, kv_base,
         ref = input_list[bs:be]
         blen = be - bs
         acc = [group[i] == ref[i + 1] for i in range(blen - 1)]
+        if cfg.spec_thresh < 1.0:                              # D:1147-1174
+            max_l, probe_l = logits
+            first_miss = next((i for i, ok in enumerate(acc) if not ok), len(acc))
+            for i in range(first_miss, len(acc)):
+                pred = np.float32(max_l[bs + i])
+                acc[i] = acc[i] or (bool(pred > 0) and
+                                    ratio_passes(probe_l[bs + i], pred, cfg.spec_thresh))
         diff = len(acc)
         for i, ok in enumerate(acc):
             if not ok:
@@ -114,7 +171,25 @@ def accept_block(st, bs, be, next_list, input_list, cfg, filt, kv_base,
         tokens, parents = st.tree_tokens, st.tree_parents
         n_nodes = len(tokens)
         consumed = [False] * n_nodes
-        decode = group[0]
+
+        def fallback(node, decode):                            # D:1228-1238
+            if not (cfg.tree_thresh < 1.0 and st.text_mode):
+                return decode
+            if any(parents[c] == node and tokens[c] == decode for c in range(node + 1, n_nodes)):
+                return decode
+            max_l, probe_l = logits
+            got = tree_ratio_fallback(node, tokens, parents, max_l[bs + node], probe_l[bs:])
+            if got is None:
+                return decode
+            kids, ratios = got
+            thr = bf16_f32(cfg.tree_thresh)
+            if not any(r >= thr for r in ratios):
+                return decode
+            nans = [i for i, r in enumerate(ratios) if np.isnan(r)]
+            best = nans[0] if nans else int(np.argmax(ratios))
+            return tokens[kids[best]]
+
+        decode = fallback(0, group[0])
         st.gen.append(decode)
         inc = 1
         filt[kv_base + bs] = True
@@ -132,7 +207,7 @@ def accept_block(st, bs, be, next_list, input_list, cfg, filt, kv_base,
             node = child
             new_index = child
             consumed[child] = True
-            decode = group[new_index]
+            decode = fallback(node, group[new_index])          # D:1256-1266
             st.gen.append(decode)
             inc += 1
             walked += 1

@@ -27,19 +27,42 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from .accept import FINISHED, BlockState, accept_block, next_block_input, realign_block
+from .accept import (FINISHED, SPEC, TREE, BlockState, accept_block, next_block_input,
+                     realign_block)
 from .compact import apply_to_mask, compaction_action, keep_columns, pad_filter
 from .masks import (assemble_next_mask, initial_packed_mask, normal_block_mask,
                     spec_block_mask, tree_block_mask)
 
 
+def ratio_logits(logits, next_ids, input_ids, spans, states):
+    """``(max_logit, probe_logit)`` per packed row, the logits tensor's
+    entries the logit-ratio rules read (D:1163-1168, D:1231-1232,
+    D:1259-1260): ``logits[r, next[r]]``; a speculative row's draft token
+    ``logits[r, input[r + 1]]``; a tree node's token at its parent's row."""
+    q = len(input_ids)
+    max_l = logits[np.arange(q), next_ids].astype(np.float32)
+    probe = np.zeros(q, dtype=np.float32)
+    for (bs, be), st in zip(spans, states):
+        if st.mode == SPEC:
+            for r in range(bs, be - 1):
+                probe[r] = logits[r, input_ids[r + 1]]
+        elif st.mode == TREE:
+            for c in range(1, len(st.tree_tokens)):
+                probe[bs + c] = logits[bs + st.tree_parents[c], st.tree_tokens[c]]
+    return max_l, probe
+
+
 def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1,
-                   max_iters=1000):
+                   max_iters=1000, logits_model=None, text_mode=()):
     """Run the loop; returns ``(generated tokens per block, trace)``.
 
     ``trace`` holds, per iteration, the packed ``input_ids``,
     ``position_ids``, the bool ``allowed`` mask [Q, KV], the blocks' modes
-    and the compaction action taken after the step.
+    and the compaction action taken after the step.  With ``logits_model``
+    (same arguments, returns float32 logits ``[Q, V]`` of bf16 values) the
+    next tokens are its first argmax per row and the logit-ratio rules of
+    ``cfg`` read its entries; ``text_mode`` holds the blocks whose parser is
+    in text mode.
     """
     nb = len(prompts)
     lens = [len(p) for p in prompts]
@@ -55,7 +78,18 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
         allowed = (mask[0, 0] > -0.1).numpy()
         q = len(input_ids)
         kv = allowed.shape[1]
-        next_ids = np.asarray(model(input_ids, position_ids, allowed, kv_tokens), dtype=np.int64)
+        logits = None
+        if logits_model is not None:
+            dense = logits_model(input_ids, position_ids, allowed, kv_tokens)
+            next_ids = np.argmax(dense, axis=1).astype(np.int64)
+            spans, b0 = [], 0
+            for b in range(nb):
+                spans.append((b0, pointer[b] + 1))
+                b0 = pointer[b] + 1
+            logits = ratio_logits(dense, next_ids, input_ids, spans, states)
+        else:
+            next_ids = np.asarray(model(input_ids, position_ids, allowed, kv_tokens),
+                                  dtype=np.int64)
         step = dict(input_ids=input_ids.copy(), position_ids=position_ids.copy(),
                     allowed=allowed.copy(), modes=[st.mode for st in states])
         trace.append(step)
@@ -71,8 +105,10 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
             if st.mode == FINISHED:
                 bs = be
                 continue
+            st.text_mode = b in text_mode
             ptr, nxt, inc, fin = accept_block(st, bs, be, next_list, input_list, cfg, filt,
-                                              kv_base, lambda row: allowed[row], False)
+                                              kv_base, lambda row: allowed[row], False,
+                                              logits=logits)
             pointer[b] = ptr
             new_tokens += inc
             bs = be

@@ -117,8 +117,26 @@ def make_scenario(seed, n_blocks=12, tight=False, vocab=None):
                 kv_len=kv_len, kv_old=kv_old, segs=segs, eos=(EOS,), seed=seed)
 
 
-def run_oracle(sc, page_block=None):
-    cfg = OA.StepConfig(pad_token_id=PAD, eos_token_ids=sc["eos"])
+def make_logits(sc, seed, thresh):
+    """Per-row (max_logit, probe_logit) float32 arrays of bf16 values for the
+    logit-ratio rules: maximal logits mostly positive (some zero or
+    negative), probes at random ratios to them, a share of them placed at
+    the bf16 threshold itself, where the rounding of the quotient decides."""
+    rng = np.random.default_rng(10_000 + seed)
+    q = sc["q_len"]
+    max_l = rng.normal(6.0, 4.0, q).astype(np.float32)
+    max_l[rng.random(q) < 0.05] = 0.0
+    max_l = OA.bf16_f32(max_l)
+    probe = OA.bf16_f32((max_l * rng.uniform(-0.2, 1.2, q)).astype(np.float32))
+    at = rng.random(q) < 0.2
+    probe[at] = OA.bf16_f32((max_l[at] * OA.bf16_f32(np.float32(thresh))).astype(np.float32))
+    return max_l, probe
+
+
+def run_oracle(sc, page_block=None, logits=None, spec_thresh=1.0, tree_thresh=1.0,
+               text_mode=()):
+    cfg = OA.StepConfig(pad_token_id=PAD, eos_token_ids=sc["eos"], spec_thresh=spec_thresh,
+                        tree_thresh=tree_thresh)
     allowed = OM.segments_to_allowed(sc["q_len"], sc["kv_len"], sc["segs"])
     filt = np.zeros(sc["kv_len"], bool)
     kv_base = sc["kv_len"] - sc["q_len"]
@@ -129,6 +147,7 @@ def run_oracle(sc, page_block=None):
                            valid_count=blk["valid"])
         if blk["tree"]:
             st.tree_tokens, st.tree_parents = blk["tree"]
+        st.text_mode = i in text_mode
         r = dict(finished=0, increment=0, pointer=-1, next_token=-1, match_count=0,
                  match_start=-1, slice_begin=-1, slice_end=-1)
         if blk["mode"] == OA.FINISHED:
@@ -138,7 +157,7 @@ def run_oracle(sc, page_block=None):
         bs, be = blk["q_start"], blk["q_start"] + blk["q_len"]
         ptr, nxt, inc, fin = OA.accept_block(
             st, bs, be, sc["next_ids"], sc["input_ids"], cfg, filt, kv_base,
-            lambda row: allowed[row], is_page_block=(i == page_block))
+            lambda row: allowed[row], is_page_block=(i == page_block), logits=logits)
         r.update(finished=fin, increment=inc, pointer=ptr, next_token=nxt)
         if not fin and i != page_block:
             window, matches, _ = OA.realign_block(st, cfg)

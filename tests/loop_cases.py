@@ -45,3 +45,20 @@ def make_loop_case(seed, n_blocks=6):
         truths.append(np.asarray(truth, dtype=np.int64))
         drafts.append(draft)
     return prompts, truths, drafts
+
+
+def logits_model(model, seed=0):
+    """Dense logits ``[Q, VOCAB + 1]`` around ``model``'s tokens, for the
+    logit-ratio rules: the model's token gets 8.0, every other entry a value
+    k / 8, k in [-48, 48), drawn from the row's token and position (all
+    exact in bf16), so a draft token's ratio is k / 64."""
+    def fn(input_ids, position_ids, allowed, kv_tokens):
+        nxt = np.asarray(model(input_ids, position_ids, allowed, kv_tokens), dtype=np.int64)
+        q = len(nxt)
+        out = np.empty((q, VOCAB + 1), dtype=np.float32)
+        for r in range(q):
+            g = np.random.default_rng((seed, int(input_ids[r]), int(position_ids[r])))
+            out[r] = g.integers(-48, 48, VOCAB + 1) / 8.0
+        out[np.arange(q), nxt] = 8.0
+        return out
+    return fn

@@ -22,7 +22,7 @@ def dev():
     return torch.device("cuda:0")
 
 
-def run_kernel(sc, dev, page_block=None):
+def run_kernel(sc, dev, page_block=None, logits=None, text_mode=()):
     from hsd_b200 import accept as A
     from hsd_b200.plan import pack_bits
     nb = len(sc["blocks"])
@@ -57,7 +57,8 @@ def run_kernel(sc, dev, page_block=None):
             tree_par += list(pars)
             toff += len(toks)
         blocks[i, f["seg"]] = i
-        blocks[i, f["flags"]] = 1 if i == page_block else 0
+        blocks[i, f["flags"]] = ((A.FLAG_PAGE_BLOCK if i == page_block else 0) |
+                                 (A.FLAG_TEXT_MODE if i in text_mode else 0))
         seg_bits[i, :(kv_len + 63) // 64] = pack_bits(blk["kv"])
     t = lambda a, dt=torch.int32: torch.as_tensor(np.asarray(a), dtype=dt).to(dev)
     cfg = A.make_config(nb, kv_len, sc["q_len"], stride, sc["eos"])
@@ -69,7 +70,10 @@ def run_kernel(sc, dev, page_block=None):
     res = A.accept_kmp(cfg, d_blocks, t(sc["next_ids"]), t(sc["input_ids"]), d_gen,
                        t(drafts or [0]), t(seg_bits.view(np.int64), torch.int64), out_bits, filt,
                        tree_tokens=t(tree_tok or [0]), tree_parents=t(tree_par or [0]),
-                       status=status)
+                       status=status,
+                       logits=None if logits is None else (
+                           torch.from_numpy(logits[0]).to(dev), torch.from_numpy(logits[1]).to(dev),
+                           logits[2], logits[3]))
     torch.cuda.synchronize()
     assert status.item() == 0, hex(status.item())
     return (res.cpu().numpy(), d_blocks.cpu().numpy(), d_gen.cpu().numpy(),
@@ -87,7 +91,12 @@ def test_accept_kmp_matches_oracle(dev, seed, tight):
     sc = AC.make_scenario(seed, tight=tight)
     page = len(sc["blocks"]) - 1 if seed % 3 == 0 else None
     expect, filt = run_oracle_checked(sc, page)
-    res, blocks, gen, vis, kfilt = run_kernel(sc, dev, page_block=page)
+    compare(sc, seed, expect, filt, run_kernel(sc, dev, page_block=page))
+
+
+def compare(sc, seed, expect, filt, kernel_out):
+    from hsd_b200 import accept as A
+    res, blocks, gen, vis, kfilt = kernel_out
     for i, (r, st, row) in enumerate(expect):
         got = {k: int(res[i, A.R[k]]) for k in A.RESULT_FIELDS}
         assert got == r, (seed, i, got, r)
@@ -105,3 +114,24 @@ def test_accept_kmp_matches_oracle(dev, seed, tight):
 def run_oracle_checked(sc, page):
     out, filt = AC.run_oracle(sc, page_block=page)
     return out, filt
+
+
+@pytest.mark.parametrize("seed", list(range(16)))
+@pytest.mark.parametrize("spec_thresh,tree_thresh", [(0.9, 1.0), (1.0, 0.5), (0.75, 0.9),
+                                                     (0.3, 0.3)])
+def test_accept_logit_ratio_matches_oracle(dev, seed, spec_thresh, tree_thresh):
+    """Thresholds below 1 (D:1147-1174, D:1228-1266): the kernel's
+    decisions on the same bf16 logits equal the oracle's, bit for bit
+    (generated tokens, pointers, filter and visibility rows)."""
+    sc = AC.make_scenario(seed, tight=bool(seed % 2))
+    page = len(sc["blocks"]) - 1 if seed % 3 == 0 else None
+    max_l, probe = AC.make_logits(sc, seed, min(spec_thresh, tree_thresh))
+    rng = np.random.default_rng(seed)
+    text_mode = {i for i in range(len(sc["blocks"])) if rng.random() < 0.6}
+    expect, filt = AC.run_oracle(sc, page_block=page, logits=(max_l, probe),
+                                 spec_thresh=spec_thresh, tree_thresh=tree_thresh,
+                                 text_mode=text_mode)
+    out = run_kernel(sc, dev, page_block=page, text_mode=text_mode,
+                     logits=(max_l, probe, spec_thresh, tree_thresh))
+    compare(sc, seed, expect, filt, out)
+

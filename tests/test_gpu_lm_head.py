@@ -131,3 +131,77 @@ def test_full_vocabulary_against_fp32_logits(dev):
         lb = (h[r0:r0 + 512].float() @ w.float().T).to(torch.bfloat16)
         ref_max[r0:r0 + 512] = lb.max(-1).values.float()
     assert torch.equal(mx[same], ref_max[same])
+
+
+def _one_step_off(exact, got, abs_sum, hd):
+    """``got`` (bf16 value) is the exact logit rounded to bf16, or within
+    one bf16 step of it plus the error bound of an fp32 sum of ``hd``
+    products (``hd * 2^-24 * sum |a_i b_i|``, which dominates when the
+    products cancel)."""
+    want = OL.round_bf16(exact)
+    _, e = np.frexp(np.maximum(np.abs(exact), 1e-30))
+    step = np.ldexp(1.0, e - 8)
+    return (got == want) | (np.abs(got - exact) <= step + hd * 2.0 ** -24 * abs_sum)
+
+
+@pytest.mark.parametrize("q,vocab,hd,n,seed", [(300, 5003, 1536, 4000, 0), (7, 64, 8, 50, 1),
+                                               (129, 4096, 200, 0, 2), (64, 151936, 1536, 512, 3)])
+def test_probe_logits_match_exact_and_cublas(dev, q, vocab, hd, n, seed):
+    """``probe_logits`` returns the bf16 logit the logits tensor holds:
+    equal to the exact dot product rounded to bf16 (one bf16 step off at
+    most, near rounding boundaries), and to torch's bf16 GEMM logits with
+    fp32 reduction the same way; toks < 0 give 0.  (torch's default bf16
+    GEMM may reduce partial sums in bf16 --
+    ``allow_bf16_reduced_precision_reduction`` -- and then differs from the
+    exactly rounded logit in a sizeable share of entries.)"""
+    from hsd_b200.lm_head import probe_logits
+    if hd % 8:
+        hd += 8 - hd % 8
+    h, w = _case(q, vocab, hd, seed)
+    rng = np.random.default_rng(seed)
+    rows = rng.integers(0, q, n).astype(np.int32)
+    toks = rng.integers(0, vocab, n).astype(np.int32)
+    toks[rng.random(n) < 0.1] = -1
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    got = probe_logits(h.to(dev), w.to(dev), torch.from_numpy(rows).to(dev),
+                       torch.from_numpy(toks).to(dev), status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    got = got.cpu().numpy().astype(np.float64)
+    if n == 0:
+        assert got.size == 0
+        return
+    on = toks >= 0
+    assert np.all(got[~on] == 0)
+    hd64 = h.double().numpy()
+    wd64 = w.double().numpy()
+    exact = np.einsum("kh,kh->k", hd64[rows[on]], wd64[toks[on]])
+    abs_sum = np.einsum("kh,kh->k", np.abs(hd64[rows[on]]), np.abs(wd64[toks[on]]))
+    ok = _one_step_off(exact, got[on], abs_sum, hd)
+    bad = np.nonzero(~ok)[0][:3]
+    assert ok.all(), [(exact[i], got[on][i], abs_sum[i]) for i in bad]
+    assert np.mean(got[on] == OL.round_bf16(exact)) > 0.97
+    # torch's logits tensor, a bf16 GEMM with fp32 reduction
+    flag = torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction
+    torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+    try:
+        ref = (h.to(dev) @ w.to(dev).T)[torch.from_numpy(rows[on]).long().to(dev),
+                                        torch.from_numpy(toks[on]).long().to(dev)]
+        ref = ref.float().cpu().numpy().astype(np.float64)
+    finally:
+        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = flag
+    assert np.mean(got[on] == ref) > 0.97
+    assert _one_step_off(exact, ref, abs_sum, hd).all()
+
+
+def test_probe_logits_bad_index_sets_status(dev):
+    from hsd_b200.lm_head import probe_logits
+    h, w = _case(8, 100, 64, 4)
+    rows = torch.tensor([0, 8, 3], dtype=torch.int32, device=dev)
+    toks = torch.tensor([5, 5, 100], dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = probe_logits(h.to(dev), w.to(dev), rows, toks, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & 0x20000
+    o = out.cpu().numpy()
+    assert np.isfinite(o[0]) and np.isnan(o[1]) and np.isnan(o[2])

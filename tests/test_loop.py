@@ -142,3 +142,62 @@ def test_registered_caches_follow_the_loops_columns(seed, period, tree):
         if not loop.step(torch.from_numpy(nxt).to(dev)):
             break
     assert loop.generated() == ref_gen
+
+
+RATIO_CASES = [(0, False, 0.3, 1.0, {1, 2, 4}), (3, True, 0.3, 0.3, {1, 2, 4}),
+               (4, True, 1.0, 0.3, {0, 1, 2, 3, 4, 5}), (7, True, 0.5, 0.5, {0, 2, 3, 5})]
+
+
+def _ratio_cfg(tree, spec_t, tree_t):
+    return OA.StepConfig(pad_token_id=LC.PAD, eos_token_ids=(LC.EOS,), min_input_length=MIL,
+                         enable_tree_decode=tree, spec_thresh=spec_t, tree_thresh=tree_t)
+
+
+@pytest.mark.parametrize("seed,tree,spec_t,tree_t,text", RATIO_CASES)
+def test_oracle_ratio_loop_departs_from_exact(seed, tree, spec_t, tree_t, text):
+    """Thresholds below 1 change what the loop generates (the rules are
+    exercised), while a logits model at the default thresholds generates
+    exactly what the token model does."""
+    prompts, truths, drafts = LC.make_loop_case(seed)
+    model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
+    lm = LC.logits_model(model, seed)
+    ratio, _ = OL.reference_loop(prompts, drafts, model, _ratio_cfg(tree, spec_t, tree_t), 400,
+                                 logits_model=lm, text_mode=text)
+    exact_lm, _ = OL.reference_loop(prompts, drafts, model, _ratio_cfg(tree, 1.0, 1.0), 400,
+                                    logits_model=lm, text_mode=text)
+    exact, _ = OL.reference_loop(prompts, drafts, model, _cfg(tree), 400)
+    assert exact_lm == exact
+    assert ratio != exact
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("seed,tree,spec_t,tree_t,text", RATIO_CASES)
+def test_device_ratio_loop_follows_oracle_loop(seed, tree, spec_t, tree_t, text):
+    """The device loop below the default thresholds: per step the same
+    inputs as the oracle loop, the logits it reads listed by
+    ``logit_probes``, and the same generated tokens."""
+    from hsd_b200.loop import VerifyLoop
+    dev = torch.device("cuda:0")
+    prompts, truths, drafts = LC.make_loop_case(seed)
+    model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
+    lm = LC.logits_model(model, seed)
+    ref_gen, trace = OL.reference_loop(prompts, drafts, model, _ratio_cfg(tree, spec_t, tree_t),
+                                       400, logits_model=lm, text_mode=text)
+    loop = VerifyLoop(prompts, drafts, eos_token_id=LC.EOS, max_new_tokens=400,
+                      pad_token_id=LC.PAD, min_input_length=MIL, enable_tree_decode=tree,
+                      spec_thresh=spec_t, tree_thresh=tree_t, device=dev)
+    flags = [b in text for b in range(len(prompts))]
+    for it, ref in enumerate(trace):
+        ids, pos, mask = loop.inputs()
+        np.testing.assert_array_equal(ids.cpu().numpy(), ref["input_ids"], err_msg=f"step {it}")
+        np.testing.assert_array_equal(pos.cpu().numpy(), ref["position_ids"])
+        allowed = mask.plan().dense_allowed()
+        dense = lm(ref["input_ids"], ref["position_ids"], allowed, loop.kv_tokens.cpu().numpy())
+        nxt = np.argmax(dense, axis=1)
+        rows, toks = (t.cpu().numpy() for t in loop.logit_probes())
+        probe = np.where(toks >= 0, dense[rows, np.maximum(toks, 0)], 0).astype(np.float32)
+        max_l = dense[np.arange(len(nxt)), nxt].astype(np.float32)
+        more = loop.step(torch.from_numpy(nxt).to(dev), max_logit=torch.from_numpy(max_l).to(dev),
+                         probe_logit=torch.from_numpy(probe).to(dev), text_mode=flags)
+        assert more == (it + 1 < len(trace)), it
+    assert loop.generated() == ref_gen
