@@ -66,7 +66,11 @@ class AcceptConfig(C.Structure):
 
 class AcceptLogits(C.Structure):
     _fields_ = [("max_logit", C.c_void_p), ("probe_logit", C.c_void_p),
-                ("spec_thresh", C.c_float), ("tree_thresh", C.c_float)]
+                ("spec_thresh", C.c_float), ("tree_thresh", C.c_float),
+                ("variant", C.c_int32), ("formula_tokens", C.c_int32 * 2)]
+
+
+HSD_ACCEPT_DOTS, HSD_ACCEPT_HUNYUAN = 0, 1
 
 
 # (name, restype, argtypes) of every entry point include/hsd_b200.h declares.

@@ -50,14 +50,16 @@ def make_config(n_blocks, kv_len, q_len, words_stride, eos_ids, match_window_siz
 
 def accept_kmp(cfg, blocks, next_ids, input_ids, gen_pool, draft_pool, seg_kv_bits,
                out_kv_bits, filter_bits, tree_tokens=None, tree_parents=None, results=None,
-               status=None, stream=None, logits=None):
+               status=None, stream=None, logits=None, variant="dots",
+               formula_tokens=(3, 1099)):
     """Launch the acceptance kernel; all tensors are device int32 / int64.
 
     ``blocks``: int32 ``[n_blocks, 16]`` (updated in place);
     returns ``results`` int32 ``[n_blocks, 8]``.  ``logits = (max_logit,
     probe_logit, spec_thresh, tree_thresh)`` (float32 ``[Q]`` tensors, see
     ``hsd_accept_logits_t``) turns on the logit-ratio rules for thresholds
-    below 1.
+    below 1; ``variant="hunyuan"`` selects the HunYuan pipeline's rules
+    (H:1653-1858) with its formula delimiters ``formula_tokens``.
     """
     lib = N.load()
     if results is None:
@@ -80,8 +82,12 @@ def accept_kmp(cfg, blocks, next_ids, input_ids, gen_pool, draft_pool, seg_kv_bi
         if t is not None and (t.dtype != torch.float32 or not t.is_contiguous()
                               or t.numel() < input_ids.numel()):
             raise ValueError("max_logit / probe_logit: contiguous float32, one per packed row")
+    if variant not in ("dots", "hunyuan"):
+        raise ValueError(f"variant must be 'dots' or 'hunyuan', not {variant!r}")
     lg = N.AcceptLogits(N.ptr(max_logit), N.ptr(probe_logit), float(spec_thresh),
-                        float(tree_thresh))
+                        float(tree_thresh),
+                        N.HSD_ACCEPT_HUNYUAN if variant == "hunyuan" else N.HSD_ACCEPT_DOTS,
+                        (C.c_int32 * 2)(*[int(t) for t in formula_tokens]))
     N.check(lib.hsd_accept_kmp_logits(*args, C.byref(lg), N.ptr(status),
                                       N.stream_handle(stream)), "hsd_accept_kmp_logits")
     return results

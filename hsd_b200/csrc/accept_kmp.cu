@@ -36,7 +36,13 @@ struct Params {
   const float* probe_logit;
   float spec_thresh, tree_thresh;  // rounded to bf16
   int32_t spec_ratio, tree_ratio;
+  int32_t hunyuan;            // HSD_ACCEPT_HUNYUAN rules
+  int32_t formula[2];         // HunYuan formula delimiters
 };
+
+__device__ __forceinline__ bool is_formula(const Params& p, int tok) {
+  return tok == p.formula[0] || tok == p.formula[1];
+}
 
 // torch's bf16 quotient: the float32 quotient rounded to bf16 (D:1171, D:1233).
 __device__ __forceinline__ float logit_ratio(float num, float den) {
@@ -47,12 +53,12 @@ __device__ __forceinline__ float logit_ratio(float num, float den) {
 // token's logit over the row's maximal logit reaches the threshold and the
 // maximal logit is positive (D:1163-1174).
 __device__ __forceinline__ bool spec_ratio_pass(const Params& p, int row) {
-  if (!p.spec_ratio) return false;
   const float pred = p.max_logit[row];
   return pred > 0.f && logit_ratio(p.probe_logit[row], pred) >= p.spec_thresh;
 }
 
-// Tree walk fallback (D:1228-1238, D:1256-1266): when the target's token
+// Tree walk fallback (D:1228-1238, D:1256-1266, H:1791-1800, H:1821-1830):
+// when the target's token
 // `decode` is not a child of `node`, the child with the first maximal ratio
 // logits[row, child] / logits[row, decode] (torch.argmax; a NaN ratio counts
 // as maximal) replaces it, if any ratio reaches the threshold.  Children are
@@ -225,10 +231,31 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
     } else if (blk.mode == HSD_MODE_SPEC) {
       ptr = bs + blk.valid_count - 1;
       int diff = blen - 1;
+      // dots: every block (D:1147-1174); HunYuan: the last block only (H:1671)
+      const bool ratio = p.spec_ratio && (!p.hunyuan || b == cfg.n_blocks - 1);
+      // HunYuan formula state before the block's draft (H:1683-1688): the
+      // parity of delimiters among the generated tokens
+      int in_formula = 0;
+      if (ratio && p.hunyuan) {
+        int cnt = 0;
+        for (int i = lane; i < glen; i += 32) cnt += is_formula(p, gen[i]);
+        for (int off = 16; off; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
+        in_formula = cnt & 1;
+      }
       for (int base = 0; base < blen - 1; base += 32) {
         const int i = base + lane;
+        bool can_ratio = ratio;
+        if (ratio && p.hunyuan) {
+          // row i may use the ratio unless its draft token is a delimiter or
+          // the delimiters up to it leave a formula open (H:1689-1695)
+          const bool dollar = i < blen && is_formula(p, p.input_ids[bs + i]);
+          const uint32_t dm = __ballot_sync(0xffffffffu, dollar);
+          const int upto = in_formula + __popc(dm & (0xffffffffu >> (31 - lane)));
+          in_formula = (in_formula + __popc(dm)) & 1;
+          can_ratio = !dollar && !(upto & 1);
+        }
         const bool miss = (i < blen - 1) && (p.next_ids[bs + i] != p.input_ids[bs + i + 1]) &&
-                          !spec_ratio_pass(p, bs + i);
+                          !(can_ratio && spec_ratio_pass(p, bs + i));
         const uint32_t bal = __ballot_sync(0xffffffffu, miss);
         if (bal) {
           diff = base + __ffs(bal) - 1;
@@ -239,8 +266,10 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
         bad = true;
       } else {
         nxt = p.next_ids[bs + diff];
+        // accepted rows keep the draft's tokens (D:1184-1186); HunYuan keeps
+        // the model's (H:1750-1754)
         for (int i = lane; i <= diff; i += 32)
-          gen[glen + i] = (i < diff) ? p.input_ids[bs + i + 1] : nxt;
+          gen[glen + i] = (i < diff && !p.hunyuan) ? p.input_ids[bs + i + 1] : p.next_ids[bs + i];
         glen += diff + 1;
         inc = diff + 1;
         if (diff != blen - 1) {
@@ -410,8 +439,14 @@ static int accept_launch(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
     hsd_host::set_error("hsd_accept_kmp: bad arguments");
     return HSD_ERR_INVALID_ARG;
   }
+  if (logits && logits->variant != HSD_ACCEPT_DOTS && logits->variant != HSD_ACCEPT_HUNYUAN) {
+    hsd_host::set_error("hsd_accept_kmp_logits: unknown variant %d", logits->variant);
+    return HSD_ERR_INVALID_ARG;
+  }
+  const bool hunyuan = logits && logits->variant == HSD_ACCEPT_HUNYUAN;
   const bool spec_ratio = logits && logits->spec_thresh < 1.0f;
-  const bool tree_ratio = logits && logits->tree_thresh < 1.0f;
+  // HunYuan's tree fallback has no `< 1` guard (H:1791, H:1821)
+  const bool tree_ratio = logits && (hunyuan || logits->tree_thresh < 1.0f);
   if ((spec_ratio || tree_ratio) && (!logits->max_logit || !logits->probe_logit)) {
     hsd_host::set_error("hsd_accept_kmp_logits: a threshold below 1 needs max_logit and "
                         "probe_logit");
@@ -425,6 +460,9 @@ static int accept_launch(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
   // the reference compares bf16 ratios with the threshold rounded to bf16
   p.spec_thresh = spec_ratio ? __bfloat162float(__float2bfloat16_rn(logits->spec_thresh)) : 1.f;
   p.tree_thresh = tree_ratio ? __bfloat162float(__float2bfloat16_rn(logits->tree_thresh)) : 1.f;
+  p.hunyuan = hunyuan;
+  p.formula[0] = hunyuan ? logits->formula_tokens[0] : -1;
+  p.formula[1] = hunyuan ? logits->formula_tokens[1] : -1;
   p.cfg = *cfg;
   p.blocks = blocks;
   p.results = results;

@@ -49,6 +49,9 @@ from .trie import continuation_trees
 class VerifyLoop:
     """Region blocks verified in parallel, one :meth:`step` per forward.
 
+    ``variant="hunyuan"`` applies the HunYuan pipeline's acceptance and
+    compaction rules (H:1653-1858, H:2237-2285) in place of the dots ones.
+
     ``prompts[b]`` is block b's prefill input (its own prompt: blocks do not
     share KV columns, as in the reference's stage-1 packing, RD:232-245) and
     ``drafts[b]`` its tokenized draft.  ``kv_tokens`` (device int32, one
@@ -63,7 +66,8 @@ class VerifyLoop:
                  max_spec_len=0, compact_period=1, enable_tree_decode=False,
                  max_tree_depth=15, max_tree_len=256,
                  repeat_sentinel=DOTS_SENTINEL, kv_planes=None, row_bytes=0,
-                 kv_capacity=None, spec_thresh=1.0, tree_thresh=1.0, device="cuda"):
+                 kv_capacity=None, spec_thresh=1.0, tree_thresh=1.0, variant="dots",
+                 formula_tokens=(3, 1099), device="cuda"):
         if len(prompts) != len(drafts) or not prompts:
             raise ValueError("one draft per prompt, at least one block")
         self.device = torch.device(device)
@@ -84,7 +88,12 @@ class VerifyLoop:
         self.period = int(compact_period)
         self.sentinel = int(repeat_sentinel)
         self.spec_thresh, self.tree_thresh = float(spec_thresh), float(tree_thresh)
-        self.ratio = self.spec_thresh < 1.0 or self.tree_thresh < 1.0
+        if variant not in ("dots", "hunyuan"):
+            raise ValueError(f"variant must be 'dots' or 'hunyuan', not {variant!r}")
+        self.variant, self.formula_tokens = variant, tuple(int(t) for t in formula_tokens)
+        # HunYuan's tree fallback runs at any threshold in text mode (H:1791)
+        self.ratio = (self.spec_thresh < 1.0 or self.tree_thresh < 1.0
+                      or (variant == "hunyuan" and self.tree_decode))
         self.kv_planes, self.row_bytes = kv_planes, int(row_bytes)
         self.drafts = [list(map(int, d)) for d in drafts]
         lens = [len(p) for p in prompts]
@@ -249,7 +258,8 @@ class VerifyLoop:
                    tree_tokens=d_tok, tree_parents=d_par, results=self.results,
                    status=self.status,
                    logits=(max_logit, probe_logit, self.spec_thresh, self.tree_thresh)
-                   if self.ratio else None)
+                   if self.ratio else None, variant=self.variant,
+                   formula_tokens=self.formula_tokens)
         res = self.results.cpu().numpy()
         self._check()
 
@@ -325,8 +335,12 @@ class VerifyLoop:
         keep_bits, keep_idx, counts = keep_indices(live, self.filter, kv)
         n_keep = int(counts[0].item())
         dead = kv - n_keep
-        rule = self.period > 0 and (self.period <= 1 or self.decode_times % self.period == 0
-                                    or dead > kv * 0.2)
+        if self.variant == "hunyuan":   # period 0 compacts too (H:2253-2259)
+            rule = (self.period <= 1 or self.decode_times % self.period == 0
+                    or dead > kv * 0.2)
+        else:                           # D:1693-1700
+            rule = self.period > 0 and (self.period <= 1 or self.decode_times % self.period == 0
+                                        or dead > kv * 0.2)
         nw = (kv + 63) // 64
         if rule and n_keep < kv:                      # compact (D:1704-1723)
             if self.kv_planes is not None:

@@ -153,7 +153,18 @@ typedef struct {
    * probe_logit(child) / max_logit(node) if one reaches thresh (D:1228-1238,
    * D:1256-1266) */
   float tree_thresh;
+  /* HSD_ACCEPT_DOTS or HSD_ACCEPT_HUNYUAN.  HunYuan (H:1653-1858): the
+   * speculative ratio applies to the last block only, never inside a
+   * formula (rows whose draft token is a formula delimiter or lies between
+   * delimiters, counting from the block's generated tokens), and accepted
+   * rows keep the model's tokens; the tree fallback runs in text-mode
+   * blocks at any tree_thresh (H:1791-1800, no `< 1` guard) */
+  int32_t variant;
+  int32_t formula_tokens[2]; /* HunYuan formula delimiters: 3 ('$'), 1099 ('$$') */
 } hsd_accept_logits_t;
+
+#define HSD_ACCEPT_DOTS 0
+#define HSD_ACCEPT_HUNYUAN 1
 
 /* ---- library ---------------------------------------------------------- */
 const char *hsd_version(void);

@@ -10,6 +10,10 @@ Restates the token-level parts of one iteration of the reference's
 * tree-walk acceptance (D:1215-1293), with the logit-ratio fallback among a
   node's children below ``HSD_TREE_THRESH`` < 1 in text mode (D:1228-1238,
   D:1256-1266)
+* with ``variant="hunyuan"`` the HunYuan pipeline's rules
+  (hsd/hunyuan_ocr_pipeline/modeling_hunyuan_vl_hsd.py, H:1653-1858): the
+  speculative ratio on the last block only, outside formulas, accepted rows
+  keeping the model's tokens, and the tree fallback at any threshold
 * EOS and repetition stop (D:1299-1319)
 * KMP re-alignment of non-page blocks (D:1321-1336, D:1417-1419)
 * next block input: speculative slice, BFS tree, or normal (D:1421-1567)
@@ -57,8 +61,10 @@ class StepConfig:
     tight_pack: bool = False       # HSD_TIGHT_PACK (D:52)
     enable_tree_decode: bool = False
     repeat_sentinel: int = 20993   # dots (D:1306); HunYuan uses 41153 (H:1873)
-    spec_thresh: float = 1.0       # HSD_SPEC_THRESH (D:971)
-    tree_thresh: float = 1.0       # HSD_TREE_THRESH (D:970)
+    spec_thresh: float = 1.0       # HSD_SPEC_THRESH (D:971); SPEC_THRESH (H:1471)
+    tree_thresh: float = 1.0       # HSD_TREE_THRESH (D:970); fixed 1 in HunYuan (H:1470)
+    variant: str = "dots"          # "dots" (D) or "hunyuan" (H)
+    formula_tokens: tuple = (3, 1099)   # HunYuan '$' and '$$' (H:1685)
 
 
 def bf16_f32(x):
@@ -113,7 +119,7 @@ def _window_update(st, cfg, increment):
 
 
 def accept_block(st, bs, be, next_list, input_list, cfg, filt, kv_base,
-                 allowed_row_fn, is_page_block, logits=None):
+                 allowed_row_fn, is_page_block, logits=None, is_last_block=False):
     """Acceptance for one block; mutates ``st`` and ``filt``.
 
     Returns ``(pointer, next_token, increment, finished_reason)`` where
@@ -144,21 +150,37 @@ def accept_block(st, bs, be, next_list, input_list, cfg, filt, kv_base,
         ref = input_list[bs:be]
         blen = be - bs
         acc = [group[i] == ref[i + 1] for i in range(blen - 1)]
-        if cfg.spec_thresh < 1.0:                              # D:1147-1174
+        hunyuan = cfg.variant == "hunyuan"
+        thresh = cfg.spec_thresh if (not hunyuan or is_last_block) else 1.0   # H:1671
+        if thresh < 1.0:                                       # D:1147-1174, H:1676-1744
             max_l, probe_l = logits
+            can = [True] * len(acc)
+            if hunyuan:                                        # H:1681-1695
+                in_formula = False
+                for t in st.gen:
+                    if t in cfg.formula_tokens:
+                        in_formula = not in_formula
+                for fi in range(blen):
+                    dollar = ref[fi] in cfg.formula_tokens
+                    if dollar:
+                        in_formula = not in_formula
+                    if fi < len(acc):
+                        can[fi] = (not in_formula) and (not dollar)
             first_miss = next((i for i, ok in enumerate(acc) if not ok), len(acc))
             for i in range(first_miss, len(acc)):
                 pred = np.float32(max_l[bs + i])
-                acc[i] = acc[i] or (bool(pred > 0) and
-                                    ratio_passes(probe_l[bs + i], pred, cfg.spec_thresh))
+                if can[i]:
+                    acc[i] = acc[i] or (bool(pred > 0) and
+                                        ratio_passes(probe_l[bs + i], pred, thresh))
         diff = len(acc)
         for i, ok in enumerate(acc):
             if not ok:
                 diff = i
                 break
         accepted = list(group[:diff + 1])
-        for i in range(diff):
-            accepted[i] = ref[i + 1]
+        if not hunyuan:                # HunYuan keeps the model's tokens (H:1750-1754)
+            for i in range(diff):
+                accepted[i] = ref[i + 1]
         st.gen.extend(accepted)
         inc = diff + 1
         nxt = group[diff]
@@ -173,7 +195,8 @@ def accept_block(st, bs, be, next_list, input_list, cfg, filt, kv_base,
         consumed = [False] * n_nodes
 
         def fallback(node, decode):                            # D:1228-1238
-            if not (cfg.tree_thresh < 1.0 and st.text_mode):
+            # HunYuan runs the fallback at any threshold (H:1791, H:1821)
+            if not ((cfg.variant == "hunyuan" or cfg.tree_thresh < 1.0) and st.text_mode):
                 return decode
             if any(parents[c] == node and tokens[c] == decode for c in range(node + 1, n_nodes)):
                 return decode

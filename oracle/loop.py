@@ -108,7 +108,7 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
             st.text_mode = b in text_mode
             ptr, nxt, inc, fin = accept_block(st, bs, be, next_list, input_list, cfg, filt,
                                               kv_base, lambda row: allowed[row], False,
-                                              logits=logits)
+                                              logits=logits, is_last_block=(b == nb - 1))
             pointer[b] = ptr
             new_tokens += inc
             bs = be
@@ -132,7 +132,8 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
         filt = pad_filter(filt, input_ids, cfg.pad_token_id)
         active = [pointer[b] for b in range(nb) if states[b].mode != FINISHED]
         keep = keep_columns(allowed, active, filt)
-        action = compaction_action(kv, int(keep.sum()), decode_times, compact_period)
+        action = compaction_action(kv, int(keep.sum()), decode_times, compact_period,
+                                   hunyuan=cfg.variant == "hunyuan")
         step["action"] = action
         mask = apply_to_mask(mask, keep, action)
         if action == "compact":

@@ -20,7 +20,7 @@ EOS = 99991
 CAP = 2048
 
 
-def make_scenario(seed, n_blocks=12, tight=False, vocab=None):
+def make_scenario(seed, n_blocks=12, tight=False, vocab=None, last_mode=None):
     rng = np.random.default_rng(seed)
     vocab = vocab or int(rng.choice([4, 8, 30, 151936]))
     kv_old = int(rng.integers(100, 600))
@@ -31,6 +31,8 @@ def make_scenario(seed, n_blocks=12, tight=False, vocab=None):
         mode = int(rng.choice([OA.NORMAL, OA.SPEC, OA.SPEC, OA.TREE, OA.FINISHED]))
         if b in (0, 3):
             mode = OA.NORMAL  # 0: prefill-style block (causal rows); 3: repetition
+        if b == n_blocks - 1 and last_mode is not None:
+            mode = last_mode
         dlen = int(rng.integers(0, 300)) if rng.random() > 0.1 else 0
         draft = [int(x) for x in rng.integers(1, vocab, dlen)]
         if draft and rng.random() < 0.7:
@@ -134,9 +136,9 @@ def make_logits(sc, seed, thresh):
 
 
 def run_oracle(sc, page_block=None, logits=None, spec_thresh=1.0, tree_thresh=1.0,
-               text_mode=()):
+               text_mode=(), variant="dots", formula_tokens=(3, 1099)):
     cfg = OA.StepConfig(pad_token_id=PAD, eos_token_ids=sc["eos"], spec_thresh=spec_thresh,
-                        tree_thresh=tree_thresh)
+                        tree_thresh=tree_thresh, variant=variant, formula_tokens=formula_tokens)
     allowed = OM.segments_to_allowed(sc["q_len"], sc["kv_len"], sc["segs"])
     filt = np.zeros(sc["kv_len"], bool)
     kv_base = sc["kv_len"] - sc["q_len"]
@@ -157,7 +159,8 @@ def run_oracle(sc, page_block=None, logits=None, spec_thresh=1.0, tree_thresh=1.
         bs, be = blk["q_start"], blk["q_start"] + blk["q_len"]
         ptr, nxt, inc, fin = OA.accept_block(
             st, bs, be, sc["next_ids"], sc["input_ids"], cfg, filt, kv_base,
-            lambda row: allowed[row], is_page_block=(i == page_block), logits=logits)
+            lambda row: allowed[row], is_page_block=(i == page_block), logits=logits,
+            is_last_block=(i == len(sc["blocks"]) - 1))
         r.update(finished=fin, increment=inc, pointer=ptr, next_token=nxt)
         if not fin and i != page_block:
             window, matches, _ = OA.realign_block(st, cfg)

@@ -22,7 +22,8 @@ def dev():
     return torch.device("cuda:0")
 
 
-def run_kernel(sc, dev, page_block=None, logits=None, text_mode=()):
+def run_kernel(sc, dev, page_block=None, logits=None, text_mode=(), variant="dots",
+               formula_tokens=(3, 1099)):
     from hsd_b200 import accept as A
     from hsd_b200.plan import pack_bits
     nb = len(sc["blocks"])
@@ -73,7 +74,8 @@ def run_kernel(sc, dev, page_block=None, logits=None, text_mode=()):
                        status=status,
                        logits=None if logits is None else (
                            torch.from_numpy(logits[0]).to(dev), torch.from_numpy(logits[1]).to(dev),
-                           logits[2], logits[3]))
+                           logits[2], logits[3]),
+                       variant=variant, formula_tokens=formula_tokens)
     torch.cuda.synchronize()
     assert status.item() == 0, hex(status.item())
     return (res.cpu().numpy(), d_blocks.cpu().numpy(), d_gen.cpu().numpy(),
@@ -135,3 +137,23 @@ def test_accept_logit_ratio_matches_oracle(dev, seed, spec_thresh, tree_thresh):
                      logits=(max_l, probe, spec_thresh, tree_thresh))
     compare(sc, seed, expect, filt, out)
 
+
+@pytest.mark.parametrize("seed", list(range(24)))
+@pytest.mark.parametrize("spec_thresh", [0.5, 1.0])
+def test_accept_hunyuan_rules_match_oracle(dev, seed, spec_thresh):
+    """HunYuan's rules (H:1653-1858) bit-exact vs the oracle: the ratio on
+    the last block only (made speculative), formula rows exact-only (the
+    delimiters made frequent: tokens 3 and 5 on small vocabularies),
+    accepted rows keeping the model's tokens, and the tree fallback in
+    text-mode blocks at threshold 1."""
+    sc = AC.make_scenario(seed, tight=bool(seed % 2), last_mode=OA.SPEC)
+    formula = (3, 5) if seed % 4 else (3, 1099)
+    max_l, probe = AC.make_logits(sc, seed, 0.5)
+    rng = np.random.default_rng(seed)
+    text_mode = {i for i in range(len(sc["blocks"])) if rng.random() < 0.6}
+    expect, filt = AC.run_oracle(sc, logits=(max_l, probe), spec_thresh=spec_thresh,
+                                 tree_thresh=1.0, text_mode=text_mode, variant="hunyuan",
+                                 formula_tokens=formula)
+    out = run_kernel(sc, dev, text_mode=text_mode, logits=(max_l, probe, spec_thresh, 1.0),
+                     variant="hunyuan", formula_tokens=formula)
+    compare(sc, seed, expect, filt, out)

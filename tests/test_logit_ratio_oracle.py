@@ -130,3 +130,53 @@ def test_accept_logit_ratio_changes_decisions():
                 spec_gain += blk["mode"] == OA.SPEC
                 tree_gain += blk["mode"] == OA.TREE
     assert spec_gain > 0 and tree_gain > 0, (spec_gain, tree_gain)
+
+
+def _hy_cfg(**kw):
+    return OA.StepConfig(pad_token_id=0, eos_token_ids=(2,), spec_thresh=0.5, variant="hunyuan",
+                         formula_tokens=(3, 1099), **kw)
+
+
+def _hy_spec(gen, input_ids, next_ids, max_l, probe, last=True):
+    st = OA.BlockState(mode=OA.SPEC, gen=list(gen), draft=[], valid_count=len(input_ids))
+    n = len(input_ids)
+    filt = np.zeros(32 + n, bool)
+    out = OA.accept_block(st, 0, n, next_ids, input_ids, _hy_cfg(), filt, 32,
+                          lambda r: np.zeros(32 + n, bool), False,
+                          logits=(np.asarray(max_l, np.float32), np.asarray(probe, np.float32)),
+                          is_last_block=last)
+    return st, out
+
+
+def test_hunyuan_ratio_keeps_model_tokens_and_last_block_only():
+    """H:1671, H:1750-1754: the ratio applies to the last block only and an
+    accepted row keeps the model's token, not the draft's."""
+    ids, nxt = [5, 6, 7, 8], [9, 10, 11, 12]        # every row misses
+    max_l, probe = [4.0] * 4, [3.0, 3.0, 1.0, 0.0]  # ratios .75 .75 .25
+    st, (ptr, tok, inc, _) = _hy_spec([4], ids, nxt, max_l, probe)
+    assert st.gen == [4, 9, 10, 11] and (ptr, tok, inc) == (2, 11, 3)
+    st, (ptr, tok, inc, _) = _hy_spec([4], ids, nxt, max_l, probe, last=False)
+    assert st.gen == [4, 9] and (ptr, inc) == (0, 1)
+
+
+def test_hunyuan_formula_rows_need_exact_match():
+    """H:1681-1695: rows whose draft token is a delimiter, or that lie inside
+    a formula opened by the generated tokens or the draft, use exact match
+    only."""
+    ratio_ok = ([4.0] * 6, [3.0] * 6)               # every ratio .75 passes
+    nxt = [20, 21, 22, 23, 24, 25]                  # every row misses
+    # no formula: all rows accepted by the ratio
+    st, (_, _, inc, _) = _hy_spec([4], [5, 6, 7, 8, 9, 10], nxt, *ratio_ok)
+    assert inc == 6
+    # a '$' in the generated text opens a formula: row 0 is inside it
+    st, (_, _, inc, _) = _hy_spec([4, 3, 6], [5, 6, 7, 8, 9, 10], nxt, *ratio_ok)
+    assert inc == 1
+    # the draft's row 2 closes it ('$$' also toggles): row 2 is a delimiter
+    # (exact only), rows 0-1 inside; with exact matches on rows 0-2 the
+    # ratio takes over from row 3
+    ids = [5, 6, 1099, 8, 9, 10]
+    nxt_exact = [6, 1099, 8, 23, 24, 25]
+    st, (_, _, inc, _) = _hy_spec([4, 3], ids, nxt_exact, *ratio_ok)
+    assert inc == 6
+    st, (_, _, inc, _) = _hy_spec([4, 3], ids, [6, 1099, 22, 23, 24, 25], *ratio_ok)
+    assert inc == 3                                 # row 2 (a delimiter) misses

@@ -148,9 +148,10 @@ RATIO_CASES = [(0, False, 0.3, 1.0, {1, 2, 4}), (3, True, 0.3, 0.3, {1, 2, 4}),
                (4, True, 1.0, 0.3, {0, 1, 2, 3, 4, 5}), (7, True, 0.5, 0.5, {0, 2, 3, 5})]
 
 
-def _ratio_cfg(tree, spec_t, tree_t):
+def _ratio_cfg(tree, spec_t, tree_t, variant="dots"):
     return OA.StepConfig(pad_token_id=LC.PAD, eos_token_ids=(LC.EOS,), min_input_length=MIL,
-                         enable_tree_decode=tree, spec_thresh=spec_t, tree_thresh=tree_t)
+                         enable_tree_decode=tree, spec_thresh=spec_t, tree_thresh=tree_t,
+                         variant=variant, formula_tokens=(3, 5))
 
 
 @pytest.mark.parametrize("seed,tree,spec_t,tree_t,text", RATIO_CASES)
@@ -170,22 +171,47 @@ def test_oracle_ratio_loop_departs_from_exact(seed, tree, spec_t, tree_t, text):
     assert ratio != exact
 
 
+HUNYUAN_CASES = [(3, True, 0.5, 1.0, {0, 1, 2, 3, 4, 5}, 0), (0, False, 0.3, 1.0, {5}, 2),
+                 (8, True, 0.5, 1.0, {1, 3, 5}, 0)]
+
+
+@pytest.mark.parametrize("seed,tree,spec_t,tree_t,text,period", HUNYUAN_CASES)
+def test_oracle_hunyuan_loop_departs_from_dots(seed, tree, spec_t, tree_t, text, period):
+    """The HunYuan rules (last-block ratio outside formulas, model tokens
+    kept, tree fallback at threshold 1, period-0 compaction) generate
+    differently from the dots rules on the same logits."""
+    prompts, truths, drafts = LC.make_loop_case(seed)
+    model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
+    lm = LC.logits_model(model, seed)
+    hy, hy_trace = OL.reference_loop(prompts, drafts, model,
+                                     _ratio_cfg(tree, spec_t, tree_t, "hunyuan"), 400,
+                                     compact_period=period, logits_model=lm, text_mode=text)
+    dots, dots_trace = OL.reference_loop(prompts, drafts, model, _ratio_cfg(tree, spec_t, tree_t),
+                                         400, compact_period=period, logits_model=lm,
+                                         text_mode=text)
+    assert hy != dots or [s["action"] for s in hy_trace] != [s["action"] for s in dots_trace]
+
+
 @pytest.mark.gpu
-@pytest.mark.parametrize("seed,tree,spec_t,tree_t,text", RATIO_CASES)
-def test_device_ratio_loop_follows_oracle_loop(seed, tree, spec_t, tree_t, text):
-    """The device loop below the default thresholds: per step the same
-    inputs as the oracle loop, the logits it reads listed by
-    ``logit_probes``, and the same generated tokens."""
+@pytest.mark.parametrize("seed,tree,spec_t,tree_t,text,variant,period",
+                         [c + ("dots", 1) for c in RATIO_CASES] +
+                         [c[:5] + ("hunyuan", c[5]) for c in HUNYUAN_CASES])
+def test_device_ratio_loop_follows_oracle_loop(seed, tree, spec_t, tree_t, text, variant, period):
+    """The device loop below the default thresholds (and with the HunYuan
+    rules): per step the same inputs as the oracle loop, the logits it reads
+    listed by ``logit_probes``, and the same generated tokens."""
     from hsd_b200.loop import VerifyLoop
     dev = torch.device("cuda:0")
     prompts, truths, drafts = LC.make_loop_case(seed)
     model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
     lm = LC.logits_model(model, seed)
-    ref_gen, trace = OL.reference_loop(prompts, drafts, model, _ratio_cfg(tree, spec_t, tree_t),
-                                       400, logits_model=lm, text_mode=text)
+    ref_gen, trace = OL.reference_loop(prompts, drafts, model,
+                                       _ratio_cfg(tree, spec_t, tree_t, variant), 400,
+                                       compact_period=period, logits_model=lm, text_mode=text)
     loop = VerifyLoop(prompts, drafts, eos_token_id=LC.EOS, max_new_tokens=400,
                       pad_token_id=LC.PAD, min_input_length=MIL, enable_tree_decode=tree,
-                      spec_thresh=spec_t, tree_thresh=tree_t, device=dev)
+                      spec_thresh=spec_t, tree_thresh=tree_t, variant=variant,
+                      formula_tokens=(3, 5), compact_period=period, device=dev)
     flags = [b in text for b in range(len(prompts))]
     for it, ref in enumerate(trace):
         ids, pos, mask = loop.inputs()
