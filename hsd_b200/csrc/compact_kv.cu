@@ -159,7 +159,22 @@ __global__ void __launch_bounds__(kBulkThreads, 1) compact_plane_bulk_kernel(
     *abort = 0;
     fence_barrier_init();
   }
-  for (int i = threadIdx.x; i < n_cached; i += kBulkThreads) s_idx[i] = keep_idx[first + i];
+  // Stage the indices with eight loads in flight per thread (one round of
+  // global latency for up to 2048 indices) before the first wave is issued.
+  constexpr int kFill = 8;
+  for (int i0 = 0; i0 < n_cached; i0 += kFill * kBulkThreads) {
+    int v[kFill];
+#pragma unroll
+    for (int u = 0; u < kFill; ++u) {
+      const int i = i0 + u * kBulkThreads + int(threadIdx.x);
+      v[u] = i < n_cached ? keep_idx[first + i] : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kFill; ++u) {
+      const int i = i0 + u * kBulkThreads + int(threadIdx.x);
+      if (i < n_cached) s_idx[i] = v[u];
+    }
+  }
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int rows_per_wave = kBulkBuf / row_bytes;

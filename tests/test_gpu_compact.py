@@ -60,6 +60,9 @@ def test_compact_matches_index_select(dev, layers, hkv, kv, dead, first):
     (80, 512, 3000, 0.3, 200),      # 512-byte rows (head dim 256), bulk kernel
     (70, 64 * 1024, 40, 0.4, 1),    # rows larger than a staging buffer: cluster kernel
     (4, 1024, 2000, 0.5, 10),       # few planes: cluster kernel
+    (100, 256, 300, 0.2, 100),      # two CTAs per plane, one wave: the second has none
+    (148, 1024, 5000, 0.3, 7),      # two CTAs per plane, one plane per SM, 32-row waves
+    (149, 256, 2000, 0.3, 5),       # more planes than SMs: one CTA per plane
 ])
 def test_compact_row_sizes_and_long_moves(dev, n_planes, row_bytes, kv, dead, first):
     """Planes of raw rows of any 16-byte multiple move like index_select,
