@@ -28,8 +28,9 @@ input.  Below the default thresholds (``spec_thresh`` / ``tree_thresh`` < 1,
 HSD_SPEC_THRESH / HSD_TREE_THRESH, D:970-971) the logit-ratio rules apply:
 :meth:`VerifyLoop.logit_probes` lists the logits they read, and
 :meth:`VerifyLoop.step` takes them with the maximal logit per row.
-Not driven by this loop: tight packing (HSD_TIGHT_PACK) and the page block's
-tokenizer-driven parsers.
+With ``tight_pack`` (HSD_TIGHT_PACK) blocks are not padded to
+``min_input_length`` and the packed input is padded to a multiple of 128
+rows.  Not driven by this loop: the page block's tokenizer-driven parsers.
 """
 from __future__ import annotations
 
@@ -44,6 +45,8 @@ from .accept import DOTS_SENTINEL, FLAG_TEXT_MODE, F, R, accept_kmp, make_config
 from .compaction import compact_bits, compact_kv, keep_indices
 from .plan import SEG_CAUSAL, SEG_NONE, SEG_SINGLE, SEG_TREE, PackedMask, pack_bits
 from .trie import continuation_trees
+
+Q_BLOCK = 128  # _HSD_Q_BLOCK (D:53): tight-packed inputs are padded to a multiple of it
 
 
 class VerifyLoop:
@@ -63,7 +66,7 @@ class VerifyLoop:
 
     def __init__(self, prompts, drafts, *, eos_token_id, max_new_tokens, pad_token_id=0,
                  match_window_size=3, match_window_size_upper_bound=10, min_input_length=128,
-                 max_spec_len=0, compact_period=1, enable_tree_decode=False,
+                 max_spec_len=0, compact_period=1, enable_tree_decode=False, tight_pack=False,
                  max_tree_depth=15, max_tree_len=256,
                  repeat_sentinel=DOTS_SENTINEL, kv_planes=None, row_bytes=0,
                  kv_capacity=None, spec_thresh=1.0, tree_thresh=1.0, variant="dots",
@@ -82,6 +85,7 @@ class VerifyLoop:
         self.mil = int(min_input_length)
         self.max_spec_len = int(max_spec_len)
         self.tree_decode = bool(enable_tree_decode)
+        self.tight = bool(tight_pack)
         self.tree_depth = int(max_tree_depth)
         self.tree_cap = (min(int(max_tree_len), self.max_spec_len) if self.max_spec_len > 0
                          else int(max_tree_len))
@@ -297,7 +301,8 @@ class VerifyLoop:
             if r[R["match_count"]] == 1:
                 toks = self.drafts[b][int(r[R["slice_begin"]]):int(r[R["slice_end"]])]
                 n = len(toks)
-                toks = toks + [self.pad] * (math.ceil(n / self.mil) * self.mil - n)
+                if not self.tight:
+                    toks = toks + [self.pad] * (math.ceil(n / self.mil) * self.mil - n)
                 new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_SPEC, SEG_CAUSAL, n
                 pos = list(range(base, base + len(toks)))
             else:
@@ -305,13 +310,14 @@ class VerifyLoop:
                 if tree is not None and len(tree[0]) > 1:    # D:1488-1543
                     tokens, depths, new_parents[b] = tree
                     n = len(tokens)
-                    pad_n = math.ceil(n / self.mil) * self.mil - n
+                    pad_n = 0 if self.tight else math.ceil(n / self.mil) * self.mil - n
                     toks = list(tokens) + [self.pad] * pad_n
                     pos = [d + base for d in depths] + [0] * pad_n
                     new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_TREE, SEG_TREE, n
                 else:                                        # D:1544-1565
-                    toks = [int(r[R["next_token"]])] + [self.pad] * (self.mil - 1)
-                    pos = [base] + [0] * (self.mil - 1)
+                    fill = 0 if self.tight else self.mil - 1
+                    toks = [int(r[R["next_token"]])] + [self.pad] * fill
+                    pos = [base] + [0] * fill
                     new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_NORMAL, SEG_SINGLE, 1
             new_ids.append(toks)
             new_pos.append(pos)
@@ -357,7 +363,16 @@ class VerifyLoop:
             self.seg_bits = self.out_bits.clone()
         self.compaction_s += time.perf_counter() - t_c
 
-        # the next packed input and its KV columns
+        # the next packed input and its KV columns; tight packing pads the
+        # input to a multiple of 128 rows at position 0 that belong to no
+        # block (D:1619-1632): they see no column (the reference's dots loop
+        # lets them inherit the last block's row, D:1640-1644, HunYuan masks
+        # them, H:2290-2293); no block reads their outputs and the pad filter
+        # drops their columns, so tokens and compaction are the same
+        if self.tight and sum(new_lens) % Q_BLOCK:
+            pad_n = Q_BLOCK - sum(new_lens) % Q_BLOCK
+            new_ids.append([self.pad] * pad_n)
+            new_pos.append([0] * pad_n)
         self.input_ids = np.concatenate([np.asarray(t, dtype=np.int64) for t in new_ids])
         self.position_ids = np.concatenate([np.asarray(t, dtype=np.int64) for t in new_pos])
         ends = np.cumsum(new_lens)

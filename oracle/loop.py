@@ -12,6 +12,9 @@ iteration (hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py):
   (D:1103-1567), the generation-finished test (D:1589-1591), the pad filter
   (D:1596-1599), keep columns and the compaction rule (D:1679-1731), the next
   dense mask (D:1634-1667, D:1737-1748) and the next pointer (D:1604-1606);
+  with ``cfg.tight_pack`` (HSD_TIGHT_PACK) blocks are not padded and the
+  packed input is padded to a multiple of 128 rows that belong to no block
+  (D:1619-1632, D:1640-1644);
 * the KV cache grows by the packed input of every forward (DynamicCache) and
   loses the compacted columns.
 
@@ -32,6 +35,8 @@ from .accept import (FINISHED, SPEC, TREE, BlockState, accept_block, next_block_
 from .compact import apply_to_mask, compaction_action, keep_columns, pad_filter
 from .masks import (assemble_next_mask, initial_packed_mask, normal_block_mask,
                     spec_block_mask, tree_block_mask)
+
+Q_BLOCK = 128  # _HSD_Q_BLOCK (D:53): tight-packed inputs are padded to a multiple of it
 
 
 def ratio_logits(logits, next_ids, input_ids, spans, states):
@@ -91,7 +96,8 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
             next_ids = np.asarray(model(input_ids, position_ids, allowed, kv_tokens),
                                   dtype=np.int64)
         step = dict(input_ids=input_ids.copy(), position_ids=position_ids.copy(),
-                    allowed=allowed.copy(), modes=[st.mode for st in states])
+                    allowed=allowed.copy(), modes=[st.mode for st in states],
+                    q_blocks=pointer[-1] + 1)   # rows owned by blocks (the rest: tight padding)
         trace.append(step)
         kv_base = kv - q
         filt = np.zeros(kv, dtype=bool)
@@ -138,7 +144,14 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
         mask = apply_to_mask(mask, keep, action)
         if action == "compact":
             kv_tokens = kv_tokens[keep]
-        mask = assemble_next_mask(mask, pointer, new_lens, new_masks)
+        # HSD_TIGHT_PACK: the packed input is padded to a multiple of
+        # _HSD_Q_BLOCK with pad tokens at position 0 (D:1619-1632)
+        pad_n = (-sum(new_lens)) % Q_BLOCK if cfg.tight_pack else 0
+        mask = assemble_next_mask(mask, pointer, new_lens, new_masks, tight_pad_len=pad_n,
+                                  hunyuan=cfg.variant == "hunyuan")
+        if pad_n:
+            new_ids.append([cfg.pad_token_id] * pad_n)
+            new_pos.append([0] * pad_n)
         input_ids = np.concatenate([np.asarray(x, dtype=np.int64) for x in new_ids])
         position_ids = np.concatenate([np.asarray(x, dtype=np.int64) for x in new_pos])
         kv_tokens = np.concatenate([kv_tokens, input_ids])

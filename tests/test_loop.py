@@ -18,9 +18,9 @@ from tests import loop_cases as LC
 MIL = 16
 
 
-def _cfg(tree=False):
+def _cfg(tree=False, tight=False):
     return OA.StepConfig(pad_token_id=LC.PAD, eos_token_ids=(LC.EOS,), min_input_length=MIL,
-                         enable_tree_decode=tree)
+                         enable_tree_decode=tree, tight_pack=tight)
 
 
 @pytest.mark.parametrize("seed,tree", [(0, False), (1, False), (2, False), (3, True),
@@ -40,20 +40,43 @@ def test_oracle_loop_reproduces_true_texts(seed, tree):
     assert len(trace) < max(len(t) for t in truths)
 
 
+@pytest.mark.parametrize("seed,tree", [(0, False), (2, False), (3, True)])
+def test_oracle_tight_loop_reproduces_true_texts(seed, tree):
+    """HSD_TIGHT_PACK: unpadded blocks, the packed input padded to a
+    multiple of 128 rows (D:1619-1632); the texts are those of the padded
+    loop, with fewer packed rows."""
+    prompts, truths, drafts = LC.make_loop_case(seed)
+    model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
+    gen, trace = OL.reference_loop(prompts, drafts, model, _cfg(tree, tight=True),
+                                   max_new_tokens=10 ** 6)
+    gen_pad, trace_pad = OL.reference_loop(prompts, drafts, model, _cfg(tree),
+                                           max_new_tokens=10 ** 6)
+    assert gen == gen_pad
+    for s in trace[1:]:
+        assert len(s["input_ids"]) % OL.Q_BLOCK == 0
+        assert (s["input_ids"][s["q_blocks"]:] == LC.PAD).all()
+        assert not s["allowed"][s["q_blocks"]:, -len(s["input_ids"]):].any()
+    assert sum(s["q_blocks"] for s in trace[1:]) < sum(len(s["input_ids"]) for s in trace_pad[1:])
+
+
 @pytest.mark.gpu
-@pytest.mark.parametrize("seed,period,tree", [(0, 1, False), (1, 1, False), (2, 3, False),
-                                              (3, 1, True), (4, 2, True)])
-def test_device_loop_follows_oracle_loop(seed, period, tree):
+@pytest.mark.parametrize("seed,period,tree,tight", [
+    (0, 1, False, False), (1, 1, False, False), (2, 3, False, False), (3, 1, True, False),
+    (4, 2, True, False), (0, 1, False, True), (2, 2, False, True), (3, 1, True, True)])
+def test_device_loop_follows_oracle_loop(seed, period, tree, tight):
+    """Same inputs, positions, mask and tokens at every step.  With tight
+    packing the rows past the blocks see no column on the device (no block
+    reads them, their columns are filtered); the block rows' masks match."""
     from hsd_b200.loop import VerifyLoop
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
     dev = torch.device("cuda:0")
     prompts, truths, drafts = LC.make_loop_case(seed)
     model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
-    ref_gen, trace = OL.reference_loop(prompts, drafts, model, _cfg(tree),
+    ref_gen, trace = OL.reference_loop(prompts, drafts, model, _cfg(tree, tight),
                                        max_new_tokens=10 ** 6, compact_period=period)
     loop = VerifyLoop(prompts, drafts, eos_token_id=LC.EOS, max_new_tokens=10 ** 6,
                       pad_token_id=LC.PAD, min_input_length=MIL, compact_period=period,
-                      enable_tree_decode=tree, device=dev)
+                      enable_tree_decode=tree, tight_pack=tight, device=dev)
     for it, ref in enumerate(trace):
         ids, pos, mask = loop.inputs()
         np.testing.assert_array_equal(ids.cpu().numpy(), ref["input_ids"], err_msg=f"step {it}")
@@ -62,7 +85,9 @@ def test_device_loop_follows_oracle_loop(seed, period, tree):
         allowed = plan.dense_allowed()
         plan.raise_on_device_error()
         assert allowed.shape == ref["allowed"].shape, (it, allowed.shape, ref["allowed"].shape)
-        np.testing.assert_array_equal(allowed, ref["allowed"], err_msg=f"mask, step {it}")
+        qb = ref["q_blocks"]
+        np.testing.assert_array_equal(allowed[:qb], ref["allowed"][:qb], err_msg=f"mask, step {it}")
+        assert not allowed[qb:].any(), it
         kv_tokens = loop.kv_tokens.cpu().numpy()
         nxt = model(ref["input_ids"], ref["position_ids"], allowed, kv_tokens)
         more = loop.step(torch.from_numpy(nxt).to(dev))
