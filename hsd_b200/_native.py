@@ -67,10 +67,14 @@ class AcceptConfig(C.Structure):
 class AcceptLogits(C.Structure):
     _fields_ = [("max_logit", C.c_void_p), ("probe_logit", C.c_void_p),
                 ("spec_thresh", C.c_float), ("tree_thresh", C.c_float),
-                ("variant", C.c_int32), ("formula_tokens", C.c_int32 * 2)]
+                ("variant", C.c_int32), ("formula_tokens", C.c_int32 * 2),
+                ("spec_mode", C.c_int32), ("spec_topk", C.c_int32), ("spec_margin", C.c_float),
+                ("rank", C.c_void_p), ("second", C.c_void_p)]
 
 
 HSD_ACCEPT_DOTS, HSD_ACCEPT_HUNYUAN = 0, 1
+HSD_SPEC_FMST, HSD_SPEC_TOPK, HSD_SPEC_ADAPTIVE = 0, 1, 2
+SPEC_MODES = {"fmst": HSD_SPEC_FMST, "topk": HSD_SPEC_TOPK, "adaptive": HSD_SPEC_ADAPTIVE}
 
 
 # (name, restype, argtypes) of every entry point include/hsd_b200.h declares.
@@ -109,6 +113,8 @@ SIGNATURES = [
     ("hsd_lm_head_argmax_workspace_bytes", _SZ, [_I32]),
     ("hsd_lm_head_argmax", C.c_int,
      [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _SZ, _P, _P]),
+    ("hsd_lm_head_rank", C.c_int,
+     [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     ("hsd_probe_logits", C.c_int,
      [_P, _I64, _P, _I64, _I32, _I32, _I32, _P, _P, _I32, _P, _P, _P]),
 ]

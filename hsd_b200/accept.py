@@ -51,7 +51,8 @@ def make_config(n_blocks, kv_len, q_len, words_stride, eos_ids, match_window_siz
 def accept_kmp(cfg, blocks, next_ids, input_ids, gen_pool, draft_pool, seg_kv_bits,
                out_kv_bits, filter_bits, tree_tokens=None, tree_parents=None, results=None,
                status=None, stream=None, logits=None, variant="dots",
-               formula_tokens=(3, 1099)):
+               formula_tokens=(3, 1099), spec_mode="fmst", spec_topk=3, spec_margin=2.0,
+               rank=None, second=None):
     """Launch the acceptance kernel; all tensors are device int32 / int64.
 
     ``blocks``: int32 ``[n_blocks, 16]`` (updated in place);
@@ -59,7 +60,11 @@ def accept_kmp(cfg, blocks, next_ids, input_ids, gen_pool, draft_pool, seg_kv_bi
     probe_logit, spec_thresh, tree_thresh)`` (float32 ``[Q]`` tensors, see
     ``hsd_accept_logits_t``) turns on the logit-ratio rules for thresholds
     below 1; ``variant="hunyuan"`` selects the HunYuan pipeline's rules
-    (H:1653-1858) with its formula delimiters ``formula_tokens``.
+    (H:1653-1858) with its formula delimiters ``formula_tokens`` and its
+    ``spec_mode`` (SPEC_MODE "fmst", "topk" or "adaptive", H:1668-1743):
+    "topk" reads ``rank`` (int32 ``[Q]``) and ``spec_topk``, "adaptive"
+    ``second`` (float32 ``[Q]``) and ``spec_margin``
+    (:func:`hsd_b200.lm_head.lm_head_rank` computes both).
     """
     lib = N.load()
     if results is None:
@@ -84,10 +89,21 @@ def accept_kmp(cfg, blocks, next_ids, input_ids, gen_pool, draft_pool, seg_kv_bi
             raise ValueError("max_logit / probe_logit: contiguous float32, one per packed row")
     if variant not in ("dots", "hunyuan"):
         raise ValueError(f"variant must be 'dots' or 'hunyuan', not {variant!r}")
+    if spec_mode not in N.SPEC_MODES:
+        raise ValueError(f"spec_mode must be one of {sorted(N.SPEC_MODES)}, not {spec_mode!r}")
+    for t, dt, need in ((rank, torch.int32, spec_mode == "topk"),
+                        (second, torch.float32, spec_mode == "adaptive")):
+        if variant == "hunyuan" and need and (t is None or t.dtype != dt or not t.is_contiguous()
+                                              or t.numel() < input_ids.numel()):
+            raise ValueError(f"spec_mode {spec_mode!r}: rank (int32) / second (float32), "
+                             "contiguous, one per packed row")
     lg = N.AcceptLogits(N.ptr(max_logit), N.ptr(probe_logit), float(spec_thresh),
                         float(tree_thresh),
                         N.HSD_ACCEPT_HUNYUAN if variant == "hunyuan" else N.HSD_ACCEPT_DOTS,
-                        (C.c_int32 * 2)(*[int(t) for t in formula_tokens]))
+                        (C.c_int32 * 2)(*[int(t) for t in formula_tokens]),
+                        N.SPEC_MODES[spec_mode], int(spec_topk), float(spec_margin),
+                        N.ptr(rank) if rank is not None else None,
+                        N.ptr(second) if second is not None else None)
     N.check(lib.hsd_accept_kmp_logits(*args, C.byref(lg), N.ptr(status),
                                       N.stream_handle(stream)), "hsd_accept_kmp_logits")
     return results

@@ -38,6 +38,11 @@ struct Params {
   int32_t spec_ratio, tree_ratio;
   int32_t hunyuan;            // HSD_ACCEPT_HUNYUAN rules
   int32_t formula[2];         // HunYuan formula delimiters
+  int32_t spec_mode;          // HunYuan SPEC_MODE: HSD_SPEC_FMST / _TOPK / _ADAPTIVE
+  int32_t spec_topk;
+  float spec_margin;          // rounded to bf16
+  const int32_t* rank;
+  const float* second;
 };
 
 __device__ __forceinline__ bool is_formula(const Params& p, int tok) {
@@ -54,7 +59,12 @@ __device__ __forceinline__ float logit_ratio(float num, float den) {
 // maximal logit is positive (D:1163-1174).
 __device__ __forceinline__ bool spec_ratio_pass(const Params& p, int row) {
   const float pred = p.max_logit[row];
-  return pred > 0.f && logit_ratio(p.probe_logit[row], pred) >= p.spec_thresh;
+  if (p.spec_mode == HSD_SPEC_TOPK) return p.rank[row] < p.spec_topk;  // H:1712-1717
+  const bool ratio = pred > 0.f && logit_ratio(p.probe_logit[row], pred) >= p.spec_thresh;
+  if (p.spec_mode != HSD_SPEC_ADAPTIVE) return ratio;
+  // H:1718-1733: top1 - top2 in bf16, compared with the bf16 margin
+  const float margin = __bfloat162float(__float2bfloat16_rn(pred - p.second[row]));
+  return ratio || (margin < p.spec_margin && p.probe_logit[row] > 0.f);
 }
 
 // Tree walk fallback (D:1228-1238, D:1256-1266, H:1791-1800, H:1821-1830):
@@ -452,6 +462,18 @@ static int accept_launch(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
                         "probe_logit");
     return HSD_ERR_INVALID_ARG;
   }
+  const int spec_mode = hunyuan ? logits->spec_mode : HSD_SPEC_FMST;
+  if (spec_mode != HSD_SPEC_FMST && spec_mode != HSD_SPEC_TOPK &&
+      spec_mode != HSD_SPEC_ADAPTIVE) {
+    hsd_host::set_error("hsd_accept_kmp_logits: unknown spec_mode %d", spec_mode);
+    return HSD_ERR_INVALID_ARG;
+  }
+  if (spec_ratio && ((spec_mode == HSD_SPEC_TOPK && !logits->rank) ||
+                     (spec_mode == HSD_SPEC_ADAPTIVE && !logits->second))) {
+    hsd_host::set_error("hsd_accept_kmp_logits: spec_mode %d needs %s", spec_mode,
+                        spec_mode == HSD_SPEC_TOPK ? "rank" : "second");
+    return HSD_ERR_INVALID_ARG;
+  }
   acc::Params p;
   p.max_logit = logits ? logits->max_logit : nullptr;
   p.probe_logit = logits ? logits->probe_logit : nullptr;
@@ -463,6 +485,13 @@ static int accept_launch(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
   p.hunyuan = hunyuan;
   p.formula[0] = hunyuan ? logits->formula_tokens[0] : -1;
   p.formula[1] = hunyuan ? logits->formula_tokens[1] : -1;
+  p.spec_mode = spec_ratio ? spec_mode : HSD_SPEC_FMST;
+  p.spec_topk = spec_mode == HSD_SPEC_TOPK ? logits->spec_topk : 0;
+  p.spec_margin = spec_mode == HSD_SPEC_ADAPTIVE
+                      ? __bfloat162float(__float2bfloat16_rn(logits->spec_margin))
+                      : 0.f;
+  p.rank = spec_mode == HSD_SPEC_TOPK ? logits->rank : nullptr;
+  p.second = spec_mode == HSD_SPEC_ADAPTIVE ? logits->second : nullptr;
   p.cfg = *cfg;
   p.blocks = blocks;
   p.results = results;

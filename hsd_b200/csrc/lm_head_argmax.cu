@@ -60,6 +60,13 @@ struct Params {
   float* max_logit;
   int32_t* status;
   int q_len, vocab, k_steps, m_tiles, tiles;
+  // rank pass (hsd_lm_head_rank): per row the threshold logit, its column
+  // and the column left out of the second best; outputs
+  const float* probe;
+  const int32_t* ref_col;
+  const int32_t* excl_col;
+  int32_t* rank;
+  float* second;
 };
 
 // bf16 bit pattern -> unsigned order-preserving code (larger value, larger code).
@@ -97,6 +104,32 @@ __device__ __forceinline__ void scan32(const uint32_t (&u)[32], int c0, int ncol
   }
 }
 
+// Rank pass over 32 accumulator columns (global column gc0, tile column c0):
+// counts the columns whose bf16 logit ranks above (thr, rc) -- a larger
+// value, or the same value at a lower column -- and keeps the largest value
+// outside column ex.
+template <bool kFull>
+__device__ __forceinline__ void rank32(const uint32_t (&u)[32], int c0, int gc0, int ncols,
+                                       float thr, int rc, int ex, int& cnt, float& best2) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    uint32_t pk;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
+        : "=r"(pk)
+        : "f"(__uint_as_float(u[2 * i + 1])), "f"(__uint_as_float(u[2 * i])));
+    const float v[2] = {__uint_as_float(pk << 16), __uint_as_float(pk & 0xFFFF0000u)};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int col = gc0 + 2 * i + h;
+      if (kFull || c0 + 2 * i + h < ncols) {
+        cnt += (v[h] > thr || (v[h] == thr && col < rc)) ? 1 : 0;
+        if (col != ex && v[h] > best2) best2 = v[h];
+      }
+    }
+  }
+}
+
+template <bool kRank>
 __global__ void __launch_bounds__(kThreads, 1)
     lm_head_argmax_kernel(const __grid_constant__ CUtensorMap tm_h,
                           const __grid_constant__ CUtensorMap tm_w, const Params p) {
@@ -211,22 +244,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       tc_fence_after();
       const int ncols = min(BN, p.vocab - n * BN);
+      const int row = m * BM + trow;
       float best = -INFINITY;
       int bcol = -1;
+      // rank pass: this row's threshold, its column and the excluded column
+      float thr = INFINITY;
+      int rc = -1, ex = -1, cnt = 0;
+      if (kRank && row < p.q_len) {
+        thr = p.probe[row];
+        rc = p.ref_col[row];
+        ex = p.excl_col[row];
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t u[32];
         tmem_ld32(lane_addr + uint32_t(acc * BN + c * 32), u);
         tmem_wait_ld(u);
-        if (ncols == BN)
+        if (kRank) {
+          if (ncols == BN)
+            rank32<true>(u, c * 32, n * BN + c * 32, ncols, thr, rc, ex, cnt, best);
+          else
+            rank32<false>(u, c * 32, n * BN + c * 32, ncols, thr, rc, ex, cnt, best);
+        } else if (ncols == BN) {
           scan32<true>(u, c * 32, ncols, best, bcol);
-        else
+        } else {
           scan32<false>(u, c * 32, ncols, best, bcol);
+        }
       }
       tc_fence_before();
       mbar_arrive(&sm.acc_empty[acc]);
-      const int row = m * BM + trow;
-      if (row < p.q_len && bcol >= 0) {
+      if (kRank) {
+        // workspace: [q_len] rank counts, then [q_len] codes of the second best (+1, 0 = none)
+        uint32_t* ranks = reinterpret_cast<uint32_t*>(p.keys);
+        if (row < p.q_len) {
+          if (cnt) atomicAdd(&ranks[row], uint32_t(cnt));
+          if (best > -INFINITY)
+            atomicMax(&ranks[p.q_len + row], ordered_bf16(__float_as_uint(best) >> 16) + 1u);
+        }
+      } else if (row < p.q_len && bcol >= 0) {
         const uint32_t code = ordered_bf16(__float_as_uint(best) >> 16);
         const uint32_t col = uint32_t(n * BN + bcol);
         atomicMax(&p.keys[row], (static_cast<unsigned long long>(code) << 32) | uint32_t(~col));
@@ -251,7 +306,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     sm.last = atomicAdd(p.done, 1u) == gridDim.x - 1;
   }
   __syncthreads();
-  if (sm.last) {
+  if (sm.last && kRank) {
+    __threadfence();
+    uint32_t* ranks = reinterpret_cast<uint32_t*>(p.keys);
+    for (int r = threadIdx.x; r < p.q_len; r += blockDim.x) {
+      p.rank[r] = int32_t(atomicExch(&ranks[r], 0u));
+      const uint32_t code = atomicExch(&ranks[p.q_len + r], 0u);
+      p.second[r] = code ? from_ordered_bf16(code - 1u) : -INFINITY;
+    }
+    if (threadIdx.x == 0) *p.done = 0;
+  } else if (sm.last) {
     __threadfence();
     for (int r = threadIdx.x; r < p.q_len; r += blockDim.x) {
       const unsigned long long key = atomicExch(&p.keys[r], 0ull);
@@ -305,47 +369,44 @@ extern "C" size_t hsd_lm_head_argmax_workspace_bytes(int32_t q_len) {
   return keys_bytes(q_len) + 256;
 }
 
-extern "C" int hsd_lm_head_argmax(const void* hidden, int64_t hidden_row_stride,
-                                  const void* weight, int64_t weight_row_stride, int32_t q_len,
-                                  int32_t vocab, int32_t hidden_dim, int32_t* ids32,
-                                  int64_t* ids64, float* max_logit, void* workspace,
-                                  size_t workspace_bytes, int32_t* status,
-                                  hsd_stream_t stream) {
+namespace {
+
+bool g_rank_attr_set[kMaxDevices] = {};
+
+// Shared argument checks, tensor maps and launch of both passes.
+int lm_head_launch(bool rank, const char* name, const void* hidden, int64_t hidden_row_stride,
+                   const void* weight, int64_t weight_row_stride, int32_t q_len, int32_t vocab,
+                   int32_t hidden_dim, lmh::Params p, void* workspace, size_t workspace_bytes,
+                   hsd_stream_t stream) {
   auto aligned16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; };
   if (!hidden || !weight || q_len <= 0 || vocab <= 0 || hidden_dim <= 0 ||
       !aligned16(hidden) || !aligned16(weight) || hidden_row_stride < hidden_dim ||
-      weight_row_stride < hidden_dim || (hidden_row_stride % 8) || (weight_row_stride % 8) ||
-      (!ids32 && !ids64)) {
+      weight_row_stride < hidden_dim || (hidden_row_stride % 8) || (weight_row_stride % 8)) {
     hsd_host::set_error(
-        "hsd_lm_head_argmax: bad arguments (q_len=%d vocab=%d hidden=%d; pointers 16-byte "
-        "aligned, row strides >= hidden and multiples of 8 elements, an id output)",
-        q_len, vocab, hidden_dim);
+        "%s: bad arguments (q_len=%d vocab=%d hidden=%d; pointers 16-byte aligned, row "
+        "strides >= hidden and multiples of 8 elements)",
+        name, q_len, vocab, hidden_dim);
     return HSD_ERR_INVALID_ARG;
   }
   const size_t need = hsd_lm_head_argmax_workspace_bytes(q_len);
   if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) || workspace_bytes < need) {
-    hsd_host::set_error("hsd_lm_head_argmax: workspace %zu bytes (need %zu, 256-byte aligned)",
+    hsd_host::set_error("%s: workspace %zu bytes (need %zu, 256-byte aligned)", name,
                         workspace_bytes, need);
     return HSD_ERR_INVALID_ARG;
   }
   const int64_t m_tiles = (int64_t(q_len) + lmh::BM - 1) / lmh::BM;
   const int64_t n_tiles = (int64_t(vocab) + lmh::BN - 1) / lmh::BN;
   if (m_tiles * n_tiles > (int64_t(1) << 30)) {
-    hsd_host::set_error("hsd_lm_head_argmax: %lld tiles", (long long)(m_tiles * n_tiles));
+    hsd_host::set_error("%s: %lld tiles", name, (long long)(m_tiles * n_tiles));
     return HSD_ERR_TOO_LARGE;
   }
   CUtensorMap th, tw;
   int rc = make_map2d(&th, hidden, hidden_dim, q_len, hidden_row_stride, lmh::BM, "hidden");
   if (!rc) rc = make_map2d(&tw, weight, hidden_dim, vocab, weight_row_stride, lmh::BN, "weight");
   if (rc) return rc;
-  lmh::Params p;
   char* ws = static_cast<char*>(workspace);
   p.keys = reinterpret_cast<unsigned long long*>(ws);
   p.done = reinterpret_cast<uint32_t*>(ws + keys_bytes(q_len));
-  p.ids32 = ids32;
-  p.ids64 = ids64;
-  p.max_logit = max_logit;
-  p.status = status;
   p.q_len = q_len;
   p.vocab = vocab;
   p.k_steps = (hidden_dim + lmh::BK - 1) / lmh::BK;
@@ -360,19 +421,70 @@ extern "C" int hsd_lm_head_argmax(const void* hidden, int64_t hidden_row_stride,
         "cudaDeviceGetAttribute");
   if (rc) return rc;
   if (dev < 0 || dev >= kMaxDevices) {
-    hsd_host::set_error("hsd_lm_head_argmax: device ordinal %d >= %d", dev, kMaxDevices);
+    hsd_host::set_error("%s: device ordinal %d >= %d", name, dev, kMaxDevices);
     return HSD_ERR_UNSUPPORTED;
   }
-  if (!g_attr_set[dev]) {
+  bool& attr = rank ? g_rank_attr_set[dev] : g_attr_set[dev];
+  if (!attr) {
     rc = hsd_host::cuda_check(
-        cudaFuncSetAttribute(lmh::lm_head_argmax_kernel,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+        rank ? cudaFuncSetAttribute(lmh::lm_head_argmax_kernel<true>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem))
+             : cudaFuncSetAttribute(lmh::lm_head_argmax_kernel<false>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
         "cudaFuncSetAttribute(lm_head_argmax_kernel)");
     if (rc) return rc;
-    g_attr_set[dev] = true;
+    attr = true;
   }
   const int grid = int(std::min<int64_t>(p.tiles, sms));
-  lmh::lm_head_argmax_kernel<<<grid, lmh::kThreads, smem,
-                               reinterpret_cast<cudaStream_t>(stream)>>>(th, tw, p);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (rank)
+    lmh::lm_head_argmax_kernel<true><<<grid, lmh::kThreads, smem, st>>>(th, tw, p);
+  else
+    lmh::lm_head_argmax_kernel<false><<<grid, lmh::kThreads, smem, st>>>(th, tw, p);
   return hsd_host::cuda_check(cudaGetLastError(), "lm_head_argmax_kernel launch");
+}
+
+}  // namespace
+
+extern "C" int hsd_lm_head_argmax(const void* hidden, int64_t hidden_row_stride,
+                                  const void* weight, int64_t weight_row_stride, int32_t q_len,
+                                  int32_t vocab, int32_t hidden_dim, int32_t* ids32,
+                                  int64_t* ids64, float* max_logit, void* workspace,
+                                  size_t workspace_bytes, int32_t* status,
+                                  hsd_stream_t stream) {
+  if (!ids32 && !ids64) {
+    hsd_host::set_error("hsd_lm_head_argmax: bad arguments (no id output)");
+    return HSD_ERR_INVALID_ARG;
+  }
+  lmh::Params p = {};
+  p.ids32 = ids32;
+  p.ids64 = ids64;
+  p.max_logit = max_logit;
+  p.status = status;
+  return lm_head_launch(false, "hsd_lm_head_argmax", hidden, hidden_row_stride, weight,
+                        weight_row_stride, q_len, vocab, hidden_dim, p, workspace,
+                        workspace_bytes, stream);
+}
+
+extern "C" int hsd_lm_head_rank(const void* hidden, int64_t hidden_row_stride,
+                                const void* weight, int64_t weight_row_stride, int32_t q_len,
+                                int32_t vocab, int32_t hidden_dim, const float* probe_logit,
+                                const int32_t* ref_col, const int32_t* excl_col, int32_t* rank,
+                                float* second, void* workspace, size_t workspace_bytes,
+                                int32_t* status, hsd_stream_t stream) {
+  if (!probe_logit || !ref_col || !excl_col || !rank || !second) {
+    hsd_host::set_error("hsd_lm_head_rank: bad arguments (probe_logit, ref_col, excl_col, "
+                        "rank and second are all required)");
+    return HSD_ERR_INVALID_ARG;
+  }
+  lmh::Params p = {};
+  p.status = status;
+  p.probe = probe_logit;
+  p.ref_col = ref_col;
+  p.excl_col = excl_col;
+  p.rank = rank;
+  p.second = second;
+  return lm_head_launch(true, "hsd_lm_head_rank", hidden, hidden_row_stride, weight,
+                        weight_row_stride, q_len, vocab, hidden_dim, p, workspace,
+                        workspace_bytes, stream);
 }

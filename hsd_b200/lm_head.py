@@ -105,3 +105,45 @@ def probe_logits(hidden, weight, rows, toks, *, out=None, status=None):
         N.ptr(rows), N.ptr(toks), n, N.ptr(out), N.ptr(status), N.stream_handle()),
         "hsd_probe_logits")
     return out
+
+
+def lm_head_rank(hidden, weight, probe_logit, ref_col, excl_col, *, status=None):
+    """Rank of a token among a row's bf16 logits and the row's second best,
+    without the logits (``hsd_lm_head_rank``), for HunYuan's SPEC_MODE=topk /
+    adaptive acceptance (H:1712-1736).
+
+    For every row r of ``hidden`` (``[R, H]`` bf16, e.g. the last block's
+    final states): ``rank[r]`` = the number of columns whose logit exceeds
+    ``probe_logit[r]`` (= ``logits[r, ref_col[r]]``, :func:`probe_logits`)
+    plus the columns below ``ref_col[r]`` with an equal logit, so
+    ``rank[r] < k`` means ``ref_col[r]`` is among ``topk(k).indices``;
+    ``second[r]`` = the largest logit outside column ``excl_col[r]`` (the
+    row's argmax), ``topk(2).values[1]``.  ``probe_logit`` float32,
+    ``ref_col`` / ``excl_col`` int32, one per row.  Returns ``(rank int32,
+    second float32)``.
+    """
+    if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("lm_head_rank: hidden and weight must be bf16")
+    if not hidden.is_cuda or hidden.device != weight.device:
+        raise ValueError("lm_head_rank: hidden and weight must be on the same CUDA device")
+    hd = hidden.shape[-1]
+    if weight.dim() != 2 or weight.shape[1] != hd:
+        raise ValueError(f"lm_head_rank: weight {tuple(weight.shape)} vs hidden dim {hd}")
+    h2 = hidden.reshape(-1, hd)
+    if h2.stride(-1) != 1:
+        h2 = h2.contiguous()
+    w = weight if weight.stride(-1) == 1 else weight.contiguous()
+    q = h2.shape[0]
+    for t, dt in ((probe_logit, torch.float32), (ref_col, torch.int32), (excl_col, torch.int32)):
+        if t.dtype != dt or t.numel() != q or not t.is_contiguous():
+            raise ValueError(f"lm_head_rank: inputs must be contiguous {dt} with {q} rows")
+    rank = torch.zeros(q, dtype=torch.int32, device=hidden.device)
+    second = torch.full((q,), float("-inf"), dtype=torch.float32, device=hidden.device)
+    if q == 0:
+        return rank, second
+    base, nbytes = _workspace(q, hidden.device)
+    N.check(N.load().hsd_lm_head_rank(
+        N.ptr(h2), h2.stride(0), N.ptr(w), w.stride(0), q, w.shape[0], hd, N.ptr(probe_logit),
+        N.ptr(ref_col), N.ptr(excl_col), N.ptr(rank), N.ptr(second), C.c_void_p(base), nbytes,
+        N.ptr(status), N.stream_handle()), "hsd_lm_head_rank")
+    return rank, second

@@ -70,7 +70,8 @@ class VerifyLoop:
                  max_tree_depth=15, max_tree_len=256,
                  repeat_sentinel=DOTS_SENTINEL, kv_planes=None, row_bytes=0,
                  kv_capacity=None, spec_thresh=1.0, tree_thresh=1.0, variant="dots",
-                 formula_tokens=(3, 1099), device="cuda"):
+                 formula_tokens=(3, 1099), spec_mode="fmst", spec_topk=3, spec_margin=2.0,
+                 device="cuda"):
         if len(prompts) != len(drafts) or not prompts:
             raise ValueError("one draft per prompt, at least one block")
         self.device = torch.device(device)
@@ -95,6 +96,11 @@ class VerifyLoop:
         if variant not in ("dots", "hunyuan"):
             raise ValueError(f"variant must be 'dots' or 'hunyuan', not {variant!r}")
         self.variant, self.formula_tokens = variant, tuple(int(t) for t in formula_tokens)
+        if spec_mode not in N.SPEC_MODES or (spec_mode != "fmst" and variant != "hunyuan"):
+            raise ValueError("spec_mode 'topk' / 'adaptive' belong to the HunYuan rules; "
+                             f"got {spec_mode!r} with variant {variant!r}")
+        self.spec_mode, self.spec_topk = spec_mode, int(spec_topk)
+        self.spec_margin = float(spec_margin)
         # HunYuan's tree fallback runs at any threshold in text mode (H:1791)
         self.ratio = (self.spec_thresh < 1.0 or self.tree_thresh < 1.0
                       or (variant == "hunyuan" and self.tree_decode))
@@ -208,7 +214,8 @@ class VerifyLoop:
                 toks[qs + 1:qs + n] = self.input_ids[qs + 1:qs + n]
         return (torch.from_numpy(rows).to(self.device), torch.from_numpy(toks).to(self.device))
 
-    def step(self, next_ids, max_logit=None, probe_logit=None, text_mode=None):
+    def step(self, next_ids, max_logit=None, probe_logit=None, text_mode=None, rank=None,
+             second=None):
         """Consume the target argmax of every packed row; prepare the next step.
 
         With thresholds below 1, ``max_logit`` (float32 ``[Q]``, the maximal
@@ -218,12 +225,22 @@ class VerifyLoop:
         ``text_mode[b]`` (the page parser's ``text_mode``, D:1229; default
         False) enables the tree fallback for block b.  Returns False once
         generation is finished (every block finished or ``max_new_tokens``
-        generated, D:1589-1591).
+        generated, D:1589-1591).  HunYuan's ``spec_mode="topk"`` reads
+        ``rank`` (int32 ``[Q]``: row r's draft token ``input_ids[r + 1]``
+        ranked among the row's logits) and ``"adaptive"`` ``second`` (float32
+        ``[Q]``: the row's second best logit);
+        :func:`hsd_b200.lm_head.lm_head_rank` computes both for the last
+        block's rows, the only rows these modes read.
         """
         if self.done:
             raise RuntimeError("the loop has finished")
         if self.ratio and (max_logit is None or probe_logit is None):
             raise ValueError("thresholds below 1 need max_logit and probe_logit")
+        if self.ratio and self.spec_thresh < 1.0 and (
+                (self.spec_mode == "topk" and rank is None)
+                or (self.spec_mode == "adaptive" and second is None)):
+            raise ValueError(f"spec_mode {self.spec_mode!r} needs "
+                             f"{'rank' if self.spec_mode == 'topk' else 'second'}")
         dev = self.device
         self.decode_times += 1
         q = int(self.input_ids.size)
@@ -263,7 +280,10 @@ class VerifyLoop:
                    status=self.status,
                    logits=(max_logit, probe_logit, self.spec_thresh, self.tree_thresh)
                    if self.ratio else None, variant=self.variant,
-                   formula_tokens=self.formula_tokens)
+                   formula_tokens=self.formula_tokens, spec_mode=self.spec_mode,
+                   spec_topk=self.spec_topk, spec_margin=self.spec_margin,
+                   rank=None if rank is None else rank.to(torch.int32).contiguous(),
+                   second=None if second is None else second.to(torch.float32).contiguous())
         res = self.results.cpu().numpy()
         self._check()
 

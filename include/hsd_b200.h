@@ -161,10 +161,26 @@ typedef struct {
    * blocks at any tree_thresh (H:1791-1800, no `< 1` guard) */
   int32_t variant;
   int32_t formula_tokens[2]; /* HunYuan formula delimiters: 3 ('$'), 1099 ('$$') */
+  /* HunYuan SPEC_MODE (H:1668-1743) for the last block's missed rows, where
+   * the ratio rule applies (spec_thresh < 1, outside formulas):
+   * HSD_SPEC_FMST (0, default) the ratio; HSD_SPEC_TOPK the draft token is
+   * among the row's spec_topk best logits (rank[r] < spec_topk, ranks from
+   * hsd_lm_head_rank); HSD_SPEC_ADAPTIVE the ratio, or
+   * bf16(max_logit - second) < bf16(spec_margin) with probe_logit > 0
+   * (second[r]: the row's second best logit, hsd_lm_head_rank).  Ignored for
+   * HSD_ACCEPT_DOTS. */
+  int32_t spec_mode;
+  int32_t spec_topk;   /* SPEC_TOPK, default 3 */
+  float spec_margin;   /* SPEC_MARGIN, default 2.0 */
+  const int32_t *rank; /* [q_len], HSD_SPEC_TOPK */
+  const float *second; /* [q_len], HSD_SPEC_ADAPTIVE */
 } hsd_accept_logits_t;
 
 #define HSD_ACCEPT_DOTS 0
 #define HSD_ACCEPT_HUNYUAN 1
+#define HSD_SPEC_FMST 0
+#define HSD_SPEC_TOPK 1
+#define HSD_SPEC_ADAPTIVE 2
 
 /* ---- library ---------------------------------------------------------- */
 const char *hsd_version(void);
@@ -380,6 +396,27 @@ int hsd_lm_head_argmax(const void *hidden, int64_t hidden_row_stride, const void
                        int32_t hidden_dim, int32_t *ids32, int64_t *ids64, float *max_logit,
                        void *workspace, size_t workspace_bytes, int32_t *status,
                        hsd_stream_t stream);
+
+/* Second pass of the fused lm_head for HunYuan's SPEC_MODE=topk / adaptive
+ * acceptance (H:1712-1736, which call logits.topk on the materialised bf16
+ * logits): over the rows given (typically the last block's), with the
+ * logits of each row rounded to bf16 as in hsd_lm_head_argmax and never
+ * written,
+ *   rank[r]   = #columns whose logit exceeds probe_logit[r], plus
+ *               #columns below ref_col[r] whose logit equals it: the 0-based
+ *               position of the draft token ref_col[r] in a descending order
+ *               that puts lower columns first among equal logits (torch
+ *               leaves that order unspecified); rank[r] < k <=> the token is
+ *               among topk(k).indices;
+ *   second[r] = the largest logit outside column excl_col[r] (the row's
+ *               argmax), i.e. topk(2).values[1].
+ * probe_logit[r] = logits[r, ref_col[r]] (hsd_probe_logits).  Same
+ * workspace contract as hsd_lm_head_argmax (the two may share one). */
+int hsd_lm_head_rank(const void *hidden, int64_t hidden_row_stride, const void *weight,
+                     int64_t weight_row_stride, int32_t q_len, int32_t vocab, int32_t hidden_dim,
+                     const float *probe_logit, const int32_t *ref_col, const int32_t *excl_col,
+                     int32_t *rank, float *second, void *workspace, size_t workspace_bytes,
+                     int32_t *status, hsd_stream_t stream);
 
 /* Single logits of the logit-ratio acceptance: out[k] = logits[rows[k],
  * toks[k]] = hidden[rows[k]] . weight[toks[k]] (bf16 in, fp32 accumulation,

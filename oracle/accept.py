@@ -65,6 +65,9 @@ class StepConfig:
     tree_thresh: float = 1.0       # HSD_TREE_THRESH (D:970); fixed 1 in HunYuan (H:1470)
     variant: str = "dots"          # "dots" (D) or "hunyuan" (H)
     formula_tokens: tuple = (3, 1099)   # HunYuan '$' and '$$' (H:1685)
+    spec_mode: str = "fmst"        # HunYuan SPEC_MODE (H:1668): "fmst", "topk", "adaptive"
+    spec_topk: int = 3             # SPEC_TOPK (H:1714)
+    spec_margin: float = 2.0       # SPEC_MARGIN (H:1720)
 
 
 def bf16_f32(x):
@@ -89,6 +92,42 @@ def ratio_passes(num, den, thresh):
     """``(num / den) >= thresh`` on bf16 tensors: torch compares in bf16,
     so the Python float threshold is rounded to bf16 first (0.9 -> 0.8984375)."""
     return bool(logit_ratio(num, den) >= bf16_f32(thresh))
+
+
+def rank_and_second(row, ref_col, excl_col):
+    """``(rank, second)`` of one row of bf16 logits (float32 array of bf16
+    values) for HunYuan's ``topk`` / ``adaptive`` modes (H:1712-1736).
+
+    ``rank``: the draft token ``ref_col``'s 0-based position when the row is
+    sorted by descending logit, lower columns first among equal logits, so
+    ``rank < k`` stands for ``ref in logits.topk(k).indices`` (torch leaves
+    the order among equal values unspecified); ``second``: the largest logit
+    outside column ``excl_col`` (the row's argmax), i.e. ``topk(2).values[1]``.
+    """
+    v = np.asarray(row, dtype=np.float32)
+    thr = v[ref_col]
+    rank = int(np.count_nonzero(v > thr) + np.count_nonzero(v[:ref_col] == thr))
+    second = np.float32(np.max(np.delete(v, excl_col))) if v.size > 1 else np.float32(-np.inf)
+    return rank, second
+
+
+def spec_mode_passes(cfg, pred, probe, thresh, rank=None, second=None):
+    """A missed speculative row of HunYuan's last block passes (H:1710-1743):
+    ``fmst``: the logit ratio; ``topk``: the draft token among the row's
+    ``spec_topk`` best (``rank < k``); ``adaptive``: the ratio, or a bf16
+    top-1 / top-2 margin below ``spec_margin`` with a positive draft logit
+    (bf16 subtraction and a bf16 comparison, as torch does on the logits)."""
+    pred = np.float32(pred)
+    ratio = bool(pred > 0) and ratio_passes(probe, pred, thresh)
+    if cfg.spec_mode == "fmst":
+        return ratio
+    if cfg.spec_mode == "topk":
+        return int(rank) < int(cfg.spec_topk)
+    if cfg.spec_mode == "adaptive":
+        margin = bf16_f32(np.float32(pred) - np.float32(second))
+        return ratio or (bool(margin < bf16_f32(np.float32(cfg.spec_margin)))
+                         and bool(np.float32(probe) > 0))
+    raise ValueError(f"spec_mode {cfg.spec_mode!r}")
 
 
 def tree_ratio_fallback(node, tokens, parents, max_logit, probe_logit):
@@ -153,7 +192,8 @@ def accept_block(st, bs, be, next_list, input_list, cfg, filt, kv_base,
         hunyuan = cfg.variant == "hunyuan"
         thresh = cfg.spec_thresh if (not hunyuan or is_last_block) else 1.0   # H:1671
         if thresh < 1.0:                                       # D:1147-1174, H:1676-1744
-            max_l, probe_l = logits
+            max_l, probe_l = logits[0], logits[1]
+            rank_l, second_l = (logits[2], logits[3]) if len(logits) > 2 else (None, None)
             can = [True] * len(acc)
             if hunyuan:                                        # H:1681-1695
                 in_formula = False
@@ -169,7 +209,12 @@ def accept_block(st, bs, be, next_list, input_list, cfg, filt, kv_base,
             first_miss = next((i for i, ok in enumerate(acc) if not ok), len(acc))
             for i in range(first_miss, len(acc)):
                 pred = np.float32(max_l[bs + i])
-                if can[i]:
+                if can[i] and hunyuan:
+                    acc[i] = acc[i] or spec_mode_passes(
+                        cfg, pred, probe_l[bs + i], thresh,
+                        None if rank_l is None else rank_l[bs + i],
+                        None if second_l is None else second_l[bs + i])
+                elif can[i]:
                     acc[i] = acc[i] or (bool(pred > 0) and
                                         ratio_passes(probe_l[bs + i], pred, thresh))
         diff = len(acc)
@@ -200,7 +245,7 @@ def accept_block(st, bs, be, next_list, input_list, cfg, filt, kv_base,
                 return decode
             if any(parents[c] == node and tokens[c] == decode for c in range(node + 1, n_nodes)):
                 return decode
-            max_l, probe_l = logits
+            max_l, probe_l = logits[0], logits[1]
             got = tree_ratio_fallback(node, tokens, parents, max_l[bs + node], probe_l[bs:])
             if got is None:
                 return decode

@@ -31,7 +31,7 @@ import numpy as np
 import torch
 
 from .accept import (FINISHED, SPEC, TREE, BlockState, accept_block, next_block_input,
-                     realign_block)
+                     rank_and_second, realign_block)
 from .compact import apply_to_mask, compaction_action, keep_columns, pad_filter
 from .masks import (assemble_next_mask, initial_packed_mask, normal_block_mask,
                     spec_block_mask, tree_block_mask)
@@ -92,6 +92,15 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
                 spans.append((b0, pointer[b] + 1))
                 b0 = pointer[b] + 1
             logits = ratio_logits(dense, next_ids, input_ids, spans, states)
+            if cfg.variant == "hunyuan" and cfg.spec_mode != "fmst":
+                # topk / adaptive: the draft token's rank and the second best
+                # logit of every speculative row (H:1712-1736)
+                rank = np.zeros(q, dtype=np.int32)
+                second = np.full(q, -np.inf, dtype=np.float32)
+                for r in range(q - 1):
+                    rank[r], second[r] = rank_and_second(dense[r], int(input_ids[r + 1]),
+                                                         int(next_ids[r]))
+                logits = logits + (rank, second)
         else:
             next_ids = np.asarray(model(input_ids, position_ids, allowed, kv_tokens),
                                   dtype=np.int64)

@@ -136,9 +136,11 @@ def make_logits(sc, seed, thresh):
 
 
 def run_oracle(sc, page_block=None, logits=None, spec_thresh=1.0, tree_thresh=1.0,
-               text_mode=(), variant="dots", formula_tokens=(3, 1099)):
+               text_mode=(), variant="dots", formula_tokens=(3, 1099), spec_mode="fmst",
+               spec_topk=3, spec_margin=2.0):
     cfg = OA.StepConfig(pad_token_id=PAD, eos_token_ids=sc["eos"], spec_thresh=spec_thresh,
-                        tree_thresh=tree_thresh, variant=variant, formula_tokens=formula_tokens)
+                        tree_thresh=tree_thresh, variant=variant, formula_tokens=formula_tokens,
+                        spec_mode=spec_mode, spec_topk=spec_topk, spec_margin=spec_margin)
     allowed = OM.segments_to_allowed(sc["q_len"], sc["kv_len"], sc["segs"])
     filt = np.zeros(sc["kv_len"], bool)
     kv_base = sc["kv_len"] - sc["q_len"]

@@ -119,6 +119,21 @@ def test_lm_head_argmax_host_checks():
     assert b"workspace" in lib.hsd_last_error()
 
 
+def test_lm_head_rank_host_checks():
+    lib = N.load()
+    a = C.c_void_p(256)
+    # a missing per-row input / an unaligned hidden pointer / too small a workspace
+    assert lib.hsd_lm_head_rank(a, 1536, a, 1536, 4, 100, 1536, None, a, a, a, a, a, 4096,
+                                None, None) != 0
+    assert b"bad arguments" in lib.hsd_last_error()
+    assert lib.hsd_lm_head_rank(C.c_void_p(8), 1536, a, 1536, 4, 100, 1536, a, a, a, a, a, a,
+                                4096, None, None) != 0
+    assert b"bad arguments" in lib.hsd_last_error()
+    assert lib.hsd_lm_head_rank(a, 1536, a, 1536, 4, 100, 1536, a, a, a, a, a, a, 64, None,
+                                None) != 0
+    assert b"workspace" in lib.hsd_last_error()
+
+
 def test_rope_append_host_checks():
     lib = N.load()
     a = C.c_void_p(256)

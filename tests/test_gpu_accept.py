@@ -23,7 +23,7 @@ def dev():
 
 
 def run_kernel(sc, dev, page_block=None, logits=None, text_mode=(), variant="dots",
-               formula_tokens=(3, 1099)):
+               formula_tokens=(3, 1099), spec=None):
     from hsd_b200 import accept as A
     from hsd_b200.plan import pack_bits
     nb = len(sc["blocks"])
@@ -75,7 +75,10 @@ def run_kernel(sc, dev, page_block=None, logits=None, text_mode=(), variant="dot
                        logits=None if logits is None else (
                            torch.from_numpy(logits[0]).to(dev), torch.from_numpy(logits[1]).to(dev),
                            logits[2], logits[3]),
-                       variant=variant, formula_tokens=formula_tokens)
+                       variant=variant, formula_tokens=formula_tokens,
+                       **({} if spec is None else dict(
+                           spec, rank=t(spec["rank"]),
+                           second=torch.from_numpy(spec["second"]).to(dev))))
     torch.cuda.synchronize()
     assert status.item() == 0, hex(status.item())
     return (res.cpu().numpy(), d_blocks.cpu().numpy(), d_gen.cpu().numpy(),
@@ -156,4 +159,33 @@ def test_accept_hunyuan_rules_match_oracle(dev, seed, spec_thresh):
                                  formula_tokens=formula)
     out = run_kernel(sc, dev, text_mode=text_mode, logits=(max_l, probe, spec_thresh, 1.0),
                      variant="hunyuan", formula_tokens=formula)
+    compare(sc, seed, expect, filt, out)
+
+
+@pytest.mark.parametrize("seed", list(range(16)))
+@pytest.mark.parametrize("mode,k,margin", [("topk", 3, 2.0), ("topk", 1, 2.0),
+                                           ("adaptive", 3, 2.0), ("adaptive", 3, 0.7)])
+def test_accept_hunyuan_spec_modes_match_oracle(dev, seed, mode, k, margin):
+    """HunYuan SPEC_MODE=topk / adaptive (H:1712-1736) bit-exact vs the
+    oracle on the same per-row ranks and second-best logits: the last
+    block's missed rows outside formulas pass when the draft token ranks
+    below k, or (adaptive) by the ratio or a bf16 top-1 / top-2 margin below
+    the bf16 threshold with a positive draft logit (some margins placed
+    exactly at it)."""
+    sc = AC.make_scenario(seed, tight=bool(seed % 2), last_mode=OA.SPEC)
+    formula = (3, 5) if seed % 4 else (3, 1099)
+    max_l, probe = AC.make_logits(sc, seed, 0.5)
+    rng = np.random.default_rng(seed + 77)
+    q = sc["q_len"]
+    rank = rng.integers(0, 6, q).astype(np.int32)
+    second = OA.bf16_f32((max_l - rng.uniform(0.0, 3.0, q)).astype(np.float32))
+    at = rng.random(q) < 0.2
+    second[at] = OA.bf16_f32((max_l[at] - OA.bf16_f32(np.float32(margin))).astype(np.float32))
+    expect, filt = AC.run_oracle(sc, logits=(max_l, probe, rank, second), spec_thresh=0.5,
+                                 tree_thresh=1.0, variant="hunyuan", formula_tokens=formula,
+                                 spec_mode=mode, spec_topk=k, spec_margin=margin)
+    out = run_kernel(sc, dev, logits=(max_l, probe, 0.5, 1.0), variant="hunyuan",
+                     formula_tokens=formula,
+                     spec=dict(spec_mode=mode, spec_topk=k, spec_margin=margin, rank=rank,
+                               second=second))
     compare(sc, seed, expect, filt, out)

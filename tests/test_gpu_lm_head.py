@@ -205,3 +205,42 @@ def test_probe_logits_bad_index_sets_status(dev):
     assert int(status.item()) & 0x20000
     o = out.cpu().numpy()
     assert np.isfinite(o[0]) and np.isnan(o[1]) and np.isnan(o[2])
+
+
+@pytest.mark.parametrize("q,vocab,hd,seed", [(200, 3000, 512, 0), (64, 1000, 256, 1),
+                                             (300, 151936 // 16, 1536, 2)])
+def test_lm_head_rank_matches_torch(dev, q, vocab, hd, seed):
+    """The rank pass against torch's bf16 logits: multiples of 1/4 in hidden
+    and weight make every fp32 sum exact, so both sides round the same
+    values to bf16 (with many equal logits).  rank = the draft token's
+    position in the descending order with lower columns first among equal
+    logits; second = the best logit outside the argmax column; rank < k
+    agrees with topk(k) wherever the k-th and (k+1)-th logits differ."""
+    from hsd_b200.lm_head import lm_head_argmax, lm_head_rank
+    from oracle import accept as OA
+    g = torch.Generator().manual_seed(seed)
+    h = (torch.randint(-4, 5, (q, hd), generator=g).float() / 4).to(torch.bfloat16)
+    w = (torch.randint(-4, 5, (vocab, hd), generator=g).float() / 4).to(torch.bfloat16)
+    logits = (h.float() @ w.float().T).to(torch.bfloat16)        # exact sums, one rounding
+    dense = logits.float().numpy()
+    ids = lm_head_argmax(h.to(dev), w.to(dev)).cpu()
+    np.testing.assert_array_equal(ids.numpy(), dense.argmax(1))
+    rng = np.random.default_rng(seed)
+    ref = np.where(rng.random(q) < 0.5, np.argsort(-dense, 1, kind="stable")[
+        np.arange(q), rng.integers(0, 8, q)], rng.integers(0, vocab, q)).astype(np.int32)
+    probe = dense[np.arange(q), ref].astype(np.float32)
+    rank, second = lm_head_rank(h.to(dev), w.to(dev), torch.from_numpy(probe).to(dev),
+                                torch.from_numpy(ref).to(dev),
+                                ids.to(torch.int32).to(dev))
+    want = [OA.rank_and_second(dense[r], int(ref[r]), int(ids[r])) for r in range(q)]
+    np.testing.assert_array_equal(rank.cpu().numpy(), [x[0] for x in want])
+    np.testing.assert_array_equal(second.cpu().numpy(), np.float32([x[1] for x in want]))
+    for k in (1, 3, 5):
+        top = logits.topk(k + 1, dim=-1).values.float().numpy()
+        clear = top[:, k - 1] != top[:, k]          # no tie at the boundary
+        in_topk = (logits.topk(k, dim=-1).indices.numpy() == ref[:, None]).any(1)
+        np.testing.assert_array_equal((rank.cpu().numpy() < k)[clear], in_topk[clear])
+    # a second call reuses the cleared workspace
+    rank2, second2 = lm_head_rank(h.to(dev), w.to(dev), torch.from_numpy(probe).to(dev),
+                                  torch.from_numpy(ref).to(dev), ids.to(torch.int32).to(dev))
+    assert torch.equal(rank2, rank) and torch.equal(second2, second)

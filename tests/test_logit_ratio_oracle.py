@@ -180,3 +180,59 @@ def test_hunyuan_formula_rows_need_exact_match():
     assert inc == 6
     st, (_, _, inc, _) = _hy_spec([4, 3], ids, [6, 1099, 22, 23, 24, 25], *ratio_ok)
     assert inc == 3                                 # row 2 (a delimiter) misses
+
+
+@pytest.mark.parametrize("mode,k,margin,thresh", [
+    ("topk", 3, 2.0, 0.5), ("topk", 1, 2.0, 0.5), ("topk", 8, 2.0, 0.9),
+    ("adaptive", 3, 2.0, 0.5), ("adaptive", 3, 0.7, 0.95), ("adaptive", 3, 1.704, 0.8)])
+def test_hunyuan_spec_modes_match_torch(mode, k, margin, thresh):
+    """HunYuan's SPEC_MODE=topk / adaptive (H:1712-1736) as the reference
+    writes them on bf16 logits rows, against the oracle's rank / second-best
+    restatement.  Rows have no ties at the top-k boundary (torch leaves the
+    order among equal values unspecified); the margin rows include exact
+    bf16 boundary cases."""
+    rng = np.random.default_rng(k * 100 + int(margin * 10))
+    rows, vocab = 96, 256
+    cfg = OA.StepConfig(variant="hunyuan", spec_mode=mode, spec_topk=k, spec_margin=margin)
+    x = rng.normal(0.0, 3.0, (rows, vocab)).astype(np.float32)
+    logits = torch.from_numpy(x).to(torch.bfloat16)
+    # distinct values per row: a permutation of a bf16-exact ladder (steps
+    # of 1/16 in [-8, 8) need at most 8 significant bits)
+    ladder = (torch.arange(vocab, dtype=torch.float32) / 16.0 - 8.0).to(torch.bfloat16)
+    for r in range(rows):
+        logits[r] = ladder[torch.from_numpy(rng.permutation(vocab))]
+        if r % 2:  # lift the maximum a random margin above the runner-up
+            top = int(logits[r].float().argmax())
+            lifted = torch.tensor(7.9375 + rng.uniform(0.0, 3.0)).to(torch.bfloat16)
+            logits[r, top] = lifted
+    dense = logits.float().numpy()
+    pred_tok = logits.float().argmax(-1)             # first maximum, as the fused argmax keeps
+    ref_tok = torch.from_numpy(np.where(rng.random(rows) < 0.5,
+                                        dense.argsort(1)[:, -1 - rng.integers(0, 6, rows)]
+                                        [np.arange(rows), np.arange(rows)],
+                                        rng.integers(0, vocab, rows)))
+    rr = torch.arange(rows)
+    ref_l, pred_l = logits[rr, ref_tok], logits[rr, pred_tok]
+    if mode == "topk":
+        want = (logits.topk(k, dim=-1).indices == ref_tok[:, None]).any(-1).numpy()
+    else:
+        top2 = logits.topk(2, dim=-1).values
+        mg = top2[:, 0] - top2[:, 1]
+        want = ((((ref_l / pred_l) >= thresh) & (pred_l > 0))
+                | ((mg < margin) & (ref_l > 0))).numpy()
+    got = []
+    for r in range(rows):
+        rank, second = OA.rank_and_second(dense[r], int(ref_tok[r]), int(pred_tok[r]))
+        got.append(OA.spec_mode_passes(cfg, dense[r, pred_tok[r]], dense[r, ref_tok[r]], thresh,
+                                       rank, second))
+    np.testing.assert_array_equal(np.array(got), want)
+
+
+def test_rank_and_second_ties():
+    """Equal logits: lower columns rank first; the second best may equal the
+    best when the maximum repeats."""
+    row = np.array([1.0, 3.0, 2.0, 3.0, 2.0], dtype=np.float32)
+    assert OA.rank_and_second(row, 1, 1) == (0, np.float32(3.0))
+    assert OA.rank_and_second(row, 3, 1) == (1, np.float32(3.0))
+    assert OA.rank_and_second(row, 4, 1)[0] == 3
+    assert OA.rank_and_second(row, 0, 1) == (4, np.float32(3.0))

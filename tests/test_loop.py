@@ -217,11 +217,35 @@ def test_oracle_hunyuan_loop_departs_from_dots(seed, tree, spec_t, tree_t, text,
     assert hy != dots or [s["action"] for s in hy_trace] != [s["action"] for s in dots_trace]
 
 
+SPEC_MODE_CASE = (1, False, 0.5, 1.0, {5}, 1)
+
+
+@pytest.mark.parametrize("mode,k,margin", [("topk", 3, 2.0), ("adaptive", 3, 50.0)])
+def test_oracle_hunyuan_spec_modes_depart_from_fmst(mode, k, margin):
+    """SPEC_MODE=topk / adaptive (H:1712-1736) accept differently from the
+    default logit ratio on the same logits model (whose top-2 margins are
+    all above 2, so the adaptive case widens the margin)."""
+    seed, tree, spec_t, tree_t, text, period = SPEC_MODE_CASE
+    prompts, truths, drafts = LC.make_loop_case(seed)
+    model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
+    lm = LC.logits_model(model, seed)
+    cfg = _ratio_cfg(tree, spec_t, tree_t, "hunyuan")
+    fmst, fmst_trace = OL.reference_loop(prompts, drafts, model, cfg, 400, compact_period=period,
+                                         logits_model=lm, text_mode=text)
+    cfg.spec_mode, cfg.spec_topk, cfg.spec_margin = mode, k, margin
+    got, trace = OL.reference_loop(prompts, drafts, model, cfg, 400, compact_period=period,
+                                   logits_model=lm, text_mode=text)
+    assert got != fmst or len(trace) != len(fmst_trace)
+
+
 @pytest.mark.gpu
-@pytest.mark.parametrize("seed,tree,spec_t,tree_t,text,variant,period",
-                         [c + ("dots", 1) for c in RATIO_CASES] +
-                         [c[:5] + ("hunyuan", c[5]) for c in HUNYUAN_CASES])
-def test_device_ratio_loop_follows_oracle_loop(seed, tree, spec_t, tree_t, text, variant, period):
+@pytest.mark.parametrize("seed,tree,spec_t,tree_t,text,variant,period,spec_mode",
+                         [c + ("dots", 1, "fmst") for c in RATIO_CASES] +
+                         [c[:5] + ("hunyuan", c[5], "fmst") for c in HUNYUAN_CASES] +
+                         [SPEC_MODE_CASE[:5] + ("hunyuan", SPEC_MODE_CASE[5], m)
+                          for m in ("topk", "adaptive")])
+def test_device_ratio_loop_follows_oracle_loop(seed, tree, spec_t, tree_t, text, variant, period,
+                                               spec_mode):
     """The device loop below the default thresholds (and with the HunYuan
     rules): per step the same inputs as the oracle loop, the logits it reads
     listed by ``logit_probes``, and the same generated tokens."""
@@ -230,13 +254,16 @@ def test_device_ratio_loop_follows_oracle_loop(seed, tree, spec_t, tree_t, text,
     prompts, truths, drafts = LC.make_loop_case(seed)
     model = OL.true_text_model(prompts, truths, LC.VOCAB, LC.EOS)
     lm = LC.logits_model(model, seed)
-    ref_gen, trace = OL.reference_loop(prompts, drafts, model,
-                                       _ratio_cfg(tree, spec_t, tree_t, variant), 400,
+    cfg = _ratio_cfg(tree, spec_t, tree_t, variant)
+    cfg.spec_mode = spec_mode
+    cfg.spec_margin = 50.0   # adaptive: the margin rule fires wherever the draft logit is > 0
+    ref_gen, trace = OL.reference_loop(prompts, drafts, model, cfg, 400,
                                        compact_period=period, logits_model=lm, text_mode=text)
     loop = VerifyLoop(prompts, drafts, eos_token_id=LC.EOS, max_new_tokens=400,
                       pad_token_id=LC.PAD, min_input_length=MIL, enable_tree_decode=tree,
                       spec_thresh=spec_t, tree_thresh=tree_t, variant=variant,
-                      formula_tokens=(3, 5), compact_period=period, device=dev)
+                      formula_tokens=(3, 5), compact_period=period, spec_mode=spec_mode,
+                      spec_margin=cfg.spec_margin, device=dev)
     flags = [b in text for b in range(len(prompts))]
     for it, ref in enumerate(trace):
         ids, pos, mask = loop.inputs()
@@ -248,7 +275,14 @@ def test_device_ratio_loop_follows_oracle_loop(seed, tree, spec_t, tree_t, text,
         rows, toks = (t.cpu().numpy() for t in loop.logit_probes())
         probe = np.where(toks >= 0, dense[rows, np.maximum(toks, 0)], 0).astype(np.float32)
         max_l = dense[np.arange(len(nxt)), nxt].astype(np.float32)
+        extra = {}
+        if spec_mode != "fmst":   # the rank pass's outputs, here from the dense logits
+            q = len(nxt)
+            rs = [OA.rank_and_second(dense[r], int(ref["input_ids"][r + 1]), int(nxt[r]))
+                  for r in range(q - 1)] + [(0, -np.inf)]
+            extra = dict(rank=torch.tensor([x[0] for x in rs], dtype=torch.int32, device=dev),
+                         second=torch.tensor(np.float32([x[1] for x in rs]), device=dev))
         more = loop.step(torch.from_numpy(nxt).to(dev), max_logit=torch.from_numpy(max_l).to(dev),
-                         probe_logit=torch.from_numpy(probe).to(dev), text_mode=flags)
+                         probe_logit=torch.from_numpy(probe).to(dev), text_mode=flags, **extra)
         assert more == (it + 1 < len(trace)), it
     assert loop.generated() == ref_gen
