@@ -272,12 +272,27 @@ def measure_next_tokens(page, dev, steps, warmup, seed=0):
     ref_ms = timed(lambda: torch.nn.functional.linear(h, w).argmax(-1))
     agree = float((out == torch.nn.functional.linear(h, w).argmax(-1)).float().mean())
     flops = 2.0 * q * VOCAB * hd
+    # HunYuan SPEC_MODE=topk / adaptive: the rank pass over one region
+    # block's rows (512, the draft cap), against the reference's
+    # F.linear + topk(3) on the same rows
+    from hsd_b200.lm_head import lm_head_rank
+    rr = min(512, q)
+    hr = h[q - rr:]
+    ids32 = out[q - rr:].to(torch.int32)
+    ref_col = torch.randint(0, VOCAB, (rr,), generator=g, device=dev, dtype=torch.int32)
+    probe = torch.nn.functional.linear(hr, w).float()[torch.arange(rr, device=dev),
+                                                      ref_col.long()].contiguous()
+    rank_ms = timed(lambda: lm_head_rank(hr, w, probe, ref_col, ids32))
+    topk_ms = timed(lambda: torch.nn.functional.linear(hr, w).topk(3, dim=-1))
     del h, w
     return {"kernel": "lm_head_argmax_kernel", "rows": q, "hidden": hd, "vocab": VOCAB,
             "launches": n, "ms": ours_ms, "tflops": flops / (ours_ms * 1e-3) / 1e12,
             "torch_linear_argmax_ms": ref_ms, "speedup_vs_torch": ref_ms / ours_ms,
             "ids_agree_with_torch": agree,
-            "logits_bytes_not_written": q * VOCAB * 2}
+            "logits_bytes_not_written": q * VOCAB * 2,
+            "rank_pass": {"rows": rr, "ms": rank_ms,
+                          "tflops": 2.0 * rr * VOCAB * hd / (rank_ms * 1e-3) / 1e12,
+                          "torch_linear_topk3_ms": topk_ms}}
 
 
 def measure_rope_append(page, dev, steps, warmup, seed=0):
