@@ -25,24 +25,39 @@ _workspaces = {}
 
 
 class AttentionWorkspace:
-    """Device scratch of the load-balanced schedule (one per device): the
-    partial rows of items cut between two SMs' shares of the work, their
-    ready flags and a launch generation.  Zero-filled once here; every call
-    leaves it ready for the next (calls sharing it must not overlap)."""
+    """Device scratch of the load-balanced schedule (one per device and
+    stream): the partial rows of items cut between two SMs' shares of the
+    work, their ready flags and a launch generation.  Zero-filled once here;
+    every call leaves it ready for the next.  Calls that share one workspace
+    must not overlap on the GPU: launches on one stream never do, which is
+    why the cache below keeps one workspace per stream."""
 
-    def __init__(self, nbytes, device):
-        self.buf = torch.zeros(nbytes + 256, dtype=torch.uint8, device=device)
+    def __init__(self, nbytes, device, stream=None):
+        dev = torch.device(device)
+        if stream is not None:
+            with torch.cuda.stream(stream):
+                self.buf = torch.zeros(nbytes + 256, dtype=torch.uint8, device=dev)
+        else:
+            self.buf = torch.zeros(nbytes + 256, dtype=torch.uint8, device=dev)
         self.base = (self.buf.data_ptr() + 255) & ~255
         self.nbytes = nbytes
 
 
-def attention_workspace(q_len, hq, hkv, device):
-    """The cached workspace of ``device``, grown to fit (q_len, hq, hkv)."""
+def attention_workspace(q_len, hq, hkv, device, stream=None):
+    """The cached workspace of (``device``, ``stream``; default the device's
+    current stream), grown to fit (q_len, hq, hkv).  A workspace that grows
+    is allocated on the same stream, and the caching allocator hands the old
+    block to no other stream, so a launch still queued on that stream keeps
+    valid scratch."""
     need = N.load().hsd_attention_workspace_bytes(int(q_len), int(hq), int(hkv))
-    key = torch.device(device).index or 0
+    dev = torch.device(device)
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    s = stream if stream is not None else torch.cuda.current_stream(dev)
+    key = (dev.index, int(s.cuda_stream))
     ws = _workspaces.get(key)
     if ws is None or ws.nbytes < need:
-        ws = AttentionWorkspace(max(need, 1 << 20), device)
+        ws = AttentionWorkspace(max(need, 1 << 20), dev, s)
         _workspaces[key] = ws
     return ws
 
@@ -69,8 +84,10 @@ def verify_attention(q, k, v, plan: TilePlan, scale=None, out=None, lse=None,
     q: ``[Hq, Q, 128]`` (or ``[1, Hq, Q, 128]``) bf16, any row/head strides;
     k, v: ``[Hkv, KV, 128]`` likewise.  Returns ``(out [Q, Hq, 128] bf16,
     lse [Hq, Q] fp32 natural log or None)``.  ``balanced`` selects the
-    stream-K schedule (equal work per SM through the cached workspace);
-    otherwise every (query tile, head pair) gets its own CTA.
+    stream-K schedule (equal work per SM through the workspace cached for
+    this device and ``stream``; calls on one stream are ordered, calls on
+    different streams get different workspaces); otherwise every (query
+    tile, head pair) gets its own CTA.
     """
     lib = N.load()
     q = _as_heads(q, "query")
@@ -86,7 +103,7 @@ def verify_attention(q, k, v, plan: TilePlan, scale=None, out=None, lse=None,
         lse = torch.empty((hq, q_len), dtype=torch.float32, device=q.device)
     ws_ptr, ws_bytes = None, 0
     if balanced:
-        ws = attention_workspace(q_len, hq, hkv, q.device)
+        ws = attention_workspace(q_len, hq, hkv, q.device, stream)
         ws_ptr, ws_bytes = ctypes.c_void_p(ws.base), ws.nbytes
     N.check(lib.hsd_verify_attention(
         N.ptr(q), q.stride(1), q.stride(0), N.ptr(k), k.stride(1), k.stride(0),

@@ -12,6 +12,8 @@
 // starts at once, which yields the same set (and so the same count and first
 // start).  The continuation tries for tree mode come packed as input
 // (hsd_continuation_trees builds them on the device).
+#include <atomic>
+
 #include "common.cuh"
 
 namespace hsd {
@@ -433,7 +435,10 @@ using namespace hsd;
 static constexpr int kMaxBlocks = 1024;
 static constexpr size_t kMaxSmem = 200 * 1024;  // filter words + FilterRecs
 static constexpr int kMaxDevices = 64;
-static bool g_attr_set[kMaxDevices] = {};
+// Set once per device; host threads driving different devices or streams may
+// race to set it, which is harmless (the attribute call is idempotent) and
+// atomic here.
+static std::atomic<bool> g_attr_set[kMaxDevices];
 
 static int accept_launch(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
                          hsd_block_result_t* results, const int32_t* next_ids,
@@ -525,13 +530,13 @@ static int accept_launch(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
     hsd_host::set_error("hsd_accept_kmp: device ordinal %d >= %d", dev, kMaxDevices);
     return HSD_ERR_UNSUPPORTED;
   }
-  if (!g_attr_set[dev]) {
+  if (!g_attr_set[dev].load(std::memory_order_acquire)) {
     rc = hsd_host::cuda_check(
         cudaFuncSetAttribute(acc::accept_kmp_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxSmem)),
         "cudaFuncSetAttribute(accept_kmp_kernel)");
     if (rc) return rc;
-    g_attr_set[dev] = true;
+    g_attr_set[dev].store(true, std::memory_order_release);
   }
   acc::accept_kmp_kernel<<<1, warps * 32, smem, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   return hsd_host::cuda_check(cudaGetLastError(), "accept_kmp_kernel launch");

@@ -24,6 +24,8 @@
 // Tiles are visited row-tile fastest (every 128-row tile of one 256-column
 // weight tile back to back), so each weight tile comes from HBM once and is
 // re-read from L2.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace hsd {
@@ -105,9 +107,12 @@ __device__ __forceinline__ void scan32(const uint32_t (&u)[32], int c0, int ncol
 }
 
 // Rank pass over 32 accumulator columns (global column gc0, tile column c0):
-// counts the columns whose bf16 logit ranks above (thr, rc) -- a larger
-// value, or the same value at a lower column -- and keeps the largest value
-// outside column ex.
+// counts the columns other than rc whose bf16 logit ranks above (thr, rc) --
+// a larger value, or the same value at a lower column -- and keeps the
+// largest value outside column ex.  Column rc itself never counts: thr comes
+// from hsd_probe_logits, whose summation order differs from the GEMM's, so
+// the GEMM's own value at rc may sit one bf16 unit above thr.  A NaN thr (a
+// probe of a bad index) counts every column, so the token ranks last.
 template <bool kFull>
 __device__ __forceinline__ void rank32(const uint32_t (&u)[32], int c0, int gc0, int ncols,
                                        float thr, int rc, int ex, int& cnt, float& best2) {
@@ -122,7 +127,7 @@ __device__ __forceinline__ void rank32(const uint32_t (&u)[32], int c0, int gc0,
     for (int h = 0; h < 2; ++h) {
       const int col = gc0 + 2 * i + h;
       if (kFull || c0 + 2 * i + h < ncols) {
-        cnt += (v[h] > thr || (v[h] == thr && col < rc)) ? 1 : 0;
+        cnt += (col != rc && (v[h] > thr || (v[h] == thr && col < rc) || thr != thr)) ? 1 : 0;
         if (col != ex && v[h] > best2) best2 = v[h];
       }
     }
@@ -360,7 +365,10 @@ int make_map2d(CUtensorMap* map, const void* base, int cols, int rows, int64_t r
 }
 
 constexpr int kMaxDevices = 64;
-bool g_attr_set[kMaxDevices] = {};
+// Per-device "attribute set" flags, atomic: host threads driving different
+// devices or streams may reach them at once (setting the attribute twice is
+// harmless).
+std::atomic<bool> g_attr_set[kMaxDevices];
 
 }  // namespace
 
@@ -371,7 +379,7 @@ extern "C" size_t hsd_lm_head_argmax_workspace_bytes(int32_t q_len) {
 
 namespace {
 
-bool g_rank_attr_set[kMaxDevices] = {};
+std::atomic<bool> g_rank_attr_set[kMaxDevices];
 
 // Shared argument checks, tensor maps and launch of both passes.
 int lm_head_launch(bool rank, const char* name, const void* hidden, int64_t hidden_row_stride,
@@ -424,8 +432,8 @@ int lm_head_launch(bool rank, const char* name, const void* hidden, int64_t hidd
     hsd_host::set_error("%s: device ordinal %d >= %d", name, dev, kMaxDevices);
     return HSD_ERR_UNSUPPORTED;
   }
-  bool& attr = rank ? g_rank_attr_set[dev] : g_attr_set[dev];
-  if (!attr) {
+  std::atomic<bool>& attr = rank ? g_rank_attr_set[dev] : g_attr_set[dev];
+  if (!attr.load(std::memory_order_acquire)) {
     rc = hsd_host::cuda_check(
         rank ? cudaFuncSetAttribute(lmh::lm_head_argmax_kernel<true>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem))
@@ -433,7 +441,7 @@ int lm_head_launch(bool rank, const char* name, const void* hidden, int64_t hidd
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
         "cudaFuncSetAttribute(lm_head_argmax_kernel)");
     if (rc) return rc;
-    attr = true;
+    attr.store(true, std::memory_order_release);
   }
   const int grid = int(std::min<int64_t>(p.tiles, sms));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

@@ -40,6 +40,8 @@
 // them into its own O in the epilogue; no second kernel.  Flags hold the
 // launch generation + 1 (the generation lives in the workspace and the last
 // CTA to exit advances it), so they never need clearing.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace hsd {
@@ -782,7 +784,10 @@ WsLayout ws_layout(int32_t q_len, int32_t hq, int32_t hkv) {
 }
 
 constexpr int kMaxDevices = 64;
-bool g_attr_set[kMaxDevices] = {};
+// Per-device "attribute set" flags, atomic: host threads driving different
+// devices or streams may reach them at once (setting the attribute twice is
+// harmless).
+std::atomic<bool> g_attr_set[kMaxDevices];
 
 }  // namespace
 
@@ -874,13 +879,13 @@ extern "C" int hsd_verify_attention(const void* q, int64_t q_row_stride, int64_t
     hsd_host::set_error("hsd_verify_attention: device ordinal %d >= %d", dev, kMaxDevices);
     return HSD_ERR_UNSUPPORTED;
   }
-  if (!g_attr_set[dev]) {
+  if (!g_attr_set[dev].load(std::memory_order_acquire)) {
     rc = hsd_host::cuda_check(
         cudaFuncSetAttribute(attn::verify_attn_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
         "cudaFuncSetAttribute(verify_attn_kernel)");
     if (rc) return rc;
-    g_attr_set[dev] = true;
+    g_attr_set[dev].store(true, std::memory_order_release);
   }
   // stream-K: one CTA per SM sharing the total work evenly; otherwise one CTA
   // per (query tile, head pair) item.

@@ -82,6 +82,11 @@ def gather_page_results(local: dict, n_pages: int, dst: int = 0, device=None):
     counts = [torch.zeros_like(n_local) for _ in range(world)]
     dist.all_gather(counts, n_local)
     max_n = int(max(c.item() for c in counts))
+    if max_n == 0:          # no rank holds a page: nothing more to gather
+        if n_pages > 0 and rank == dst:
+            raise RuntimeError(f"pages without results after the gather: "
+                               f"{list(range(n_pages))[:8]}")
+        return {} if rank == dst else None
     lens = torch.full((max_n, 2), -1, dtype=torch.int64, device=device)
     for j, i in enumerate(idx):
         lens[j, 0] = i

@@ -402,8 +402,9 @@ int hsd_lm_head_argmax(const void *hidden, int64_t hidden_row_stride, const void
  * logits): over the rows given (typically the last block's), with the
  * logits of each row rounded to bf16 as in hsd_lm_head_argmax and never
  * written,
- *   rank[r]   = #columns whose logit exceeds probe_logit[r], plus
- *               #columns below ref_col[r] whose logit equals it: the 0-based
+ *   rank[r]   = #columns other than ref_col[r] whose logit exceeds
+ *               probe_logit[r], plus #columns below ref_col[r] whose logit
+ *               equals it (a NaN probe_logit[r] gives vocab - 1): the 0-based
  *               position of the draft token ref_col[r] in a descending order
  *               that puts lower columns first among equal logits (torch
  *               leaves that order unspecified); rank[r] < k <=> the token is

@@ -106,7 +106,10 @@ def rank_and_second(row, ref_col, excl_col):
     """
     v = np.asarray(row, dtype=np.float32)
     thr = v[ref_col]
-    rank = int(np.count_nonzero(v > thr) + np.count_nonzero(v[:ref_col] == thr))
+    if np.isnan(thr):       # a probe of a bad index ranks the token last
+        rank = v.size - 1
+    else:
+        rank = int(np.count_nonzero(v > thr) + np.count_nonzero(v[:ref_col] == thr))
     second = np.float32(np.max(np.delete(v, excl_col))) if v.size > 1 else np.float32(-np.inf)
     return rank, second
 

@@ -244,3 +244,52 @@ def test_lm_head_rank_matches_torch(dev, q, vocab, hd, seed):
     rank2, second2 = lm_head_rank(h.to(dev), w.to(dev), torch.from_numpy(probe).to(dev),
                                   torch.from_numpy(ref).to(dev), ids.to(torch.int32).to(dev))
     assert torch.equal(rank2, rank) and torch.equal(second2, second)
+
+
+@pytest.mark.parametrize("q,vocab,hd,seed", [(256, 151936 // 8, 1536, 3), (96, 5000, 1024, 4)])
+def test_lm_head_rank_with_probe_kernel_logits(dev, q, vocab, hd, seed):
+    """The rank pass fed by hsd_probe_logits on random bf16 inputs, where the
+    probe's summation order differs from the GEMM's and the two bf16 logits
+    of the draft token may differ by one unit: the token must not count
+    itself, so rank < k agrees with torch.topk(k) of the fp32-accumulated
+    logits on every row whose k-th and (k+1)-th logits are more than two
+    bf16 units apart and whose draft logit is not within two units of them."""
+    from hsd_b200.lm_head import lm_head_argmax, lm_head_rank, probe_logits
+    g = torch.Generator().manual_seed(seed)
+    h = torch.randn(q, hd, generator=g).to(torch.bfloat16)
+    w = (torch.randn(vocab, hd, generator=g) / hd ** 0.5).to(torch.bfloat16)
+    logits = (h.float() @ w.float().T).to(torch.bfloat16).float()
+    ids = lm_head_argmax(h.to(dev), w.to(dev)).to(torch.int32)
+    rng = np.random.default_rng(seed)
+    order = torch.argsort(logits, dim=1, descending=True, stable=True).numpy()
+    ref = np.where(rng.random(q) < 0.7, order[np.arange(q), rng.integers(0, 6, q)],
+                   rng.integers(0, vocab, q)).astype(np.int32)
+    rows = torch.arange(q, dtype=torch.int32, device=dev)
+    d_ref = torch.from_numpy(ref).to(dev)
+    probe = probe_logits(h.to(dev), w.to(dev), rows, d_ref)
+    rank, _ = lm_head_rank(h.to(dev), w.to(dev), probe, d_ref, ids)
+    rank = rank.cpu().numpy()
+    dense = logits.numpy()
+    thr = dense[np.arange(q), ref]
+    ulp = 2.0 * np.float32(2.0 ** -7) * np.maximum(np.abs(dense).max(1), 1e-3)
+    checked = 0
+    for k in (1, 3, 5):
+        top = logits.topk(k + 1, dim=-1).values.numpy()
+        clear = ((top[:, k - 1] - top[:, k]) > ulp) & (np.abs(thr - top[:, k - 1]) > ulp) \
+            & (np.abs(thr - top[:, k]) > ulp)
+        in_topk = (logits.topk(k, dim=-1).indices.numpy() == ref[:, None]).any(1)
+        np.testing.assert_array_equal((rank < k)[clear], in_topk[clear])
+        checked += int(clear.sum())
+    assert checked > q  # most rows are decided away from a tie
+
+
+def test_lm_head_rank_nan_probe_ranks_last(dev):
+    """A NaN probe (hsd_probe_logits of a bad index) gives rank vocab - 1,
+    never a rank that would accept the token."""
+    from hsd_b200.lm_head import lm_head_argmax, lm_head_rank
+    h, w = _case(16, 1000, 64, 5)
+    ids = lm_head_argmax(h.to(dev), w.to(dev)).to(torch.int32)
+    probe = torch.full((16,), float("nan"), device=dev)
+    ref = torch.arange(16, dtype=torch.int32, device=dev)
+    rank, _ = lm_head_rank(h.to(dev), w.to(dev), probe, ref, ids)
+    assert (rank.cpu().numpy() == 999).all()

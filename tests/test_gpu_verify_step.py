@@ -1,6 +1,7 @@
 """GPU parity of a whole verification step (``VerifyStep``) against the oracle.
 
-One step of a small packed region page runs through the device path (KV
+One step of a packed page -- a small region page, and the three benchmarked
+pages at their full sizes -- runs through the device path (KV
 append, tile plan, attention on every layer, acceptance + KMP, keep indices,
 in-place compaction, visibility remap) and is checked against the oracle's
 restatement of the same iteration: per-block pointer / increment / finished
@@ -58,6 +59,24 @@ def _oracle(page):
 
 
 def test_step_matches_oracle(page):
+    _check_step_against_oracle(page)
+
+
+@pytest.mark.parametrize("name", ["stage1_regions", "stage2_page", "hunyuan_regions"])
+def test_full_size_step_matches_oracle(name):
+    """The benchmarked pages at their full sizes: stage-1 regions (Q 2176 over
+    KV 4800, 761 tiles per head, 28 layers), the stage-2 page (one
+    3072-token causal draft over a 4096-token prefix, KV 7168, 2136 tiles)
+    and the HunYuan-scale regions (24 layers, 16 / 8 heads, tight-packed
+    4096-row chunk): the stream-K split, the owner merge and the block walk
+    at the lengths and tile counts the bench times.  Attention on the first
+    and last layer (output and LSE) within the attention tolerance, the
+    per-block results, kept columns and compacted caches bit-exact."""
+    from hsd_b200 import workloads as W
+    _check_step_against_oracle(W.WORKLOADS[name](seed=0))
+
+
+def _check_step_against_oracle(page):
     from hsd_b200.accept import R
     s = _step(page)
     appended = s.cache.clone()
@@ -80,10 +99,16 @@ def test_step_matches_oracle(page):
 
     mask = torch.as_tensor(allowed)
     for l in (0, page.layers - 1):
-        ref, _ = OAtt.attention_fp32(q[l].cpu(), appended[l, 0].cpu(), appended[l, 1].cpu(),
-                                     mask)
+        ref, ref_lse = OAtt.attention_fp32(q[l].cpu(), appended[l, 0].cpu(),
+                                           appended[l, 1].cpu(), mask)
         err = (s.out[l].float().cpu() - ref).abs()
-        assert err.max().item() <= MAX_ABS and err.mean().item() <= MEAN_ABS
+        assert err.max().item() <= MAX_ABS and err.mean().item() <= MEAN_ABS, (
+            l, err.max().item(), err.mean().item())
+        rows = mask.any(1)
+        lerr = (s.lse[l].cpu()[:, rows] - ref_lse[:, rows]).abs()
+        assert lerr.max().item() <= 2e-2, (l, lerr.max().item())
+        assert torch.isneginf(s.lse[l].cpu()[:, ~rows]).all()
+    assert int(s.status.item()) == 0
 
 
 def _state(s):

@@ -59,12 +59,13 @@ def _worker(rank, world, port, n_pages, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_gather_to_rank0_over_gloo(world):
+@pytest.mark.parametrize("world,n_pages", [(2, 11), (3, 11), (2, 1), (2, 0)])
+def test_gather_to_rank0_over_gloo(world, n_pages):
+    """Every page's result reaches rank 0, including with fewer pages than
+    ranks (a rank with no page) and with no page at all (an empty dict)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    n_pages = 11
     procs = [ctx.Process(target=_worker, args=(r, world, port, n_pages, q)) for r in range(world)]
     for p in procs:
         p.start()
