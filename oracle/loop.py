@@ -18,9 +18,9 @@ iteration (hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py):
 * the KV cache grows by the packed input of every forward (DynamicCache) and
   loses the compacted columns.
 
-Only region blocks are restated: the page block's text/select/bbox parsers
-need the tokenizer and stay on the host (D:1337-1419), so the loop also has
-no "last block finished" stop (D:1591-1592).  ``model(input_ids,
+Without ``page`` every block is a region block; with it the last block is
+the page block of :mod:`oracle.page` (its parser-driven candidates,
+D:1337-1567, and the "last block finished" stop, D:1591-1592).  ``model(input_ids,
 position_ids, allowed, kv_tokens)`` stands for the target forward + argmax:
 ``allowed`` is the step's [Q, KV] visibility, ``kv_tokens`` the token of
 every KV column.
@@ -58,16 +58,23 @@ def ratio_logits(logits, next_ids, input_ids, spans, states):
 
 
 def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1,
-                   max_iters=1000, logits_model=None, text_mode=()):
+                   max_iters=1000, logits_model=None, text_mode=(), page=None):
     """Run the loop; returns ``(generated tokens per block, trace)``.
 
     ``trace`` holds, per iteration, the packed ``input_ids``,
-    ``position_ids``, the bool ``allowed`` mask [Q, KV], the blocks' modes
-    and the compaction action taken after the step.  With ``logits_model``
-    (same arguments, returns float32 logits ``[Q, V]`` of bf16 values) the
-    next tokens are its first argmax per row and the logit-ratio rules of
-    ``cfg`` read its entries; ``text_mode`` holds the blocks whose parser is
-    in text mode.
+    ``position_ids``, the bool ``allowed`` mask [Q, KV], the KV column ids
+    the previous compaction kept (``kept_column_ids``: ids numbered in order
+    of appearance), the blocks' modes and the compaction action taken after
+    the step.  With ``logits_model`` (same arguments, returns float32 logits
+    ``[Q, V]`` of bf16 values) the next tokens are its first argmax per row
+    and the logit-ratio rules of ``cfg`` read its entries; ``text_mode``
+    holds the blocks whose parser is in text mode.
+
+    ``page`` (an :class:`oracle.page.OraclePage`) makes the last block the
+    page block, as in the reference: no repetition stop for it (D:1306),
+    its next input from the parser-driven candidates (D:1337-1567), the
+    parser's text mode for every block's tree fallback (D:1229, D:1257), and
+    the loop ends when it finishes (D:1591-1592).
     """
     nb = len(prompts)
     lens = [len(p) for p in prompts]
@@ -75,6 +82,9 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
     position_ids = np.concatenate([np.arange(n, dtype=np.int64) for n in lens])
     mask = initial_packed_mask(lens)
     kv_tokens = input_ids.copy()
+    kv_ids = np.arange(len(input_ids), dtype=np.int64)
+    next_id = len(input_ids)
+    kept_ids = np.zeros(0, dtype=np.int64)
     pointer = [int(x) for x in np.cumsum(lens) - 1]
     states = [BlockState(draft=list(d), mws=cfg.match_window_size) for d in drafts]
     new_tokens = 0
@@ -106,6 +116,7 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
                                   dtype=np.int64)
         step = dict(input_ids=input_ids.copy(), position_ids=position_ids.copy(),
                     allowed=allowed.copy(), modes=[st.mode for st in states],
+                    kept_column_ids=kept_ids.copy(),
                     q_blocks=pointer[-1] + 1)   # rows owned by blocks (the rest: tight padding)
         trace.append(step)
         kv_base = kv - q
@@ -120,18 +131,29 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
             if st.mode == FINISHED:
                 bs = be
                 continue
-            st.text_mode = b in text_mode
+            is_page = page is not None and b == nb - 1
+            st.text_mode = (page.parser.text_mode if page is not None else b in text_mode)
             ptr, nxt, inc, fin = accept_block(st, bs, be, next_list, input_list, cfg, filt,
-                                              kv_base, lambda row: allowed[row], False,
+                                              kv_base, lambda row: allowed[row], is_page,
                                               logits=logits, is_last_block=(b == nb - 1))
             pointer[b] = ptr
             new_tokens += inc
             bs = be
             if fin:
                 continue
-            window, matches, trie = realign_block(st, cfg)
-            ids, pos, kind, n = next_block_input(st, cfg, window, matches, trie, nxt,
-                                                 int(position_ids[ptr]) + 1)
+            if is_page:                                        # D:1337-1567, last block
+                ids, pos, kind, n_valid, n_match, tree = page.next_input(
+                    st.gen, inc, st.mws, [x.gen for x in states],
+                    [x.mode == FINISHED for x in states], int(position_ids[ptr]) + 1)
+                st.matches_len = n_match
+                st.valid_count = n_valid
+                st.mode = {"causal": SPEC, "tree": TREE, "single": 0}[kind]
+                st.tree_tokens, st.tree_parents = (tree if tree is not None else (None, None))
+                n = len(ids)
+            else:
+                window, matches, trie = realign_block(st, cfg)
+                ids, pos, kind, n = next_block_input(st, cfg, window, matches, trie, nxt,
+                                                     int(position_ids[ptr]) + 1)
             new_ids.append(ids)
             new_pos.append(pos)
             new_lens[b] = n
@@ -141,7 +163,8 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
                 new_masks[b] = tree_block_mask(st.tree_parents, n)
             else:
                 new_masks[b] = normal_block_mask(n)
-        if new_tokens >= max_new_tokens or all(st.mode == FINISHED for st in states):
+        if new_tokens >= max_new_tokens or all(st.mode == FINISHED for st in states) or (
+                page is not None and states[-1].mode == FINISHED):
             step["action"] = "stop"
             break
         filt = pad_filter(filt, input_ids, cfg.pad_token_id)
@@ -153,6 +176,7 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
         mask = apply_to_mask(mask, keep, action)
         if action == "compact":
             kv_tokens = kv_tokens[keep]
+            kv_ids = kv_ids[keep]
         # HSD_TIGHT_PACK: the packed input is padded to a multiple of
         # _HSD_Q_BLOCK with pad tokens at position 0 (D:1619-1632)
         pad_n = (-sum(new_lens)) % Q_BLOCK if cfg.tight_pack else 0
@@ -163,7 +187,10 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
             new_pos.append([0] * pad_n)
         input_ids = np.concatenate([np.asarray(x, dtype=np.int64) for x in new_ids])
         position_ids = np.concatenate([np.asarray(x, dtype=np.int64) for x in new_pos])
+        kept_ids = kv_ids.copy()
         kv_tokens = np.concatenate([kv_tokens, input_ids])
+        kv_ids = np.concatenate([kv_ids, np.arange(next_id, next_id + len(input_ids))])
+        next_id += len(input_ids)
         pointer = [int(x) for x in np.cumsum(new_lens) - 1]
     return [list(st.gen) for st in states], trace
 

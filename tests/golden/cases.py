@@ -5,6 +5,7 @@ reference's outputs (plus an input checksum that catches RNG drift).
 """
 from __future__ import annotations
 
+import json
 import math
 import random
 
@@ -126,4 +127,87 @@ def attention_cases():
     q, k, v = qkv(6, 1, 200, 150, seed=2)
     out.append(("masked_rows_mqa", (q, k, v, _dense(small), None,
                                     [0, 149, 150, 155, 160, 199])))
+    return out
+
+
+# ---------------------------------------------------------------- batch_generate
+_WORDS = ("alpha beta gamma delta kappa omega sigma theta lambda zeta table figure "
+          "value result model page line text data item score total mean rate").split()
+
+
+def _sentence(rng, n_words):
+    words = [str(rng.choice(_WORDS)) for _ in range(n_words)]
+    if rng.random() < 0.5:
+        words.insert(int(rng.integers(0, len(words))), str(int(rng.integers(10, 9999))))
+    s = " ".join(words)
+    return s[0].upper() + s[1:] + "."
+
+
+def _perturb_chars(rng, text, p):
+    out = []
+    for c in text:
+        u = rng.random()
+        if u < p / 3:
+            continue                                       # deletion
+        out.append(chr(int(rng.integers(97, 123))) if u < 2 * p / 3 else c)
+        if u > 1 - p / 3:
+            out.append(chr(int(rng.integers(97, 123))))    # insertion
+    return "".join(out)
+
+
+def _page_json(texts, rng):
+    cats = ["Text", "Title", "Caption", "Section-header"]
+    items = []
+    for i, t in enumerate(texts):
+        x1, y1 = int(rng.integers(10, 500)), int(rng.integers(10, 900))
+        box = [x1, y1, x1 + int(rng.integers(50, 900)), y1 + int(rng.integers(20, 90))]
+        items.append('{"bbox": [%d, %d, %d, %d], "category": "%s", "text": %s}'
+                     % (*box, cats[i % len(cats)], json.dumps(t)))
+    return "[" + ", ".join(items) + "]"
+
+
+def batch_generate_cases():
+    """Seeded pages for the reference's ``batch_generate``: region blocks with
+    a target text and a draft of it (clean, noisy, useless, or a periodic
+    text that ends in the repetition stop), then the page block whose target
+    is dots.ocr-style layout JSON quoting the region texts, so its parser
+    passes through select, bbox and text modes.  Each case also names the
+    loop switches (tree decoding, compaction period, tight packing, the
+    speculative length cap)."""
+    specs = [
+        dict(name="plain_period3", seed=11, regions=3, tree=False, compact_period=3,
+             tight_pack=False, max_spec_len=0, periodic=False),
+        dict(name="tree_period1", seed=12, regions=4, tree=True, compact_period=1,
+             tight_pack=False, max_spec_len=0, periodic=False),
+        dict(name="tree_tight_period2_repeat", seed=13, regions=4, tree=True,
+             compact_period=2, tight_pack=True, max_spec_len=0, periodic=True),
+        dict(name="tree_tight_speccap", seed=14, regions=3, tree=True, compact_period=3,
+             tight_pack=True, max_spec_len=24, periodic=False),
+        dict(name="tight_never_compact", seed=15, regions=3, tree=False, compact_period=0,
+             tight_pack=True, max_spec_len=0, periodic=False),
+    ]
+    out = []
+    for sp in specs:
+        rng = np.random.default_rng(sp["seed"])
+        texts, drafts, prompts = [], [], []
+        for b in range(sp["regions"]):
+            prompts.append("R%02d crop, read the text:" % b)
+            if sp["periodic"] and b == 1:
+                t = "xy" * 40
+                d = t[:50]
+            else:
+                t = _sentence(rng, int(rng.integers(6, 12)))
+                kind = b % 3
+                d = (_perturb_chars(rng, t, 0.02) if kind == 0 else
+                     _perturb_chars(rng, t, 0.12) if kind == 1 else
+                     _sentence(rng, 5))
+            texts.append(t)
+            drafts.append(d)
+        page = _page_json(texts, rng)
+        prompts.append("PAGE%02d, give the layout as JSON:" % sp["seed"])
+        texts.append(page)
+        out.append(dict(name=sp["name"], prompts=prompts, texts=texts, drafts=drafts,
+                        tree=sp["tree"], compact_period=sp["compact_period"],
+                        tight_pack=sp["tight_pack"], max_spec_len=sp["max_spec_len"],
+                        max_new_tokens=100000))
     return out

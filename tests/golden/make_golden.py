@@ -2,7 +2,9 @@
 
 Run in a container where the reference checkout is present:
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference [kmp|blockmask|attention|batch_generate ...]
+
+(or set ``HSD_REFERENCE_ROOT``).
 
 It imports ``hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py`` from the
 reference and records, for seeded inputs:
@@ -15,7 +17,15 @@ reference and records, for seeded inputs:
 * ``attention_*.npz`` -- ``flex_attention_forward`` outputs (D:72-135) with
                          the module's ``torch.compile``d FlexAttention swapped
                          for the eager one, because the compiled kernel
-                         rejects ``return_lse`` on the CPU.
+                         rejects ``return_lse`` on the CPU;
+* ``batch_generate.json`` -- the unmodified ``DotsOCRForCausalLM.batch_generate``
+                         (D:923-1810) driven by the stand-in model and
+                         tokenizer of ``standin.py`` over packed pages of
+                         region blocks and a layout-JSON page block: every
+                         forward's packed input ids, positions, the KV
+                         columns the previous compaction kept and a hash of
+                         the dense mask, then the generated tokens, the
+                         decode count and the compaction counters.
 
 The fixtures are committed; tests read them without the reference.
 """
@@ -103,12 +113,71 @@ def make_attention(ref):
     return n
 
 
+def run_reference_batch_generate(ref, case):
+    """One ``DotsOCRForCausalLM.batch_generate`` call of the reference,
+    unmodified, on the stand-in model and tokenizer (tests/golden/standin.py):
+    returns its outputs and the per-forward trace.  The module-level switches
+    the reference reads at import (HSD_TIGHT_PACK, HSD_COMPACT_PERIOD,
+    HSD_MAX_SPEC_LEN, D:52-62) are set on the imported module; the page
+    block's pre-tokenizer (D:625-645) is the stand-in tokenizer and the
+    cached candidate trees are rebuilt for every call."""
+    from tests.golden import standin as SI
+
+    tok = SI.CharTokenizer()
+    ref._HSD_TIGHT_PACK = bool(case["tight_pack"])
+    ref._HSD_COMPACT_PERIOD = int(case["compact_period"])
+    ref._HSD_MAX_SPEC_LEN = int(case["max_spec_len"])
+    ref._HSD_MAX_TREE_LEN = 0
+    ref._pre_tokenizer = tok
+    ref.CACHED_SELECT_MODE_ONE_MATCHES_TREE = None
+    ref.CACHED_BBOX_MODE_ONE_MATCHES_TREE = None
+    prompts = [tok.encode(t) for t in case["prompts"]]
+    texts = [tok.encode(t) for t in case["texts"]]
+    model = SI.StandInLM(prompts, texts)
+    ids, mask, pos, pointer = SI.packed_prefill(prompts)
+    drafts = [{"block_content": d, "raw_block_content": d} for d in case["drafts"]]
+    gen, decode_times, stats = ref.DotsOCRForCausalLM.batch_generate(
+        model, input_ids=ids, attention_mask=mask, position_ids=pos, pointer=pointer,
+        tokenizer=tok, draft=drafts, enable_tree_decode=bool(case["tree"]),
+        eos_token_id=[SI.EOS], max_new_tokens=int(case["max_new_tokens"]))
+    return dict(generated=[list(map(int, g)) for g in gen], decode_times=int(decode_times),
+                compact_calls=int(stats[6]), compact_skipped=int(stats[7]),
+                steps=[SI.step_digest(t) for t in model.trace],
+                first_steps=[dict(input_ids=t["input_ids"].tolist(),
+                                  position_ids=t["position_ids"].tolist())
+                             for t in model.trace[:6]])
+
+
+def make_batch_generate(ref):
+    import contextlib
+    import io
+
+    from tests.golden.cases import batch_generate_cases
+    out = []
+    for case in batch_generate_cases():
+        with contextlib.redirect_stdout(io.StringIO()):   # the loop prints its statistics
+            got = run_reference_batch_generate(ref, case)
+        out.append(dict(case, **got))
+    with open(os.path.join(HERE, "batch_generate.json"), "w") as f:
+        json.dump(out, f, separators=(",", ":"))
+    return len(out)
+
+
 def main():
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("HSD_REFERENCE_ROOT")
+    if not root:
+        raise SystemExit("usage: make_golden.py <reference checkout> "
+                         "(or set HSD_REFERENCE_ROOT)")
     ref = _import_reference(root)
-    print("kmp cases", make_kmp(ref))
-    print("blockmask cases", make_blockmask(ref))
-    print("attention cases", make_attention(ref))
+    only = sys.argv[2:] or ["kmp", "blockmask", "attention", "batch_generate"]
+    if "kmp" in only:
+        print("kmp cases", make_kmp(ref))
+    if "blockmask" in only:
+        print("blockmask cases", make_blockmask(ref))
+    if "attention" in only:
+        print("attention cases", make_attention(ref))
+    if "batch_generate" in only:
+        print("batch_generate cases", make_batch_generate(ref))
 
 
 if __name__ == "__main__":
