@@ -12,6 +12,7 @@ nothing is expanded the way ``repeat_kv`` (D:137-146) does.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import math
 
@@ -153,3 +154,40 @@ def flex_attention_forward(module, query, key, value, attention_mask, scaling=No
         query, key, value = (t.to(torch.bfloat16) for t in (query, key, value))
     out, lse = verify_attention(query, key, value, plan, scale=scaling)
     return out.to(dtype).unsqueeze(0), lse.to(dtype).unsqueeze(0)
+
+
+# ---------------------------------------------------------------- transformers
+ATTENTION_NAME = "hsd_b200"
+_step = {"mask": None}
+
+
+@contextlib.contextmanager
+def step_attention_mask(mask):
+    """Within the block, attention calls that receive no mask use ``mask``
+    (a :class:`PackedMask` or :class:`TilePlan`).  transformers drops a mask
+    object it cannot prepare for a custom attention implementation, so the
+    verification loop hands each step's mask to the decoder layers this way;
+    every layer of the step then reuses the one tile plan."""
+    prev = _step["mask"]
+    _step["mask"] = mask
+    try:
+        yield
+    finally:
+        _step["mask"] = prev
+
+
+def transformers_attention(module, query, key, value, attention_mask, scaling=None,
+                           dropout=0.0, **kwargs):
+    """The attention callable registered with transformers' AttentionInterface
+    under :data:`ATTENTION_NAME` (the role of D:378-381): the packed
+    verification attention over the mask given, or the step's mask of
+    :func:`step_attention_mask` when transformers passes none."""
+    mask = attention_mask if attention_mask is not None else _step["mask"]
+    return flex_attention_forward(module, query, key, value, mask, scaling)
+
+
+def register_transformers_attention():
+    """Register :func:`transformers_attention` as ``"hsd_b200"``; returns the name."""
+    from transformers import AttentionInterface
+    AttentionInterface.register(ATTENTION_NAME, transformers_attention)
+    return ATTENTION_NAME

@@ -17,6 +17,8 @@
 //    phases (compact_planes_kernel) -- no global spin-waits in either.
 #include <cooperative_groups.h>
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace cg = cooperative_groups;
@@ -383,7 +385,9 @@ namespace {
 // With at least this many planes one CTA per plane keeps most SMs streaming.
 constexpr int kPlaneCtaMinPlanes = 64;
 constexpr int kMaxDevices = 64;
-bool g_bulk_attr_set[kMaxDevices] = {};
+// Per-device "attribute set" flags, atomic: host threads driving different
+// devices or streams may reach them at once (setting it twice is harmless).
+std::atomic<bool> g_bulk_attr_set[kMaxDevices];
 }  // namespace
 
 extern "C" {
@@ -411,13 +415,13 @@ int hsd_compact_kv(const uint64_t* plane_ptrs, int32_t n_planes, int32_t row_byt
       hsd_host::set_error("hsd_compact_kv: device ordinal %d >= %d", dev, kMaxDevices);
       return HSD_ERR_UNSUPPORTED;
     }
-    if (!g_bulk_attr_set[dev]) {
+    if (!g_bulk_attr_set[dev].load(std::memory_order_acquire)) {
       rc = hsd_host::cuda_check(
           cudaFuncSetAttribute(compact::compact_plane_bulk_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, compact::kBulkSmem),
           "cudaFuncSetAttribute(compact_plane_bulk_kernel)");
       if (rc) return rc;
-      g_bulk_attr_set[dev] = true;
+      g_bulk_attr_set[dev].store(true, std::memory_order_release);
     }
     compact::compact_plane_bulk_kernel<<<n_planes, compact::kBulkThreads, compact::kBulkSmem,
                                          st>>>(plane_ptrs, n_planes, row_bytes, keep_idx, n_keep,

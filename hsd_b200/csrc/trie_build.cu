@@ -22,6 +22,8 @@
 // Levels stop at max_depth or once the BFS index passes the cap.
 #include <climits>
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace hsd {
@@ -253,7 +255,9 @@ __global__ void __launch_bounds__(kThreads) trie_kernel(const Params p) {
 
 namespace {
 constexpr int kMaxDevices = 64;
-bool g_trie_attr[kMaxDevices] = {};
+// Per-device "attribute set" flags, atomic: host threads driving different
+// devices or streams may reach them at once (setting it twice is harmless).
+std::atomic<bool> g_trie_attr[kMaxDevices];
 }  // namespace
 
 extern "C" int hsd_continuation_trees(const int32_t* draft_pool, const int32_t* draft_off,
@@ -294,13 +298,13 @@ extern "C" int hsd_continuation_trees(const int32_t* draft_pool, const int32_t* 
     hsd_host::set_error("hsd_continuation_trees: device ordinal %d >= %d", dev, kMaxDevices);
     return HSD_ERR_UNSUPPORTED;
   }
-  if (!g_trie_attr[dev]) {
+  if (!g_trie_attr[dev].load(std::memory_order_acquire)) {
     rc = hsd_host::cuda_check(cudaFuncSetAttribute(trie::trie_kernel,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    int(smem)),
                               "cudaFuncSetAttribute(trie_kernel)");
     if (rc) return rc;
-    g_trie_attr[dev] = true;
+    g_trie_attr[dev].store(true, std::memory_order_release);
   }
   trie::trie_kernel<<<n_trees, trie::kThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   return hsd_host::cuda_check(cudaGetLastError(), "trie_kernel launch");

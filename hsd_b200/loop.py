@@ -41,7 +41,7 @@ import numpy as np
 import torch
 
 from . import _native as N
-from .accept import DOTS_SENTINEL, FLAG_TEXT_MODE, F, R, accept_kmp, make_config
+from .accept import DOTS_SENTINEL, FLAG_PAGE_BLOCK, FLAG_TEXT_MODE, F, R, accept_kmp, make_config
 from .compaction import compact_bits, compact_kv, keep_indices
 from .plan import SEG_CAUSAL, SEG_NONE, SEG_SINGLE, SEG_TREE, PackedMask, pack_bits
 from .trie import continuation_trees
@@ -71,7 +71,15 @@ class VerifyLoop:
                  repeat_sentinel=DOTS_SENTINEL, kv_planes=None, row_bytes=0,
                  kv_capacity=None, spec_thresh=1.0, tree_thresh=1.0, variant="dots",
                  formula_tokens=(3, 1099), spec_mode="fmst", spec_topk=3, spec_margin=2.0,
+                 packed=None, page_block=False, pad_rows_inherit=False, compact_hook=None,
                  device="cuda"):
+        if packed is not None:
+            # the caller's packed prefill: (input_ids, position_ids, pointer)
+            p_ids, p_pos, p_ptr = packed[:3]
+            p_ids = np.asarray(p_ids, dtype=np.int64).reshape(-1)
+            ends = np.asarray(p_ptr, dtype=np.int64).reshape(-1) + 1
+            starts = np.concatenate([[0], ends[:-1]])
+            prompts = [p_ids[a:b] for a, b in zip(starts, ends)]
         if len(prompts) != len(drafts) or not prompts:
             raise ValueError("one draft per prompt, at least one block")
         self.device = torch.device(device)
@@ -115,15 +123,26 @@ class VerifyLoop:
         cap = self.max_new_tokens + max([len(d) for d in self.drafts] + [0]) + self.mil + 8
         self.gen_cap = cap
 
+        # the last block is the page block: its next input comes from the
+        # caller (page_next of step()), no repetition stop, no token KMP
+        self.page_block = bool(page_block)
+        self.pad_rows_inherit = bool(pad_rows_inherit)
+        self.compact_hook = compact_hook
+        if self.page_block:
+            self.drafts[-1] = []
         # host state of the current step
         self.input_ids = np.concatenate([np.asarray(p, dtype=np.int64) for p in prompts])
-        self.position_ids = np.concatenate([np.arange(n, dtype=np.int64) for n in lens])
+        if packed is not None:
+            self.position_ids = np.asarray(packed[1], dtype=np.int64).reshape(-1).copy()
+        else:
+            self.position_ids = np.concatenate([np.arange(n, dtype=np.int64) for n in lens])
         self.q_start = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
         self.q_len = np.asarray(lens, dtype=np.int64)
         self.kinds = [SEG_CAUSAL] * self.nb
         self.trees = None                            # device trees of this step's TREE blocks
         self.tree_slot = [-1] * self.nb              # row of block b in self.trees
         self.tree_parents = [None] * self.nb         # host parents of block b's tree
+        self.host_tree = [None] * self.nb            # (tokens, parents) of a host-built tree
         self.modes = [N.HSD_MODE_NORMAL] * self.nb   # D:978
         # non-pad rows per block (the reference counts them while
         # block_valid_counts is None, D:1108-1111)
@@ -147,6 +166,8 @@ class VerifyLoop:
             blocks[b, F["mws"]] = self.mws0
             blocks[b, F["seg"]] = b
             doff += len(self.drafts[b])
+        if self.page_block:
+            blocks[self.nb - 1, F["flags"]] = FLAG_PAGE_BLOCK
         self.d_draft_off = torch.from_numpy(blocks[:, F["draft_off"]].copy()).to(dev)
         self.d_draft_len = torch.from_numpy(blocks[:, F["draft_len"]].copy()).to(dev)
         self.blocks = torch.from_numpy(blocks).to(dev)
@@ -158,6 +179,10 @@ class VerifyLoop:
         self.results = torch.zeros((self.nb, len(R)), dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.kv_tokens = torch.from_numpy(self.input_ids.astype(np.int32)).to(dev)
+        if packed is not None and len(packed) > 3 and packed[3] is not None:
+            # visibility the blocks' rows inherit from outside their own prompt
+            vis = packed[3]
+            self.seg_bits[:, :vis.shape[1]] = vis
         self._mask = None
 
     # ------------------------------------------------------------------
@@ -174,18 +199,37 @@ class VerifyLoop:
                 row_seg[qs:qs + ql] = b
                 if self.kinds[b] == SEG_TREE:
                     # node i sees itself and its ancestors (D:1506-1533), rows
-                    # from the tree kernel; pad rows see nothing
+                    # from the tree kernel or the host tree; pad rows see nothing
                     tw = (ql + 63) // 64
-                    i = self.tree_slot[b]
                     n = int(self.valid[b])
-                    rows = torch.zeros((ql, tw), dtype=torch.int64, device=self.device)
-                    w = min(tw, self.trees.anc.shape[2])
-                    rows[:n, :w] = self.trees.anc[i, :n, :w]
+                    if self.host_tree[b] is not None:
+                        anc = np.zeros((ql, tw * 64), dtype=bool)
+                        par = self.host_tree[b][1]
+                        for j in range(n):
+                            a = j
+                            while a >= 0:
+                                anc[j, a] = True
+                                a = par[a]
+                        rows = torch.from_numpy(pack_bits(anc).view(np.int64)).to(self.device)
+                    else:
+                        i = self.tree_slot[b]
+                        rows = torch.zeros((ql, tw), dtype=torch.int64, device=self.device)
+                        w = min(tw, self.trees.anc.shape[2])
+                        rows[:n, :w] = self.trees.anc[i, :n, :w]
                     tree_rows.append(rows.reshape(-1))
                     segs[b, 3], segs[b, 4] = tree_off, tw
                     tree_off += ql * tw
+            kv_bits = self.seg_bits
+            q_blocks = int(self.q_start[-1] + self.q_len[-1]) if self.nb else 0
+            if self.pad_rows_inherit and q > q_blocks:
+                # tight padding rows inherit the last block's row and see
+                # none of the new columns (D:1640-1644)
+                segs = np.concatenate([segs, np.asarray([[q_blocks, q - q_blocks, SEG_NONE,
+                                                          0, 0, 0]], dtype=np.int32)])
+                row_seg[q_blocks:] = self.nb
+                kv_bits = torch.cat([self.seg_bits, self.seg_bits[self.nb - 1:self.nb]])
             tree_bits = torch.cat(tree_rows) if tree_rows else None
-            self._mask = PackedMask.from_bits(q, self.kv_len, segs, row_seg, self.seg_bits,
+            self._mask = PackedMask.from_bits(q, self.kv_len, segs, row_seg, kv_bits,
                                               self.device, tree_bits)
         ids = torch.from_numpy(self.input_ids.astype(np.int32)).to(self.device)
         pos = torch.from_numpy(self.position_ids).to(self.device)
@@ -215,7 +259,7 @@ class VerifyLoop:
         return (torch.from_numpy(rows).to(self.device), torch.from_numpy(toks).to(self.device))
 
     def step(self, next_ids, max_logit=None, probe_logit=None, text_mode=None, rank=None,
-             second=None):
+             second=None, page_next=None):
         """Consume the target argmax of every packed row; prepare the next step.
 
         With thresholds below 1, ``max_logit`` (float32 ``[Q]``, the maximal
@@ -231,6 +275,11 @@ class VerifyLoop:
         ``[Q]``: the row's second best logit);
         :func:`hsd_b200.lm_head.lm_head_rank` computes both for the last
         block's rows, the only rows these modes read.
+
+        With a page block, ``page_next(loop, gen, increment, mws, pos_base)``
+        gives its next input (a :class:`hsd_b200.page_block.PageInput`) from
+        its generated tokens ``gen`` after the step; it runs on the host
+        while the device computes the other blocks' trees and keep indices.
         """
         if self.done:
             raise RuntimeError("the loop has finished")
@@ -256,19 +305,36 @@ class VerifyLoop:
             flags = np.asarray([FLAG_TEXT_MODE if t else 0 for t in text_mode], dtype=np.int32)
             if flags.size != self.nb:
                 raise ValueError("text_mode: one flag per block")
+            if self.page_block:
+                flags[-1] |= FLAG_PAGE_BLOCK
             self.blocks[:, F["flags"]] = torch.from_numpy(flags).to(dev)
         toff = np.zeros(self.nb, dtype=np.int32)
         tnodes = np.zeros(self.nb, dtype=np.int32)
         d_tok = d_par = torch.zeros(1, dtype=torch.int32, device=dev)
-        if self.trees is not None:
-            # this step's tree blocks read their nodes straight from the tree kernel's rows
-            for b in range(self.nb):
-                if self.modes[b] == N.HSD_MODE_TREE:
-                    toff[b] = self.tree_slot[b] * self.trees.cap
-                    tnodes[b] = self.valid[b]
+        host_trees = [b for b in range(self.nb)
+                      if self.modes[b] == N.HSD_MODE_TREE and self.host_tree[b] is not None]
+        if self.trees is not None or host_trees:
+            # this step's tree blocks read their nodes straight from the tree
+            # kernel's rows; host-built trees (the page block's) follow them
+            base = 0
+            toks, pars = [], []
+            if self.trees is not None:
+                toks.append(self.trees.tokens.reshape(-1))
+                pars.append(self.trees.parents.reshape(-1))
+                base = int(self.trees.tokens.numel())
+                for b in range(self.nb):
+                    if self.modes[b] == N.HSD_MODE_TREE and self.host_tree[b] is None:
+                        toff[b] = self.tree_slot[b] * self.trees.cap
+                        tnodes[b] = self.valid[b]
+            for b in host_trees:
+                t, par = self.host_tree[b]
+                toff[b], tnodes[b] = base, len(t)
+                toks.append(torch.tensor(t, dtype=torch.int32, device=dev))
+                pars.append(torch.tensor(par, dtype=torch.int32, device=dev))
+                base += len(t)
             self.blocks[:, F["tree_off"]] = torch.from_numpy(toff).to(dev)
             self.blocks[:, F["tree_nodes"]] = torch.from_numpy(tnodes).to(dev)
-            d_tok, d_par = self.trees.tokens.reshape(-1), self.trees.parents.reshape(-1)
+            d_tok, d_par = torch.cat(toks), torch.cat(pars)
         self.filter.zero_()
         self.out_bits.zero_()
         cfg = make_config(self.nb, kv, q, self.stride, self.eos, self.mws0, self.mws_ub,
@@ -290,7 +356,8 @@ class VerifyLoop:
         # continuation trees of the blocks without exactly one match, one launch
         want = [b for b in range(self.nb)
                 if self.tree_decode and self.modes[b] != N.HSD_MODE_FINISHED
-                and not res[b][R["finished"]] and res[b][R["match_count"]] != 1]
+                and not res[b][R["finished"]] and res[b][R["match_count"]] != 1
+                and not (self.page_block and b == self.nb - 1)]
         new_trees, new_slot, host_trees = None, [-1] * self.nb, {}
         if want:
             idx = torch.tensor(want, dtype=torch.long, device=dev)
@@ -304,10 +371,25 @@ class VerifyLoop:
                 new_slot[b] = i
             self._check()
 
+        # the page block's next input, from the host (D:1337-1567)
+        self.step_finished = [self.modes[b] == N.HSD_MODE_FINISHED or bool(res[b][R["finished"]])
+                              for b in range(self.nb)]
+        page_in = None
+        last = self.nb - 1
+        if (self.page_block and page_next is not None
+                and self.modes[last] != N.HSD_MODE_FINISHED and not res[last][R["finished"]]):
+            blk = self.blocks[last].cpu().numpy()
+            off, n = int(blk[F["gen_off"]]), int(blk[F["gen_len"]])
+            gen = self.gen_pool[off:off + n].cpu().tolist()
+            r = res[last]
+            page_in = page_next(self, gen, int(r[R["increment"]]), int(blk[F["mws"]]),
+                                int(self.position_ids[int(r[R["pointer"]])]) + 1)
+            self.blocks[last, F["matches_len"]] = int(page_in.matches)
         # next inputs (D:1421-1565) from the result rows
         new_ids, new_pos, new_lens = [], [], [0] * self.nb
         new_modes, new_valid, new_kinds = list(self.modes), [0] * self.nb, list(self.kinds)
         new_parents = [None] * self.nb
+        new_host_tree = [None] * self.nb
         for b in range(self.nb):
             if self.modes[b] == N.HSD_MODE_FINISHED:
                 new_kinds[b] = SEG_NONE   # no rows any more
@@ -318,7 +400,18 @@ class VerifyLoop:
                 new_modes[b], new_kinds[b] = N.HSD_MODE_FINISHED, SEG_NONE
                 continue
             base = int(self.position_ids[int(r[R["pointer"]])]) + 1
-            if r[R["match_count"]] == 1:
+            if page_in is not None and b == self.nb - 1:
+                toks, pos = list(page_in.ids), list(page_in.pos)
+                if page_in.kind == "spec":
+                    new_modes[b], new_kinds[b] = N.HSD_MODE_SPEC, SEG_CAUSAL
+                elif page_in.kind == "tree":
+                    new_modes[b], new_kinds[b] = N.HSD_MODE_TREE, SEG_TREE
+                    new_parents[b] = list(page_in.parents)
+                    new_host_tree[b] = (list(toks[:page_in.valid]), list(page_in.parents))
+                else:
+                    new_modes[b], new_kinds[b] = N.HSD_MODE_NORMAL, SEG_SINGLE
+                new_valid[b] = int(page_in.valid)
+            elif r[R["match_count"]] == 1:
                 toks = self.drafts[b][int(r[R["slice_begin"]]):int(r[R["slice_end"]])]
                 n = len(toks)
                 if not self.tight:
@@ -343,7 +436,8 @@ class VerifyLoop:
             new_pos.append(pos)
             new_lens[b] = len(toks)
         if self.new_tokens >= self.max_new_tokens or all(
-                m == N.HSD_MODE_FINISHED for m in new_modes):
+                m == N.HSD_MODE_FINISHED for m in new_modes) or (
+                self.page_block and new_modes[-1] == N.HSD_MODE_FINISHED):   # D:1589-1592
             self.modes = new_modes
             self.done = True
             return False
@@ -372,6 +466,8 @@ class VerifyLoop:
             if self.kv_planes is not None:
                 compact_kv(self.kv_planes, self.row_bytes, keep_idx, counts=counts,
                            status=self.status)
+            if self.compact_hook is not None:
+                self.compact_hook(keep_idx, counts, n_keep)
             self.kv_tokens = self.kv_tokens[keep_idx[:n_keep].long()]
             self.seg_bits = compact_bits(self.out_bits, keep_idx, counts, self.stride)
             kv = n_keep
@@ -400,6 +496,7 @@ class VerifyLoop:
         self.q_start = ends - self.q_len
         self.modes, self.valid, self.kinds = new_modes, new_valid, new_kinds
         self.trees, self.tree_slot, self.tree_parents = new_trees, new_slot, new_parents
+        self.host_tree = new_host_tree
         self.kv_len = kv + int(self.input_ids.size)
         if self.kv_len > self.kv_cap:
             raise N.HSDError(f"KV columns {self.kv_len} exceed the loop's capacity {self.kv_cap}")

@@ -313,7 +313,8 @@ class PageBlock:
         """The page block's next input after a step that generated
         ``increment`` tokens (``gen``: all its tokens so far; ``mws``: its
         match window size after the step; ``outputs`` / ``finished``: the
-        other blocks' generated tokens and whether they finished)."""
+        other blocks' generated tokens and whether they finished, or
+        ``outputs`` a callable returning both, called only in text mode)."""
         self.parser.feed(self.tok.decode(gen[-increment:]) if increment else "")
         w = min(self.mws_ub, int(mws))
         window = list(gen[-w:])
@@ -328,6 +329,8 @@ class PageBlock:
             self.mode = "text"
             wtext = unescape_json_fragment(self.tok.decode(window))
             wclean = cleaned_with_map(wtext)[0]
+            if callable(outputs):
+                outputs, finished = outputs()
             text, toks, clean, where = self._others(outputs, finished)
             matches = kmp_matches(clean, wclean) if wclean else []
             trie = None if len(matches) == 1 else continuation_trie(toks, window[-1],
