@@ -276,8 +276,8 @@ class VerifyLoop:
         :func:`hsd_b200.lm_head.lm_head_rank` computes both for the last
         block's rows, the only rows these modes read.
 
-        With a page block, ``page_next(loop, gen, increment, mws, pos_base)``
-        gives its next input (a :class:`hsd_b200.page_block.PageInput`) from
+        With a page block, ``page_next(loop, gen, increment, mws, pos_base,
+        next_token)`` gives its next input (a :class:`hsd_b200.page_block.PageInput`) from
         its generated tokens ``gen`` after the step; it runs on the host
         while the device computes the other blocks' trees and keep indices.
         """
@@ -383,7 +383,8 @@ class VerifyLoop:
             gen = self.gen_pool[off:off + n].cpu().tolist()
             r = res[last]
             page_in = page_next(self, gen, int(r[R["increment"]]), int(blk[F["mws"]]),
-                                int(self.position_ids[int(r[R["pointer"]])]) + 1)
+                                int(self.position_ids[int(r[R["pointer"]])]) + 1,
+                                int(r[R["next_token"]]))
             self.blocks[last, F["matches_len"]] = int(page_in.matches)
         # next inputs (D:1421-1565) from the result rows
         new_ids, new_pos, new_lens = [], [], [0] * self.nb
@@ -435,7 +436,12 @@ class VerifyLoop:
             new_ids.append(toks)
             new_pos.append(pos)
             new_lens[b] = len(toks)
-        if self.new_tokens >= self.max_new_tokens or all(
+        if self.page_block and self.variant == "hunyuan":
+            # the HunYuan loop counts the page block's own tokens (H:2133)
+            produced = int(self.blocks[self.nb - 1, F["gen_len"]].item())
+        else:
+            produced = self.new_tokens
+        if produced >= self.max_new_tokens or all(
                 m == N.HSD_MODE_FINISHED for m in new_modes) or (
                 self.page_block and new_modes[-1] == N.HSD_MODE_FINISHED):   # D:1589-1592
             self.modes = new_modes
@@ -474,9 +480,12 @@ class VerifyLoop:
         elif not rule:                                # dead columns masked (D:1724-1729)
             self.seg_bits = self.out_bits.clone()
             self.seg_bits[:, :nw] &= keep_bits[None, :nw]
-            self.compactions_skipped += 1
+            if self.variant != "hunyuan":             # dots counts masked steps (D:1730)
+                self.compactions_skipped += 1
         else:
             self.seg_bits = self.out_bits.clone()
+            if self.variant == "hunyuan":             # HunYuan: nothing to drop (H:2275)
+                self.compactions_skipped += 1
         self.compaction_s += time.perf_counter() - t_c
 
         # the next packed input and its KV columns; tight packing pads the

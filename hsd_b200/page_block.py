@@ -309,12 +309,15 @@ class PageBlock:
         n = len(ids)
         return list(ids) + [self.tok.pad_token_id] * (math.ceil(n / self.mil) * self.mil - n)
 
-    def next_input(self, gen, increment, mws, pos_base, outputs, finished):
+    def next_input(self, gen, increment, mws, pos_base, outputs, finished, next_token=None):
         """The page block's next input after a step that generated
         ``increment`` tokens (``gen``: all its tokens so far; ``mws``: its
         match window size after the step; ``outputs`` / ``finished``: the
         other blocks' generated tokens and whether they finished, or
-        ``outputs`` a callable returning both, called only in text mode)."""
+        ``outputs`` a callable returning both, called only in text mode;
+        ``next_token``: the step's next token of the block, the input of a
+        normal step -- the target's own token at the last accepted node,
+        which a tree fallback may have replaced in ``gen``, D:1288)."""
         self.parser.feed(self.tok.decode(gen[-increment:]) if increment else "")
         w = min(self.mws_ub, int(mws))
         window = list(gen[-w:])
@@ -357,7 +360,76 @@ class PageBlock:
             ids = self._pad(tokens)
             pos = [d + pos_base for d in depths] + [0] * (len(ids) - n)
             return PageInput("tree", ids, pos, n, len(matches), parents, depths)
-        nxt = gen[-1]
+        nxt = gen[-1] if next_token is None else int(next_token)
+        if self.tight:
+            return PageInput("normal", [nxt], [pos_base], 1, len(matches))
+        return PageInput("normal", [nxt] + [self.tok.pad_token_id] * (self.mil - 1),
+                         [pos_base] + [0] * (self.mil - 1), 1, len(matches))
+
+
+class HunyuanPageBlock(PageBlock):
+    """The HunYuan pipeline's page block (hsd/hunyuan_ocr_pipeline/
+    modeling_hunyuan_vl_hsd.py H:1900-2025): no layout parser -- every step
+    matches the window's cleaned characters against the other blocks'
+    decoded outputs, each prefixed with a blank line; a unique match makes
+    the rest of that output (not re-escaped) the next speculative input, with
+    no length cap; otherwise the continuation trie of the window over the
+    re-tokenized outputs, capped at ``tree_cap`` nodes (H:2046-2104)."""
+
+    def _others(self, outputs, finished):
+        if len(outputs) == 0:
+            one = self.norm_draft[0] if self.norm_draft else ""
+            one = "\n\n" + one.replace("\n\n", "\n")
+            chars, where = cleaned_with_map(one)
+            return ([self.norm_draft[0] if self.norm_draft else ""],
+                    [self.tok.encode(one, add_special_tokens=False)], [chars], [where])
+        text, toks, clean, where = [], [], [], []
+        todo = [b for b in range(len(outputs)) if b not in self._finished_text]
+        dec = (self.tok.batch_decode([outputs[b] for b in todo], skip_special_tokens=True)
+               if todo else [])
+        fresh = {}
+        for b, d in zip(todo, dec):
+            d = "\n\n" + d.replace("\n\n", "\n")
+            c, w = cleaned_with_map(d)
+            entry = (d, self.tok.encode(d, add_special_tokens=False), c, w)
+            fresh[b] = entry
+            if finished[b]:
+                self._finished_text[b] = entry
+        for b in range(len(outputs)):
+            d, t, c, w = self._finished_text.get(b) or fresh[b]
+            text.append(d)
+            toks.append(t)
+            clean.append(c)
+            where.append(w)
+        return text, toks, clean, where
+
+    def next_input(self, gen, increment, mws, pos_base, outputs, finished, next_token=None):
+        w = min(self.mws_ub, int(mws))
+        window = list(gen[-w:])
+        self.mode = "text"
+        wclean = cleaned_with_map(self.tok.decode(window))[0]
+        if callable(outputs):
+            outputs, finished = outputs()
+        text, toks, clean, where = self._others(outputs, finished)
+        matches = kmp_matches(clean, wclean) if wclean else []
+        if len(matches) == 1:
+            item, start, _ = matches[0]
+            start = where[item][start + len(wclean) - 1]
+            rest = text[item][start + 1:]
+            overlap = self.tok.decode(gen[-1])
+            if rest.startswith(overlap):
+                rest = rest[len(overlap):]
+            ids = self._pad([gen[-1]] + self.tok.encode(rest, add_special_tokens=False))
+            valid = len(ids) if self.tight else len(ids) - ids.count(self.tok.pad_token_id)
+            return PageInput("spec", ids, list(range(pos_base, pos_base + len(ids))), valid, 1)
+        trie = continuation_trie(toks, window[-1], self.depth)
+        if self.tree_decode and trie.has_children():
+            tokens, depths, parents = trie.bfs(self.cap)
+            n = len(tokens)
+            ids = self._pad(tokens)
+            pos = [d + pos_base for d in depths] + [0] * (len(ids) - n)
+            return PageInput("tree", ids, pos, n, len(matches), parents, depths)
+        nxt = gen[-1] if next_token is None else int(next_token)
         if self.tight:
             return PageInput("normal", [nxt], [pos_base], 1, len(matches))
         return PageInput("normal", [nxt] + [self.tok.pad_token_id] * (self.mil - 1),

@@ -144,7 +144,7 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
             if is_page:                                        # D:1337-1567, last block
                 ids, pos, kind, n_valid, n_match, tree = page.next_input(
                     st.gen, inc, st.mws, [x.gen for x in states],
-                    [x.mode == FINISHED for x in states], int(position_ids[ptr]) + 1)
+                    [x.mode == FINISHED for x in states], int(position_ids[ptr]) + 1, nxt)
                 st.matches_len = n_match
                 st.valid_count = n_valid
                 st.mode = {"causal": SPEC, "tree": TREE, "single": 0}[kind]
@@ -163,7 +163,10 @@ def reference_loop(prompts, drafts, model, cfg, max_new_tokens, compact_period=1
                 new_masks[b] = tree_block_mask(st.tree_parents, n)
             else:
                 new_masks[b] = normal_block_mask(n)
-        if new_tokens >= max_new_tokens or all(st.mode == FINISHED for st in states) or (
+        # the HunYuan loop stops on the page block's own length (H:2133)
+        produced = (len(states[-1].gen) if cfg.variant == "hunyuan" and page is not None
+                    else new_tokens)
+        if produced >= max_new_tokens or all(st.mode == FINISHED for st in states) or (
                 page is not None and states[-1].mode == FINISHED):
             step["action"] = "stop"
             break

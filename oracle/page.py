@@ -195,9 +195,10 @@ class OraclePage:
             state = (wclean, t_draft, t_map)
         return matches, tree, state
 
-    def next_input(self, gen, increment, mws, generated, finished, pos_base):
+    def next_input(self, gen, increment, mws, generated, finished, pos_base, next_token):
         """``(ids, pos, kind, valid, matches_len, parents)`` of the last block:
-        kind "causal" (speculative), "tree" or "single" (normal)."""
+        kind "causal" (speculative), "tree" or "single" (normal, whose input
+        is ``next_token_int``, D:1546-1565)."""
         cfg, tok = self.cfg, self.tok
         pad, mil = cfg.pad_token_id, cfg.min_input_length
         matches, tree, state = self.candidates(gen, increment, mws, generated, finished)
@@ -228,7 +229,84 @@ class OraclePage:
                 ids += [pad] * (math.ceil(len(ids) / mil) * mil - len(ids))
                 pos += [0] * (len(ids) - len(pos))
             return ids, pos, "tree", len(tokens), len(matches), (tokens, parents)
-        nxt = gen[-1]
+        nxt = next_token
+        if cfg.tight_pack:
+            return [nxt], [pos_base], "single", 1, len(matches), None
+        return ([nxt] + [pad] * (mil - 1), [pos_base] + [0] * (mil - 1), "single", 1,
+                len(matches), None)
+
+
+class OracleHunyuanPage(OraclePage):
+    """The HunYuan loop's last block (hsd/hunyuan_ocr_pipeline/
+    modeling_hunyuan_vl_hsd.py H:1900-2025 and H:2046-2104): the text rule
+    at every step without a parser, the other blocks' outputs prefixed with
+    a blank line and not re-escaped, no speculative length cap, the tree cap
+    ``max_tree_len``."""
+
+    def next_input(self, gen, increment, mws, generated, finished, pos_base, next_token):
+        cfg, tok = self.cfg, self.tok
+        pad, mil = cfg.pad_token_id, cfg.min_input_length
+        w = min(cfg.match_window_size_upper_bound, mws)
+        window = gen[-w:]
+        wtext = tok.decode(window)
+        wclean = [c for c in clean_string_and_get_maps(wtext)['cleaned_string']]
+        if len(generated) > 1:
+            t_draft, t_tok, t_clean, t_map = [], [], [], []
+            for bid in range(len(generated) - 1):
+                if bid in self.cache:
+                    c = self.cache[bid]
+                else:
+                    one = tok.batch_decode([generated[bid]], skip_special_tokens=True)[0]
+                    one = one.replace("\n\n", "\n")
+                    one = "\n\n" + one
+                    cl = clean_string_and_get_maps(one)
+                    c = (one, tok.encode(one, add_special_tokens=False),
+                         [ch for ch in cl['cleaned_string']], cl['new_to_old_map'])
+                    if finished[bid]:
+                        self.cache[bid] = c
+                t_draft.append(c[0])
+                t_tok.append(c[1])
+                t_clean.append(c[2])
+                t_map.append(c[3])
+        else:
+            one = self.norm_draft[0] if self.norm_draft else ""
+            one = one.replace("\n\n", "\n")
+            one = "\n\n" + one
+            t_draft = [self.norm_draft[0]] if self.norm_draft else [""]
+            t_tok = [tok.encode(one, add_special_tokens=False)]
+            cl = clean_string_and_get_maps(one)
+            t_clean = [[ch for ch in cl['cleaned_string']]]
+            t_map = [cl['new_to_old_map']]
+        if len(wclean) != 0:
+            _, matches = find_all_matches_kmp(t_clean, wclean, compute_lps(wclean), 1)
+        else:
+            matches = []
+        tree = None
+        if len(matches) != 1:
+            tree, _ = find_all_matches_kmp(t_tok, window, compute_lps(window),
+                                           cfg.max_tree_depth)
+        if len(matches) == 1:
+            item_idx, start, _ = matches[0]
+            start += len(wclean) - 1
+            start = t_map[item_idx][start]
+            one = t_draft[item_idx][start + 1:]
+            might = tok.decode(gen[-1])
+            if one.startswith(might):
+                one = one[len(might):]
+            ids = [gen[-1]] + tok.encode(one, add_special_tokens=False)
+            if not cfg.tight_pack:
+                ids += [pad] * (math.ceil(len(ids) / mil) * mil - len(ids))
+            valid = len(ids) - (ids.count(pad) if not cfg.tight_pack else 0)
+            return ids, list(range(pos_base, pos_base + len(ids))), "causal", valid, 1, None
+        if cfg.enable_tree_decode and len(tree.children) > 0:
+            tokens, depths, parents = trie_bfs(tree, cfg.max_tree_len)
+            ids = list(tokens)
+            pos = [d + pos_base for d in depths]
+            if not cfg.tight_pack:
+                ids += [pad] * (math.ceil(len(ids) / mil) * mil - len(ids))
+            pos += [0] * (len(ids) - len(pos))
+            return ids, pos, "tree", len(tokens), len(matches), (tokens, parents)
+        nxt = next_token
         if cfg.tight_pack:
             return [nxt], [pos_base], "single", 1, len(matches), None
         return ([nxt] + [pad] * (mil - 1), [pos_base] + [0] * (mil - 1), "single", 1,

@@ -211,3 +211,20 @@ def batch_generate_cases():
                         tight_pack=sp["tight_pack"], max_spec_len=sp["max_spec_len"],
                         max_new_tokens=100000))
     return out
+
+
+def hunyuan_generate_cases():
+    """Pages for the HunYuan loop: region blocks as in
+    :func:`batch_generate_cases` and a page block whose target is the
+    regions' texts as plain paragraphs (the HunYuan page output is text, not
+    layout JSON); no reference run exists for these (its module needs a
+    transformers model class absent here), the oracle's restatement is the
+    check."""
+    out = []
+    for c in batch_generate_cases():
+        texts = list(c["texts"][:-1])
+        page = "\n\n".join(texts)
+        out.append(dict(c, name="hunyuan_" + c["name"],
+                        prompts=c["prompts"][:-1] + ["PAGE%s, read the page:" % c["name"][:2]],
+                        texts=texts + [page]))
+    return out

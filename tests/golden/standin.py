@@ -135,6 +135,8 @@ class StandInLM:
         if past_key_values is None:
             past_key_values = StandInCache(dev)
         before = past_key_values.columns()
+        if position_ids.dim() == 3:        # HunYuan's [1, 4, Q] positions: row 0
+            position_ids = position_ids[:, 0]
         past_key_values.append(input_ids[0], position_ids[0])
         cols = past_key_values.columns()
         q, kv = input_ids.shape[1], cols.shape[0]

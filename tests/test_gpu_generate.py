@@ -51,3 +51,42 @@ def test_drop_in_batch_generate_matches_reference_runs(case, monkeypatch):
     assert decode_times == case["decode_times"]
     assert (stats[6], stats[7]) == (case["compact_calls"], case["compact_skipped"])
     assert len(stats) == 8
+
+
+HCASES = __import__("tests.golden.cases", fromlist=["x"]).hunyuan_generate_cases()
+
+
+@pytest.mark.parametrize("case", HCASES, ids=[c["name"] for c in HCASES])
+def test_hunyuan_drop_in_matches_oracle_loop(case, monkeypatch):
+    """The HunYuan drop-in (``batch_generate_hunyuan``, the H:1426-1448
+    signature) against the oracle's restatement of the HunYuan loop on the
+    same stand-in model: bit-identical forwards (ids, row-0 positions of the
+    ``[1, 4, Q]`` position ids, kept KV columns, mask) and the dict return
+    of H:2324-2343."""
+    from hsd_b200.generate import batch_generate_hunyuan
+    from tests.test_hunyuan_loop import oracle_hunyuan_run
+    dev = torch.device("cuda:0")
+    monkeypatch.setenv("HSD_TIGHT_PACK", "1" if case["tight_pack"] else "0")
+    monkeypatch.setenv("HSD_COMPACT_PERIOD", str(case["compact_period"]))
+    gen_ref, trace = oracle_hunyuan_run(case)
+    tok = SI.CharTokenizer()
+    prompts = [tok.encode(t) for t in case["prompts"]]
+    texts = [tok.encode(t) for t in case["texts"]]
+    model = SI.StandInLM(prompts, texts)
+    ids, mask, pos, pointer = SI.packed_prefill(prompts, device=dev)
+    pos4 = pos[:, None].expand(1, 4, -1)
+    drafts = [{"block_content": d} for d in case["drafts"]]
+    out = batch_generate_hunyuan(
+        model, input_ids=ids, attention_mask=mask, position_ids=pos4, pointer=pointer,
+        tokenizer=tok, draft=drafts, enable_tree_decode=bool(case["tree"]),
+        eos_token_id=[SI.EOS], max_new_tokens=int(case["max_new_tokens"]))
+    assert len(model.trace) == len(trace)
+    for i, (t, ref) in enumerate(zip(model.trace, trace)):
+        assert SI.step_digest(t) == SI.trace_digest(ref), f"step {i}"
+    assert out["generated_tokens"] == gen_ref
+    assert out["decode_times"] == len(trace)
+    assert out["decode_token_num"] == len(gen_ref[-1])
+    used = out["used_time"]
+    assert used["kv_compact_calls"] == sum(1 for s in trace if s["action"] != "stop")
+    assert used["kv_compact_skipped"] == sum(1 for s in trace if s["action"] == "none")
+    assert len(out["compute_intensity"]) == len(trace)

@@ -99,10 +99,10 @@ def test_package_page_block_matches_oracle_page_block(case):
     calls = []
     orig = page.next_input
 
-    def both(gen, inc, mws, generated, finished, pos_base):
-        want = orig(gen, inc, mws, generated, finished, pos_base)
+    def both(gen, inc, mws, generated, finished, pos_base, nxt):
+        want = orig(gen, inc, mws, generated, finished, pos_base, nxt)
         got = mine.next_input(list(gen), inc, mws, pos_base,
-                              [list(g) for g in generated[:-1]], list(finished[:-1]))
+                              [list(g) for g in generated[:-1]], list(finished[:-1]), nxt)
         kind = {"causal": "spec", "tree": "tree", "single": "normal"}[want[2]]
         assert (got.kind, got.ids, got.pos, got.valid, got.matches) == (
             kind, want[0], want[1], want[3], want[4]), f"call {len(calls)}"
