@@ -87,6 +87,12 @@ __device__ __forceinline__ void rotate8(uint4 a, uint4 b, uint4 c1, uint4 c2, ui
 }
 
 __global__ void __launch_bounds__(kThreads) rope_append_kernel(const Params p) {
+  // Launched with programmatic dependent launch: the CTAs are scheduled
+  // while the previous kernel on the stream finishes, and nothing is read
+  // before it has completed.  The next kernel may be scheduled at once: it
+  // waits for this one's completion in its own griddepcontrol.wait.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int64_t total = p.n_q + p.n_k + p.n_v;
   for (int64_t u = int64_t(blockIdx.x) * kThreads + threadIdx.x; u < total;
        u += int64_t(gridDim.x) * kThreads) {
@@ -179,7 +185,16 @@ extern "C" int hsd_rope_append(void* q, int64_t q_row_stride, const void* k, con
   const int64_t total = p.n_q + p.n_k + p.n_v;
   const int64_t blocks = (total + rope::kThreads - 1) / rope::kThreads;
   const int grid = int(blocks < 148 * 16 ? blocks : 148 * 16);
-  rope::rope_append_kernel<<<grid, rope::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      p);
-  return hsd_host::cuda_check(cudaGetLastError(), "rope_append_kernel launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(rope::kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return hsd_host::cuda_check(cudaLaunchKernelEx(&cfg, rope::rope_append_kernel, p),
+                              "rope_append_kernel launch");
 }

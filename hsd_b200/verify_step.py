@@ -129,18 +129,24 @@ class VerifyStep:
         self.attn_launches_per_step = L
         # append 1 + plan 2 + attention L + accept 1 + keep 1 + compact 1 + bits 1
         self.kernel_launches_per_step = 1 + 2 + L + 4
+        # the end-to-end form appends layer by layer: L appends instead of 1
+        self.kernel_launches_per_host_step = L + 2 + L + 4
 
     # ------------------------------------------------------------------
     def _ptr(self, t):
         return C.c_void_p(t.data_ptr())
 
-    def run(self, stream=None, attn_events=None, phase_events=None, layer_ready=None):
+    def run(self, stream=None, attn_events=None, phase_events=None, layer_ready=None,
+            buffers=0):
         """Launch one verification step on ``stream`` (no host sync).
 
         ``attn_events[l]`` (start, end) bracket layer l's attention call;
         ``phase_events`` (dict of name -> (start, end)) bracket the phases
-        append / plan / accept / keep / compact / bits; layer l's attention
-        waits for ``layer_ready[l]`` (an event) when given.
+        append / plan / accept / keep / compact / bits.  With
+        ``layer_ready`` (one event per layer) the step reads its query and
+        new K/V rows from input set ``buffers`` (see :meth:`run_from_host`)
+        and appends and attends layer by layer, layer l waiting only for
+        ``layer_ready[l]``.
 
         Independent launches run on a second stream: the KV append beside
         the tile plan (both feed the attention), the visibility-row remap
@@ -166,8 +172,10 @@ class VerifyStep:
         if concurrent:
             side.wait_stream(main)
         mark("append", 0)
-        N.check(lib.hsd_kv_append(p(self.planes), p(self.new_planes), self.planes.numel(),
-                                  self.row_bytes, self.prefix, self.q_len, sst), "hsd_kv_append")
+        if layer_ready is None:
+            N.check(lib.hsd_kv_append(p(self.planes), p(self.new_planes), self.planes.numel(),
+                                      self.row_bytes, self.prefix, self.q_len, sst),
+                    "hsd_kv_append")
         mark("append", 1)
         with torch.cuda.stream(main):
             self.filter.zero_()
@@ -181,8 +189,8 @@ class VerifyStep:
         mark("plan", 1)
         if concurrent:
             main.wait_stream(side)
-        # 3. attention, every layer
-        self.run_attention(main, attn_events, layer_ready)
+        # 3. attention, every layer (with its own append when the rows arrive per layer)
+        self.run_attention(main, attn_events, layer_ready, buffers)
         # 4. acceptance + KMP
         mark("accept", 0)
         N.check(lib.hsd_accept_kmp(
@@ -212,20 +220,29 @@ class VerifyStep:
         if concurrent:
             main.wait_stream(side)
 
-    def run_attention(self, stream=None, attn_events=None, layer_ready=None):
-        """The step's attention launches alone (every layer, current plan)."""
+    def run_attention(self, stream=None, attn_events=None, layer_ready=None, buffers=0):
+        """The step's attention launches alone (every layer, current plan);
+        with ``layer_ready`` each layer first waits for its event and
+        appends its own new K/V rows from input set ``buffers``."""
         lib = N.load()
         st = N.stream_handle(stream)
         ts = stream if stream is not None else torch.cuda.current_stream()
         p = self._ptr
         scale = 1.0 / np.sqrt(self.d)
         ql, kvl, hq, hkv, d = self.q_len, self.kv_len, self.hq, self.hkv, self.d
+        qset = self.q if buffers == 0 else self._alt["q"]
+        per = 2 * hkv
         for l in range(self.L):
-            q = self.q[l]
+            q = qset[l]
             k = self.cache[l, 0]
             v = self.cache[l, 1]
             if layer_ready is not None:
                 ts.wait_event(layer_ready[l])
+                src = self.new_planes if buffers == 0 else self._alt["new_planes"]
+                N.check(lib.hsd_kv_append(C.c_void_p(self.planes.data_ptr() + 8 * l * per),
+                                          C.c_void_p(src.data_ptr() + 8 * l * per), per,
+                                          self.row_bytes, self.prefix, self.q_len, st),
+                        "hsd_kv_append")
             if attn_events is not None:
                 attn_events[l][0].record(stream)
             N.check(lib.hsd_verify_attention(
@@ -263,47 +280,79 @@ class VerifyStep:
         h = self.host_buffers()
         return sum(h[k].numel() * h[k].element_size() for k in ("results", "counts"))
 
-    def run_from_host(self, stream=None):
+    def _second_input_set(self):
+        if getattr(self, "_alt", None) is None:
+            q2 = torch.empty_like(self.q)
+            kv2 = torch.empty_like(self.new_kv)
+            planes = [kv2[l, kv, h].data_ptr() for l in range(self.L) for kv in range(2)
+                      for h in range(self.hkv)]
+            self._alt = dict(q=q2, new_kv=kv2, new_planes=torch.tensor(
+                planes, dtype=torch.int64, device=self.device))
+        return self._alt
+
+    def run_from_host(self, stream=None, buffers=0, fork=True):
         """End-to-end step: pinned host inputs -> device step -> results to host.
 
-        The new K/V rows and token ids are copied on the compute stream (the
-        KV append needs all of them); Q, three quarters of the bytes, goes
-        layer by layer on a copy stream, each layer's attention waiting only
-        for its own Q, so the copies overlap the step's kernels.
+        Every layer's query rows and new K/V rows (all but a few KB of the
+        step's bytes) go layer by layer on a copy stream into input set
+        ``buffers`` (0 or 1); each layer's append and attention wait only for
+        that layer's rows, so the copies overlap the step's kernels.  The
+        copy stream waits for nothing else: alternating ``buffers`` between
+        consecutive steps lets step i+1's copies run under step i's kernels
+        (set k is rewritten only after the step that last read it, two steps
+        back, has finished).  The token ids (KBs) go on the compute stream.
+        Inside a CUDA graph capture the copy stream forks from the capturing
+        stream when ``fork`` (the graph's first step) and otherwise queues
+        behind its own earlier copies: replays of a graph never overlap.
         """
         h = self.host_buffers()
         cs = stream if stream is not None else torch.cuda.current_stream()
         if getattr(self, "_copy_stream", None) is None:
             self._copy_stream = torch.cuda.Stream(device=self.device)
-            self._q_ready = [torch.cuda.Event() for _ in range(self.L)]
+            self._ready = [[torch.cuda.Event() for _ in range(self.L)] for _ in range(2)]
+            self._set_free = [torch.cuda.Event(), torch.cuda.Event()]
+            self._set_used = [False, False]
         xs = self._copy_stream
-        xs.wait_stream(cs)  # the previous step no longer reads q
+        q, nkv = (self.q, self.new_kv) if buffers == 0 else (
+            self._second_input_set()["q"], self._second_input_set()["new_kv"])
+        if torch.cuda.is_current_stream_capturing():
+            if fork:
+                xs.wait_stream(cs)
+        elif self._set_used[buffers]:
+            xs.wait_event(self._set_free[buffers])  # the step that last read this set is done
+        else:
+            xs.wait_stream(cs)
         with torch.cuda.stream(xs):
             for l in range(self.L):
-                self.q[l].copy_(h["q"][l], non_blocking=True)
-                self._q_ready[l].record(xs)
+                q[l].copy_(h["q"][l], non_blocking=True)
+                nkv[l].copy_(h["new_kv"][l], non_blocking=True)
+                self._ready[buffers][l].record(xs)
         with torch.cuda.stream(cs):
-            self.new_kv.copy_(h["new_kv"], non_blocking=True)
             self.input_ids.copy_(h["input_ids"], non_blocking=True)
             self.next_ids.copy_(h["next_ids"], non_blocking=True)
-        self.run(cs, layer_ready=self._q_ready)
-        cs.wait_stream(xs)
+        self.run(cs, layer_ready=self._ready[buffers], buffers=buffers)
+        if not torch.cuda.is_current_stream_capturing():
+            self._set_free[buffers].record(cs)
+            self._set_used[buffers] = True
         with torch.cuda.stream(cs):
             h["results"].copy_(self.results, non_blocking=True)
             h["counts"].copy_(self.counts, non_blocking=True)
 
     def capture(self, from_host=False, attention_only=False):
-        """A CUDA graph of one whole step (``run`` or ``run_from_host``, or
-        only its attention launches): the launches replay with no host work
-        between them.  Call :meth:`run` once before capturing (first-call
-        setup such as kernel attributes must not happen inside a capture)."""
+        """A CUDA graph of one whole step (``run`` or, ``from_host``, two
+        consecutive ``run_from_host`` steps on alternating input sets, or
+        only the step's attention launches): the launches replay with no
+        host work between them.  Call :meth:`run` (and, for ``from_host``,
+        :meth:`run_from_host` on both sets) once before capturing: first-call
+        setup must not happen inside a capture."""
         torch.cuda.synchronize(self.device)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             if attention_only:
                 self.run_attention()
             elif from_host:
-                self.run_from_host()
+                self.run_from_host(buffers=0, fork=True)
+                self.run_from_host(buffers=1, fork=False)
             else:
                 self.run()
         torch.cuda.synchronize(self.device)

@@ -117,14 +117,20 @@ def _state(s):
 
 
 def test_from_host_and_graph_match_device_form(page):
+    """The end-to-end form (rows copied layer by layer into alternating
+    device input sets, appended per layer) and its two-step CUDA graph give
+    the device-resident form's state after the same number of steps."""
     a = _step(page)
     a.run()
     a.run()
     want = _state(a)
+    a.run()
+    a.run()
+    want4 = _state(a)
 
     b = _step(page)
-    b.run_from_host()
-    b.run_from_host()
+    b.run_from_host(buffers=0)
+    b.run_from_host(buffers=1)
     h = b.host_buffers()
     torch.cuda.synchronize()
     assert torch.equal(h["results"], b.results.cpu())
@@ -133,9 +139,11 @@ def test_from_host_and_graph_match_device_form(page):
         assert torch.equal(x, y)
 
     c = _step(page)
-    c.run_from_host()
+    c.run_from_host(buffers=0)
+    c.run_from_host(buffers=1)
     g = c.capture(from_host=True)
     g.replay()
-    for x, y in zip(want, _state(c)):
+    for x, y in zip(want4, _state(c)):
         assert torch.equal(x, y)
+    assert int(c.status.item()) == 0
     del g
