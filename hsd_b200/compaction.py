@@ -30,16 +30,24 @@ def plane_pointers(tensors, device=None):
     return torch.tensor(addrs, dtype=torch.int64, device=dev)
 
 
-def keep_indices(live_bits, filter_bits, kv_len, stream=None):
-    """keep = OR(live rows) & ~filter -> (keep_bits, keep_idx, counts[2]) on device."""
+def keep_indices(live_bits, filter_bits, kv_len, stream=None, out=None):
+    """keep = OR(live rows) & ~filter -> (keep_bits, keep_idx, counts[2]) on device.
+
+    ``out``: optional preallocated ``(keep_bits, keep_idx, counts)`` with at
+    least ``ceil(kv_len / 64)`` words and ``kv_len`` indices."""
     lib = N.load()
     dev = live_bits.device
     n_live = live_bits.shape[0] if live_bits.dim() == 2 else 1
     stride = live_bits.shape[-1]
     nw = (kv_len + 63) // 64
-    keep_bits = torch.empty(nw, dtype=torch.int64, device=dev)
-    keep_idx = torch.empty(max(kv_len, 1), dtype=torch.int32, device=dev)
-    counts = torch.empty(2, dtype=torch.int32, device=dev)
+    if out is not None:
+        keep_bits, keep_idx, counts = out
+        if keep_bits.numel() < nw or keep_idx.numel() < max(kv_len, 1) or counts.numel() < 2:
+            raise ValueError("keep_indices: preallocated outputs too small")
+    else:
+        keep_bits = torch.empty(nw, dtype=torch.int64, device=dev)
+        keep_idx = torch.empty(max(kv_len, 1), dtype=torch.int32, device=dev)
+        counts = torch.empty(2, dtype=torch.int32, device=dev)
     N.check(lib.hsd_keep_indices(N.ptr(live_bits), n_live, stride, N.ptr(filter_bits), kv_len,
                                  N.ptr(keep_bits), N.ptr(keep_idx), N.ptr(counts),
                                  N.stream_handle(stream)), "hsd_keep_indices")

@@ -179,6 +179,18 @@ class VerifyLoop:
         self.results = torch.zeros((self.nb, len(R)), dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.kv_tokens = torch.from_numpy(self.input_ids.astype(np.int32)).to(dev)
+        self.gen_host = [[] for _ in range(self.nb)]
+        self._flags = blocks[:, F["flags"]].copy()
+        self._upd_cols = torch.tensor([F["mode"], F["q_start"], F["q_len"], F["valid_count"],
+                                       F["flags"], F["tree_off"], F["tree_nodes"]],
+                                      dtype=torch.long, device=dev)
+        self._zero_i32 = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._pinned = None
+        self._copied = torch.cuda.Event()
+        self._keep_out = (torch.empty(self.stride, dtype=torch.int64, device=dev),
+                          torch.empty(self.kv_cap, dtype=torch.int32, device=dev),
+                          torch.empty(2, dtype=torch.int32, device=dev))
+        self._blk = blocks
         if packed is not None and len(packed) > 3 and packed[3] is not None:
             # visibility the blocks' rows inherit from outside their own prompt
             vis = packed[3]
@@ -231,9 +243,10 @@ class VerifyLoop:
             tree_bits = torch.cat(tree_rows) if tree_rows else None
             self._mask = PackedMask.from_bits(q, self.kv_len, segs, row_seg, kv_bits,
                                               self.device, tree_bits)
-        ids = torch.from_numpy(self.input_ids.astype(np.int32)).to(self.device)
-        pos = torch.from_numpy(self.position_ids).to(self.device)
-        return ids, pos, self._mask
+            # the step's ids and positions go up once, with the mask
+            self._ids = torch.from_numpy(self.input_ids.astype(np.int32)).to(self.device)
+            self._pos = torch.from_numpy(self.position_ids).to(self.device)
+        return self._ids, self._pos, self._mask
 
     def logit_probes(self):
         """``(rows, toks)``, int32 device ``[Q]``: the logits
@@ -294,35 +307,29 @@ class VerifyLoop:
         self.decode_times += 1
         q = int(self.input_ids.size)
         kv = self.kv_len
-        upd = torch.tensor(np.stack([np.asarray(self.modes), self.q_start, self.q_len,
-                                     np.asarray(self.valid)], 1),
-                           dtype=torch.int32, device=dev)
-        self.blocks[:, F["mode"]] = upd[:, 0]
-        self.blocks[:, F["q_start"]] = upd[:, 1]
-        self.blocks[:, F["q_len"]] = upd[:, 2]
-        self.blocks[:, F["valid_count"]] = upd[:, 3]
+        nb = self.nb
         if text_mode is not None:
             flags = np.asarray([FLAG_TEXT_MODE if t else 0 for t in text_mode], dtype=np.int32)
-            if flags.size != self.nb:
+            if flags.size != nb:
                 raise ValueError("text_mode: one flag per block")
             if self.page_block:
                 flags[-1] |= FLAG_PAGE_BLOCK
-            self.blocks[:, F["flags"]] = torch.from_numpy(flags).to(dev)
-        toff = np.zeros(self.nb, dtype=np.int32)
-        tnodes = np.zeros(self.nb, dtype=np.int32)
-        d_tok = d_par = torch.zeros(1, dtype=torch.int32, device=dev)
-        host_trees = [b for b in range(self.nb)
+            self._flags = flags
+        # tree blocks read their nodes from the tree kernel's rows of the last
+        # step; host-built trees (the page block's) follow them
+        toff = np.zeros(nb, dtype=np.int32)
+        tnodes = np.zeros(nb, dtype=np.int32)
+        d_tok = d_par = self._zero_i32
+        host_trees = [b for b in range(nb)
                       if self.modes[b] == N.HSD_MODE_TREE and self.host_tree[b] is not None]
         if self.trees is not None or host_trees:
-            # this step's tree blocks read their nodes straight from the tree
-            # kernel's rows; host-built trees (the page block's) follow them
             base = 0
             toks, pars = [], []
             if self.trees is not None:
                 toks.append(self.trees.tokens.reshape(-1))
                 pars.append(self.trees.parents.reshape(-1))
                 base = int(self.trees.tokens.numel())
-                for b in range(self.nb):
+                for b in range(nb):
                     if self.modes[b] == N.HSD_MODE_TREE and self.host_tree[b] is None:
                         toff[b] = self.tree_slot[b] * self.trees.cap
                         tnodes[b] = self.valid[b]
@@ -332,12 +339,17 @@ class VerifyLoop:
                 toks.append(torch.tensor(t, dtype=torch.int32, device=dev))
                 pars.append(torch.tensor(par, dtype=torch.int32, device=dev))
                 base += len(t)
-            self.blocks[:, F["tree_off"]] = torch.from_numpy(toff).to(dev)
-            self.blocks[:, F["tree_nodes"]] = torch.from_numpy(tnodes).to(dev)
             d_tok, d_par = torch.cat(toks), torch.cat(pars)
+        # this step's block fields and pad columns: one upload each
+        cols = np.stack([np.asarray(self.modes), self.q_start, self.q_len,
+                         np.asarray(self.valid), self._flags, toff, tnodes], 1).astype(np.int32)
+        self.blocks[:, self._upd_cols] = torch.from_numpy(cols).to(dev, non_blocking=True)
+        pad_cols = np.zeros(self.stride * 64, dtype=bool)
+        pad_cols[kv - q:kv] = self.input_ids == self.pad
+        pad_dev = torch.from_numpy(pack_bits(pad_cols).view(np.int64)).to(dev, non_blocking=True)
         self.filter.zero_()
         self.out_bits.zero_()
-        cfg = make_config(self.nb, kv, q, self.stride, self.eos, self.mws0, self.mws_ub,
+        cfg = make_config(nb, kv, q, self.stride, self.eos, self.mws0, self.mws_ub,
                           self.max_spec_len, self.sentinel)
         ids, _, _ = self.inputs()
         accept_kmp(cfg, self.blocks, next_ids.to(torch.int32), ids, self.gen_pool,
@@ -350,48 +362,112 @@ class VerifyLoop:
                    spec_topk=self.spec_topk, spec_margin=self.spec_margin,
                    rank=None if rank is None else rank.to(torch.int32).contiguous(),
                    second=None if second is None else second.to(torch.float32).contiguous())
-        res = self.results.cpu().numpy()
-        self._check()
+        # pad columns of this step's input join the filter after the blocks'
+        # own updates, as the reference ORs them in after its block loop (D:1596-1599)
+        self.filter |= pad_dev
 
-        # continuation trees of the blocks without exactly one match, one launch
-        want = [b for b in range(self.nb)
-                if self.tree_decode and self.modes[b] != N.HSD_MODE_FINISHED
-                and not res[b][R["finished"]] and res[b][R["match_count"]] != 1
-                and not (self.page_block and b == self.nb - 1)]
-        new_trees, new_slot, host_trees = None, [-1] * self.nb, {}
-        if want:
-            idx = torch.tensor(want, dtype=torch.long, device=dev)
+        # device work that needs no host decision: the continuation trees of
+        # every live region block (the host keeps those of blocks without
+        # exactly one match), the keep indices over every block's row (a
+        # finished block's row is empty, or all filtered when it finished in
+        # this step, so the active rows give the same keep, D:1679-1687) and
+        # the new tokens of every block
+        cand = [b for b in range(nb) if self.tree_decode and self.modes[b] != N.HSD_MODE_FINISHED
+                and not (self.page_block and b == nb - 1)]
+        new_trees = None
+        if cand:
+            idx = torch.tensor(cand, dtype=torch.long, device=dev)
             new_trees = continuation_trees(
                 self.draft_pool, self.d_draft_off[idx].contiguous(),
                 self.d_draft_len[idx].contiguous(),
                 self.results[idx, R["next_token"]].contiguous(), self.tree_depth,
                 self.tree_cap, status=self.status)
-            for i, (b, tree) in enumerate(zip(want, new_trees.host())):
-                host_trees[b] = tree
-                new_slot[b] = i
-            self._check()
+        keep_bits, keep_idx, counts = keep_indices(self.out_bits, self.filter, kv,
+                                                   out=self._keep_out)
+        live = [b for b in range(nb) if self.modes[b] != N.HSD_MODE_FINISHED]
+        gidx = np.concatenate([b * self.gen_cap + len(self.gen_host[b])
+                               + np.arange(int(self.q_len[b])) for b in live]
+                              or [np.zeros(0, dtype=np.int64)]).astype(np.int64)
+        gidx = np.minimum(gidx, self.gen_pool.numel() - 1)
+        parts = [self.results.reshape(-1), self.status, counts, self.blocks.reshape(-1)]
+        if gidx.size:
+            parts.append(self.gen_pool[torch.from_numpy(gidx).to(dev, non_blocking=True)])
+        if new_trees is not None:
+            parts += [new_trees.counts, new_trees.tokens.reshape(-1),
+                      new_trees.depths.reshape(-1), new_trees.parents.reshape(-1)]
+        # ---- the step's one device -> host copy
+        packed = torch.cat(parts)
+        if self._pinned is None or self._pinned.numel() < packed.numel():
+            self._pinned = torch.empty(max(packed.numel(), 4096) * 2, dtype=torch.int32,
+                                       pin_memory=True)
+        host = self._pinned[:packed.numel()]
+        host.copy_(packed, non_blocking=True)
+        self._copied.record()
+        self._copied.synchronize()
+        h = host.numpy()
+        o = 0
+        res = h[o:o + nb * len(R)].reshape(nb, len(R)).copy()
+        o += nb * len(R)
+        code = int(h[o])
+        o += 1
+        n_keep = int(h[o])
+        o += 2
+        blk = h[o:o + nb * 16].reshape(nb, 16).copy()
+        o += nb * 16
+        newtok = h[o:o + gidx.size]
+        o += gidx.size
+        if code:
+            raise N.HSDError(f"device status 0x{code:x} in the verification loop")
+        host_tree_lists = {}
+        if new_trees is not None:
+            cap, nt = new_trees.cap, len(cand)
+            tcnt = h[o:o + nt]
+            o += nt
+            arr = [h[o + k * nt * cap:o + (k + 1) * nt * cap].reshape(nt, cap) for k in range(3)]
+            for i, b in enumerate(cand):
+                c = int(tcnt[i])
+                host_tree_lists[b] = (arr[0][i, :c].tolist(), arr[1][i, :c].tolist(),
+                                      arr[2][i, :c].tolist())
+        # generated tokens on the host (EOS dropped, D:1303; the draft after
+        # a repetition stop, D:1317)
+        j = 0
+        for b in live:
+            n = int(self.q_len[b])
+            r = res[b]
+            inc = int(r[R["increment"]])
+            if r[R["finished"]] == 2:
+                self.gen_host[b] = list(self.drafts[b])
+            else:
+                self.gen_host[b] += newtok[j:j + inc].tolist()
+                if r[R["finished"]] == 1:
+                    self.gen_host[b].pop()
+            j += n
+        self._blk = blk
+
+        want = [b for b in cand if not res[b][R["finished"]] and res[b][R["match_count"]] != 1]
+        new_slot = [-1] * nb
+        for b in want:
+            new_slot[b] = cand.index(b)
 
         # the page block's next input, from the host (D:1337-1567)
         self.step_finished = [self.modes[b] == N.HSD_MODE_FINISHED or bool(res[b][R["finished"]])
-                              for b in range(self.nb)]
+                              for b in range(nb)]
         page_in = None
-        last = self.nb - 1
+        last = nb - 1
         if (self.page_block and page_next is not None
                 and self.modes[last] != N.HSD_MODE_FINISHED and not res[last][R["finished"]]):
-            blk = self.blocks[last].cpu().numpy()
-            off, n = int(blk[F["gen_off"]]), int(blk[F["gen_len"]])
-            gen = self.gen_pool[off:off + n].cpu().tolist()
             r = res[last]
-            page_in = page_next(self, gen, int(r[R["increment"]]), int(blk[F["mws"]]),
+            page_in = page_next(self, list(self.gen_host[last]), int(r[R["increment"]]),
+                                int(blk[last][F["mws"]]),
                                 int(self.position_ids[int(r[R["pointer"]])]) + 1,
                                 int(r[R["next_token"]]))
             self.blocks[last, F["matches_len"]] = int(page_in.matches)
         # next inputs (D:1421-1565) from the result rows
-        new_ids, new_pos, new_lens = [], [], [0] * self.nb
-        new_modes, new_valid, new_kinds = list(self.modes), [0] * self.nb, list(self.kinds)
-        new_parents = [None] * self.nb
-        new_host_tree = [None] * self.nb
-        for b in range(self.nb):
+        new_ids, new_pos, new_lens = [], [], [0] * nb
+        new_modes, new_valid, new_kinds = list(self.modes), [0] * nb, list(self.kinds)
+        new_parents = [None] * nb
+        new_host_tree = [None] * nb
+        for b in range(nb):
             if self.modes[b] == N.HSD_MODE_FINISHED:
                 new_kinds[b] = SEG_NONE   # no rows any more
                 continue
@@ -401,7 +477,7 @@ class VerifyLoop:
                 new_modes[b], new_kinds[b] = N.HSD_MODE_FINISHED, SEG_NONE
                 continue
             base = int(self.position_ids[int(r[R["pointer"]])]) + 1
-            if page_in is not None and b == self.nb - 1:
+            if page_in is not None and b == nb - 1:
                 toks, pos = list(page_in.ids), list(page_in.pos)
                 if page_in.kind == "spec":
                     new_modes[b], new_kinds[b] = N.HSD_MODE_SPEC, SEG_CAUSAL
@@ -420,7 +496,7 @@ class VerifyLoop:
                 new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_SPEC, SEG_CAUSAL, n
                 pos = list(range(base, base + len(toks)))
             else:
-                tree = host_trees.get(b)
+                tree = host_tree_lists.get(b) if b in want else None
                 if tree is not None and len(tree[0]) > 1:    # D:1488-1543
                     tokens, depths, new_parents[b] = tree
                     n = len(tokens)
@@ -438,7 +514,7 @@ class VerifyLoop:
             new_lens[b] = len(toks)
         if self.page_block and self.variant == "hunyuan":
             # the HunYuan loop counts the page block's own tokens (H:2133)
-            produced = int(self.blocks[self.nb - 1, F["gen_len"]].item())
+            produced = len(self.gen_host[nb - 1])
         else:
             produced = self.new_tokens
         if produced >= self.max_new_tokens or all(
@@ -448,18 +524,9 @@ class VerifyLoop:
             self.done = True
             return False
 
-        # pad columns of this step's input are filtered (D:1596-1599)
-        pad_cols = np.zeros(self.stride * 64, dtype=bool)
-        pad_cols[kv - q:kv] = self.input_ids == self.pad
-        self.filter |= torch.from_numpy(pack_bits(pad_cols).view(np.int64)).to(dev)
-
-        # keep = OR(rows of the active blocks) & ~filter (D:1679-1687)
+        # the compaction rule (D:1693-1700, H:2253-2259) on the kept count
         t_c = time.perf_counter()
         self.compaction_calls += 1
-        active = [b for b in range(self.nb) if new_modes[b] != N.HSD_MODE_FINISHED]
-        live = self.out_bits[torch.tensor(active, dtype=torch.long, device=dev)]
-        keep_bits, keep_idx, counts = keep_indices(live, self.filter, kv)
-        n_keep = int(counts[0].item())
         dead = kv - n_keep
         if self.variant == "hunyuan":   # period 0 compacts too (H:2253-2259)
             rule = (self.period <= 1 or self.decode_times % self.period == 0
@@ -490,10 +557,10 @@ class VerifyLoop:
 
         # the next packed input and its KV columns; tight packing pads the
         # input to a multiple of 128 rows at position 0 that belong to no
-        # block (D:1619-1632): they see no column (the reference's dots loop
-        # lets them inherit the last block's row, D:1640-1644, HunYuan masks
-        # them, H:2290-2293); no block reads their outputs and the pad filter
-        # drops their columns, so tokens and compaction are the same
+        # block (D:1619-1632): with ``pad_rows_inherit`` they see the last
+        # block's row (the dots loop, D:1640-1644), otherwise nothing (the
+        # HunYuan loop, H:2290-2293); no block reads their outputs and the
+        # pad filter drops their columns, so tokens and compaction are the same
         if self.tight and sum(new_lens) % Q_BLOCK:
             pad_n = Q_BLOCK - sum(new_lens) % Q_BLOCK
             new_ids.append([self.pad] * pad_n)
@@ -504,7 +571,8 @@ class VerifyLoop:
         self.q_len = np.asarray(new_lens, dtype=np.int64)
         self.q_start = ends - self.q_len
         self.modes, self.valid, self.kinds = new_modes, new_valid, new_kinds
-        self.trees, self.tree_slot, self.tree_parents = new_trees, new_slot, new_parents
+        self.trees = new_trees if want else None
+        self.tree_slot, self.tree_parents = new_slot, new_parents
         self.host_tree = new_host_tree
         self.kv_len = kv + int(self.input_ids.size)
         if self.kv_len > self.kv_cap:
@@ -515,11 +583,9 @@ class VerifyLoop:
         return True
 
     def generated(self):
-        """Generated tokens of every block (EOS dropped, D:1303)."""
-        lens = self.blocks[:, F["gen_len"]].cpu().numpy()
-        pool = self.gen_pool.cpu().numpy()
-        return [pool[b * self.gen_cap: b * self.gen_cap + int(lens[b])].tolist()
-                for b in range(self.nb)]
+        """Generated tokens of every block (EOS dropped, D:1303), kept on the
+        host from each step's copy of the blocks' new tokens."""
+        return [list(g) for g in self.gen_host]
 
     def _check(self):
         code = int(self.status.item())

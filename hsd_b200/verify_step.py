@@ -124,6 +124,7 @@ class VerifyStep:
         self.new_planes = torch.tensor(src, dtype=torch.int64, device=dev)
         self.row_bytes = d * 2
         self.period = period
+        self.copy_layers = 4   # layers per host -> device copy in run_from_host
         self._host = None
         self._side = None  # second stream for the step's independent launches
         self.attn_launches_per_step = L
@@ -323,10 +324,14 @@ class VerifyStep:
         else:
             xs.wait_stream(cs)
         with torch.cuda.stream(xs):
-            for l in range(self.L):
-                q[l].copy_(h["q"][l], non_blocking=True)
-                nkv[l].copy_(h["new_kv"][l], non_blocking=True)
-                self._ready[buffers][l].record(xs)
+            # a few layers per copy: large enough for the link's full rate,
+            # small enough that the first layers' kernels start early
+            for l0 in range(0, self.L, self.copy_layers):
+                l1 = min(self.L, l0 + self.copy_layers)
+                q[l0:l1].copy_(h["q"][l0:l1], non_blocking=True)
+                nkv[l0:l1].copy_(h["new_kv"][l0:l1], non_blocking=True)
+                for l in range(l0, l1):
+                    self._ready[buffers][l].record(xs)
         with torch.cuda.stream(cs):
             self.input_ids.copy_(h["input_ids"], non_blocking=True)
             self.next_ids.copy_(h["next_ids"], non_blocking=True)
