@@ -36,6 +36,13 @@ and ``self.model.config`` whose ``_attn_implementation`` is switched to
 ``flex_attention`` (D:948-949).  The page block's candidate trees use
 ``pre_tokenizer=`` (keyword) or else ``tokenizer``; the reference loads the
 same tokenizer again from the model files for them (D:625-645).
+
+``fused_lm_head=True`` (keyword): after the prefill, each step runs the
+decoder alone (``self.model``, which must return ``last_hidden_state`` and
+``past_key_values``) and takes the next tokens from
+:func:`hsd_b200.lm_head.lm_head_argmax` over ``self.lm_head.weight``, so the
+``[Q, vocab]`` logits of D:1060 are never written; the logits the ratio
+rules read come from :func:`hsd_b200.lm_head.probe_logits`.
 """
 from __future__ import annotations
 
@@ -47,6 +54,7 @@ import torch
 
 from .attention import register_transformers_attention, step_attention_mask
 from .compaction import compact_kv
+from .lm_head import lm_head_argmax, probe_logits
 from .loop import VerifyLoop
 from .page_block import PageBlock, halfwidth_clean
 
@@ -165,6 +173,7 @@ def _run(self, input_ids, pixel_values, image_grid_thw, attention_mask, position
         "max_new_tokens must be provided for speculative generation."
     eos = list(eos_token_id) if isinstance(eos_token_id, (list, tuple)) else [int(eos_token_id)]
     pre_tokenizer = kwargs.get("pre_tokenizer", None)
+    fused = bool(kwargs.get("fused_lm_head", False))
     # the raw block content is tokenized so that tokens match the model's output (D:958-964)
     draft_raw = [item.get("raw_block_content", item["block_content"]) for item in draft]
     norm_draft = [halfwidth_clean(item["block_content"]) for item in draft]
@@ -227,11 +236,23 @@ def _run(self, input_ids, pixel_values, image_grid_thw, attention_mask, position
     while True:
         decode_times += 1
         t0 = time.time()
+        hidden = None
         with step_attention_mask(None if isinstance(mask, torch.Tensor) else mask):
-            outputs = self.forward(**model_inputs)
+            if fused and decode_times > 1:
+                # the decoder alone: the lm_head GEMM and argmax are one kernel below
+                dec = self.model(**model_inputs)
+                hidden = dec.last_hidden_state[0]
+                outputs = dec
+            else:
+                outputs = self.forward(**model_inputs)
         cache["kv"] = outputs.past_key_values
-        logits = outputs.logits[0]
-        next_ids = logits.argmax(dim=-1)
+        if hidden is not None:
+            weight = self.lm_head.weight
+            max_l = torch.empty(hidden.shape[0], dtype=torch.float32, device=dev)
+            next_ids = lm_head_argmax(hidden, weight, max_logit=max_l)
+        else:
+            logits = outputs.logits[0]
+            next_ids = logits.argmax(dim=-1)
         torch.cuda.synchronize(dev)
         t1 = time.time()
         t_fwd += t1 - t0
@@ -240,10 +261,14 @@ def _run(self, input_ids, pixel_values, image_grid_thw, attention_mask, position
         extra = {}
         if loop.ratio:
             rows, toks = loop.logit_probes()
-            probe = logits[rows.long(), toks.clamp(min=0).long()].float()
-            probe = torch.where(toks >= 0, probe, torch.zeros_like(probe))
-            extra = dict(max_logit=logits.gather(1, next_ids[:, None])[:, 0].float(),
-                         probe_logit=probe)
+            if hidden is not None:
+                probe = probe_logits(hidden, weight, rows, toks)
+                extra = dict(max_logit=max_l, probe_logit=probe)
+            else:
+                probe = logits[rows.long(), toks.clamp(min=0).long()].float()
+                probe = torch.where(toks >= 0, probe, torch.zeros_like(probe))
+                extra = dict(max_logit=logits.gather(1, next_ids[:, None])[:, 0].float(),
+                             probe_logit=probe)
         more = loop.step(next_ids, text_mode=[page.parser.text_mode] * nb,
                          page_next=page_next, **extra)
         if not more:

@@ -90,3 +90,45 @@ def test_hunyuan_drop_in_matches_oracle_loop(case, monkeypatch):
     assert used["kv_compact_calls"] == sum(1 for s in trace if s["action"] != "stop")
     assert used["kv_compact_skipped"] == sum(1 for s in trace if s["action"] == "none")
     assert len(out["compute_intensity"]) == len(trace)
+
+
+def _tiny_qwen2(dev):
+    from transformers.models.qwen2.modeling_qwen2 import Qwen2Config, Qwen2ForCausalLM
+    torch.manual_seed(0)
+    cfg = Qwen2Config(vocab_size=SI.VOCAB, hidden_size=256, intermediate_size=512,
+                      num_hidden_layers=2, num_attention_heads=2, num_key_value_heads=1,
+                      head_dim=128, rope_theta=1e6, max_position_embeddings=8192,
+                      initializer_range=0.5, tie_word_embeddings=False)
+    return Qwen2ForCausalLM(cfg).to(dev, torch.bfloat16).eval()
+
+
+@pytest.mark.parametrize("tree", [False, True])
+def test_drop_in_on_a_transformers_qwen2(tree, monkeypatch):
+    """The drop-in driving a real transformers decoder (a small random
+    Qwen2ForCausalLM, head_dim 128, bf16): its attention layers run through
+    the registered "hsd_b200" attention on the caller's dense prefill mask
+    and then on each step's PackedMask, its DynamicCache is compacted in
+    place, and the config's attention implementation is restored.  With
+    ``fused_lm_head`` the decoder runs alone and the fused lm_head + argmax
+    picks the tokens: the same run, token for token, as the logits path."""
+    from hsd_b200.generate import batch_generate
+    dev = torch.device("cuda:0")
+    monkeypatch.setenv("HSD_TIGHT_PACK", "1")
+    monkeypatch.setenv("HSD_COMPACT_PERIOD", "1")
+    case = CASES[1]
+    tok = SI.CharTokenizer()
+    prompts = [tok.encode(t) for t in case["prompts"]]
+    drafts = [{"block_content": d, "raw_block_content": d} for d in case["drafts"]]
+    model = _tiny_qwen2(dev)
+    impl = model.config._attn_implementation
+    runs = []
+    for fused in (False, True):
+        ids, mask, pos, pointer = SI.packed_prefill(prompts, device=dev)
+        gen, decode_times, stats = batch_generate(
+            model, input_ids=ids, attention_mask=mask, position_ids=pos, pointer=pointer,
+            tokenizer=tok, draft=drafts, enable_tree_decode=tree, eos_token_id=[SI.EOS],
+            max_new_tokens=160, fused_lm_head=fused)
+        runs.append((gen, decode_times, stats[6], stats[7]))
+        assert model.config._attn_implementation == impl
+        assert decode_times > 3 and stats[6] == decode_times - 1
+    assert runs[0] == runs[1]
