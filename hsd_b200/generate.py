@@ -208,7 +208,8 @@ def _run(self, input_ids, pixel_values, image_grid_thw, attention_mask, position
                       max_tree_depth=max_tree_depth, max_tree_len=max_tree_len,
                       spec_thresh=spec_thresh, tree_thresh=tree_thresh,
                       packed=(ids_host, pos_host, ptr_host, None), page_block=True,
-                      pad_rows_inherit=True, compact_hook=hook, device=dev)
+                      pad_rows_inherit=True, compact_hook=hook, track_kv_tokens=False,
+                      device=dev)
     loop.seg_bits[:] = 0
     vis = _inherited_rows(attention_mask, pointer, min(loop.stride, (ids_host.size + 63) // 64))
     loop.seg_bits[:, :vis.shape[1]] = vis
@@ -381,7 +382,8 @@ def _run_hunyuan(self, input_ids, attention_mask, position_ids, pixel_values, im
                       repeat_sentinel=41153, spec_thresh=spec_thresh, tree_thresh=1.0,
                       variant="hunyuan", spec_mode=spec_mode, spec_topk=spec_topk,
                       spec_margin=spec_margin, packed=(ids_host, pos_host, ptr_host, None),
-                      page_block=True, pad_rows_inherit=False, compact_hook=hook, device=dev)
+                      page_block=True, pad_rows_inherit=False, compact_hook=hook, track_kv_tokens=False,
+                      device=dev)
     loop.seg_bits[:] = 0
     vis = _inherited_rows(attention_mask, pointer, min(loop.stride, (ids_host.size + 63) // 64))
     loop.seg_bits[:, :vis.shape[1]] = vis

@@ -58,7 +58,8 @@ class VerifyLoop:
     ``prompts[b]`` is block b's prefill input (its own prompt: blocks do not
     share KV columns, as in the reference's stage-1 packing, RD:232-245) and
     ``drafts[b]`` its tokenized draft.  ``kv_tokens`` (device int32, one
-    token per KV column) is kept compacted alongside the mask; pass
+    token per KV column; ``track_kv_tokens=False`` skips it) is kept
+    compacted alongside the mask; pass
     ``kv_planes`` (device int64 plane addresses, see
     :func:`hsd_b200.compaction.plane_pointers`) and ``row_bytes`` to have
     model caches compacted in place too.
@@ -72,7 +73,7 @@ class VerifyLoop:
                  kv_capacity=None, spec_thresh=1.0, tree_thresh=1.0, variant="dots",
                  formula_tokens=(3, 1099), spec_mode="fmst", spec_topk=3, spec_margin=2.0,
                  packed=None, page_block=False, pad_rows_inherit=False, compact_hook=None,
-                 device="cuda"):
+                 track_kv_tokens=True, device="cuda"):
         if packed is not None:
             # the caller's packed prefill: (input_ids, position_ids, pointer)
             p_ids, p_pos, p_ptr = packed[:3]
@@ -178,7 +179,8 @@ class VerifyLoop:
         self.filter = torch.zeros(self.stride, dtype=torch.int64, device=dev)
         self.results = torch.zeros((self.nb, len(R)), dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.kv_tokens = torch.from_numpy(self.input_ids.astype(np.int32)).to(dev)
+        self.kv_tokens = (torch.from_numpy(self.input_ids.astype(np.int32)).to(dev)
+                          if track_kv_tokens else None)
         self.gen_host = [[] for _ in range(self.nb)]
         self._flags = blocks[:, F["flags"]].copy()
         self._upd_cols = torch.tensor([F["mode"], F["q_start"], F["q_len"], F["valid_count"],
@@ -449,9 +451,59 @@ class VerifyLoop:
         for b in want:
             new_slot[b] = cand.index(b)
 
-        # the page block's next input, from the host (D:1337-1567)
+        # stop rule and compaction first: they need only the copied results,
+        # so the compaction runs on the device while the host does the page
+        # block's parser and matching and packs the next input below
         self.step_finished = [self.modes[b] == N.HSD_MODE_FINISHED or bool(res[b][R["finished"]])
                               for b in range(nb)]
+        for b in live:
+            self.new_tokens += int(res[b][R["increment"]])
+        if self.page_block and self.variant == "hunyuan":
+            # the HunYuan loop counts the page block's own tokens (H:2133)
+            produced = len(self.gen_host[nb - 1])
+        else:
+            produced = self.new_tokens
+        if produced >= self.max_new_tokens or all(self.step_finished) or (
+                self.page_block and self.step_finished[-1]):                  # D:1589-1592
+            self.modes = [N.HSD_MODE_FINISHED if f else m
+                          for f, m in zip(self.step_finished, self.modes)]
+            self.done = True
+            return False
+
+        # the compaction rule (D:1693-1700, H:2253-2259) on the kept count
+        t_c = time.perf_counter()
+        self.compaction_calls += 1
+        dead = kv - n_keep
+        if self.variant == "hunyuan":   # period 0 compacts too (H:2253-2259)
+            rule = (self.period <= 1 or self.decode_times % self.period == 0
+                    or dead > kv * 0.2)
+        else:                           # D:1693-1700
+            rule = self.period > 0 and (self.period <= 1 or self.decode_times % self.period == 0
+                                        or dead > kv * 0.2)
+        nw = (kv + 63) // 64
+        if rule and n_keep < kv:                      # compact (D:1704-1723)
+            if self.kv_planes is not None:
+                compact_kv(self.kv_planes, self.row_bytes, keep_idx, counts=counts,
+                           status=self.status)
+            if self.compact_hook is not None:
+                self.compact_hook(keep_idx, counts, n_keep)
+            if self.kv_tokens is not None:
+                self.kv_tokens = self.kv_tokens[keep_idx[:n_keep].long()]
+            self.seg_bits = compact_bits(self.out_bits, keep_idx, counts, self.stride)
+            kv = n_keep
+        elif not rule:                                # dead columns masked (D:1724-1729)
+            self.seg_bits = self.out_bits.clone()
+            self.seg_bits[:, :nw] &= keep_bits[None, :nw]
+            if self.variant != "hunyuan":             # dots counts masked steps (D:1730)
+                self.compactions_skipped += 1
+        else:
+            self.seg_bits = self.out_bits.clone()
+            if self.variant == "hunyuan":             # HunYuan: nothing to drop (H:2275)
+                self.compactions_skipped += 1
+        self.compaction_s += time.perf_counter() - t_c
+
+
+        # the page block's next input, from the host (D:1337-1567)
         page_in = None
         last = nb - 1
         if (self.page_block and page_next is not None
@@ -472,7 +524,6 @@ class VerifyLoop:
                 new_kinds[b] = SEG_NONE   # no rows any more
                 continue
             r = res[b]
-            self.new_tokens += int(r[R["increment"]])
             if r[R["finished"]]:
                 new_modes[b], new_kinds[b] = N.HSD_MODE_FINISHED, SEG_NONE
                 continue
@@ -512,49 +563,6 @@ class VerifyLoop:
             new_ids.append(toks)
             new_pos.append(pos)
             new_lens[b] = len(toks)
-        if self.page_block and self.variant == "hunyuan":
-            # the HunYuan loop counts the page block's own tokens (H:2133)
-            produced = len(self.gen_host[nb - 1])
-        else:
-            produced = self.new_tokens
-        if produced >= self.max_new_tokens or all(
-                m == N.HSD_MODE_FINISHED for m in new_modes) or (
-                self.page_block and new_modes[-1] == N.HSD_MODE_FINISHED):   # D:1589-1592
-            self.modes = new_modes
-            self.done = True
-            return False
-
-        # the compaction rule (D:1693-1700, H:2253-2259) on the kept count
-        t_c = time.perf_counter()
-        self.compaction_calls += 1
-        dead = kv - n_keep
-        if self.variant == "hunyuan":   # period 0 compacts too (H:2253-2259)
-            rule = (self.period <= 1 or self.decode_times % self.period == 0
-                    or dead > kv * 0.2)
-        else:                           # D:1693-1700
-            rule = self.period > 0 and (self.period <= 1 or self.decode_times % self.period == 0
-                                        or dead > kv * 0.2)
-        nw = (kv + 63) // 64
-        if rule and n_keep < kv:                      # compact (D:1704-1723)
-            if self.kv_planes is not None:
-                compact_kv(self.kv_planes, self.row_bytes, keep_idx, counts=counts,
-                           status=self.status)
-            if self.compact_hook is not None:
-                self.compact_hook(keep_idx, counts, n_keep)
-            self.kv_tokens = self.kv_tokens[keep_idx[:n_keep].long()]
-            self.seg_bits = compact_bits(self.out_bits, keep_idx, counts, self.stride)
-            kv = n_keep
-        elif not rule:                                # dead columns masked (D:1724-1729)
-            self.seg_bits = self.out_bits.clone()
-            self.seg_bits[:, :nw] &= keep_bits[None, :nw]
-            if self.variant != "hunyuan":             # dots counts masked steps (D:1730)
-                self.compactions_skipped += 1
-        else:
-            self.seg_bits = self.out_bits.clone()
-            if self.variant == "hunyuan":             # HunYuan: nothing to drop (H:2275)
-                self.compactions_skipped += 1
-        self.compaction_s += time.perf_counter() - t_c
-
         # the next packed input and its KV columns; tight packing pads the
         # input to a multiple of 128 rows at position 0 that belong to no
         # block (D:1619-1632): with ``pad_rows_inherit`` they see the last
@@ -577,8 +585,9 @@ class VerifyLoop:
         self.kv_len = kv + int(self.input_ids.size)
         if self.kv_len > self.kv_cap:
             raise N.HSDError(f"KV columns {self.kv_len} exceed the loop's capacity {self.kv_cap}")
-        self.kv_tokens = torch.cat([self.kv_tokens,
-                                    torch.from_numpy(self.input_ids.astype(np.int32)).to(dev)])
+        if self.kv_tokens is not None:
+            self.kv_tokens = torch.cat([self.kv_tokens,
+                                        torch.from_numpy(self.input_ids.astype(np.int32)).to(dev)])
         self._mask = None
         return True
 
