@@ -185,6 +185,13 @@ def batch_generate_cases():
              tight_pack=True, max_spec_len=24, periodic=False),
         dict(name="tight_never_compact", seed=15, regions=3, tree=False, compact_period=0,
              tight_pack=True, max_spec_len=0, periodic=False),
+        # the logit-ratio rules below HSD_SPEC_THRESH / HSD_TREE_THRESH = 1
+        # (D:1147-1174, D:1228-1266), on graded bf16 logits
+        dict(name="ratio_spec", seed=16, regions=3, tree=False, compact_period=1,
+             tight_pack=True, max_spec_len=0, periodic=False, spec_thresh=0.75),
+        dict(name="ratio_spec_tree", seed=17, regions=3, tree=True, compact_period=2,
+             tight_pack=False, max_spec_len=0, periodic=False, spec_thresh=0.8,
+             tree_thresh=0.75),
     ]
     out = []
     for sp in specs:
@@ -209,7 +216,9 @@ def batch_generate_cases():
         out.append(dict(name=sp["name"], prompts=prompts, texts=texts, drafts=drafts,
                         tree=sp["tree"], compact_period=sp["compact_period"],
                         tight_pack=sp["tight_pack"], max_spec_len=sp["max_spec_len"],
-                        max_new_tokens=100000))
+                        spec_thresh=sp.get("spec_thresh", 1.0),
+                        tree_thresh=sp.get("tree_thresh", 1.0),
+                        max_new_tokens=100000 if "spec_thresh" not in sp else 600))
     return out
 
 

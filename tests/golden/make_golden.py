@@ -133,13 +133,25 @@ def run_reference_batch_generate(ref, case):
     ref.CACHED_BBOX_MODE_ONE_MATCHES_TREE = None
     prompts = [tok.encode(t) for t in case["prompts"]]
     texts = [tok.encode(t) for t in case["texts"]]
-    model = SI.StandInLM(prompts, texts)
+    graded = case["spec_thresh"] < 1.0 or case["tree_thresh"] < 1.0
+    model = SI.StandInLM(prompts, texts, graded=graded)
     ids, mask, pos, pointer = SI.packed_prefill(prompts)
     drafts = [{"block_content": d, "raw_block_content": d} for d in case["drafts"]]
-    gen, decode_times, stats = ref.DotsOCRForCausalLM.batch_generate(
-        model, input_ids=ids, attention_mask=mask, position_ids=pos, pointer=pointer,
-        tokenizer=tok, draft=drafts, enable_tree_decode=bool(case["tree"]),
-        eos_token_id=[SI.EOS], max_new_tokens=int(case["max_new_tokens"]))
+    # the reference reads the thresholds from the environment at call time (D:970-971)
+    saved = {k: os.environ.get(k) for k in ("HSD_SPEC_THRESH", "HSD_TREE_THRESH")}
+    os.environ["HSD_SPEC_THRESH"] = str(case["spec_thresh"])
+    os.environ["HSD_TREE_THRESH"] = str(case["tree_thresh"])
+    try:
+        gen, decode_times, stats = ref.DotsOCRForCausalLM.batch_generate(
+            model, input_ids=ids, attention_mask=mask, position_ids=pos, pointer=pointer,
+            tokenizer=tok, draft=drafts, enable_tree_decode=bool(case["tree"]),
+            eos_token_id=[SI.EOS], max_new_tokens=int(case["max_new_tokens"]))
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
     return dict(generated=[list(map(int, g)) for g in gen], decode_times=int(decode_times),
                 compact_calls=int(stats[6]), compact_skipped=int(stats[7]),
                 steps=[SI.step_digest(t) for t in model.trace],

@@ -109,12 +109,13 @@ class StandInLM:
     and ``texts[b]`` are block b's prompt and target text (token lists);
     ``trace`` records every forward's inputs."""
 
-    def __init__(self, prompts, texts, vocab=VOCAB, eos=EOS, head=6):
+    def __init__(self, prompts, texts, vocab=VOCAB, eos=EOS, head=6, graded=False):
         self.model = SimpleNamespace(config=SimpleNamespace(_attn_implementation="eager"))
         self.heads = {tuple(int(t) for t in p[:head]): b for b, p in enumerate(prompts)}
         self.prompts = [list(map(int, p)) for p in prompts]
         self.texts = [list(map(int, t)) for t in texts]
         self.vocab, self.eos, self.head = vocab, eos, head
+        self.graded = graded
         self.trace = []
 
     def predict(self, ctx):
@@ -151,9 +152,27 @@ class StandInLM:
             kept_column_ids=before[:, 1].astype(np.int64),
             mask_sha=hashlib.sha256(np.packbits(allowed, axis=-1).tobytes()
                                     + np.asarray(allowed.shape, np.int64).tobytes()).hexdigest()))
-        logits = torch.zeros((1, q, self.vocab), dtype=torch.float32)
-        logits[0, torch.arange(q), torch.from_numpy(pred)] = 1.0
+        if self.graded:
+            rows = np.stack([self.graded_row(toks[allowed[r]].tolist(), int(pred[r]))
+                             for r in range(q)]) if q else np.zeros((0, self.vocab), np.float32)
+            logits = torch.from_numpy(rows)[None].to(torch.bfloat16)
+        else:
+            logits = torch.zeros((1, q, self.vocab), dtype=torch.float32)
+            logits[0, torch.arange(q), torch.from_numpy(pred)] = 1.0
         return SimpleNamespace(logits=logits.to(dev), past_key_values=past_key_values)
+
+    def graded_row(self, ctx, pred):
+        """Logits of one row for the logit-ratio rules: 8 at the predicted
+        token, every other token k / 8 with k in [0, 56] hashed from the last
+        context tokens and the token (exact in bf16), so some draft tokens
+        pass a ratio threshold below 1 without being the argmax."""
+        h = 0
+        for t in ctx[-2:]:
+            h = (h * 1000003 + int(t) + 11) % 2147483647
+        k = (h * 2654435761 + np.arange(self.vocab, dtype=np.int64) * 40503) % 57
+        row = k.astype(np.float32) / 8.0
+        row[pred] = 8.0
+        return row
 
     __call__ = forward
 
@@ -209,3 +228,16 @@ def trace_digest(step):
                          + np.asarray(allowed.shape, np.int64).tobytes()).hexdigest()
     return step_digest(dict(input_ids=step["input_ids"], position_ids=step["position_ids"],
                             kept_column_ids=step["kept_column_ids"], mask_sha=sha))
+
+
+def oracle_logits_model(lm):
+    """Dense float32 logits ``[Q, V]`` of :meth:`StandInLM.graded_row` for
+    ``oracle.loop.reference_loop(logits_model=...)``."""
+    def fn(input_ids, position_ids, allowed, kv_tokens):
+        kv_tokens = np.asarray(kv_tokens, dtype=np.int64)
+        rows = []
+        for r in range(allowed.shape[0]):
+            ctx = kv_tokens[allowed[r]].tolist()
+            rows.append(lm.graded_row(ctx, lm.predict(ctx)))
+        return np.stack(rows).astype(np.float32)
+    return fn

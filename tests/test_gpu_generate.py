@@ -1,4 +1,6 @@
-"""The drop-in ``batch_generate`` against the reference's own runs.
+"""The drop-in ``batch_generate`` against the reference's own runs
+(including runs below the default logit-ratio thresholds, on graded bf16
+logits).
 
 ``hsd_b200.generate.batch_generate`` has the signature and return value of
 the reference's ``DotsOCRForCausalLM.batch_generate``
@@ -33,10 +35,13 @@ def test_drop_in_batch_generate_matches_reference_runs(case, monkeypatch):
     monkeypatch.setenv("HSD_TIGHT_PACK", "1" if case["tight_pack"] else "0")
     monkeypatch.setenv("HSD_COMPACT_PERIOD", str(case["compact_period"]))
     monkeypatch.setenv("HSD_MAX_SPEC_LEN", str(case["max_spec_len"]))
+    monkeypatch.setenv("HSD_SPEC_THRESH", str(case["spec_thresh"]))
+    monkeypatch.setenv("HSD_TREE_THRESH", str(case["tree_thresh"]))
     tok = SI.CharTokenizer()
     prompts = [tok.encode(t) for t in case["prompts"]]
     texts = [tok.encode(t) for t in case["texts"]]
-    model = SI.StandInLM(prompts, texts)
+    graded = case["spec_thresh"] < 1.0 or case["tree_thresh"] < 1.0
+    model = SI.StandInLM(prompts, texts, graded=graded)   # bf16 logits for the ratio rules
     ids, mask, pos, pointer = SI.packed_prefill(prompts, device=dev)
     drafts = [{"block_content": d, "raw_block_content": d} for d in case["drafts"]]
     gen, decode_times, stats = batch_generate(

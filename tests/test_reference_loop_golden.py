@@ -36,18 +36,32 @@ def _setup(case):
                         max_tree_depth=15, max_tree_len=256,
                         max_spec_len=int(case["max_spec_len"]),
                         tight_pack=bool(case["tight_pack"]),
-                        enable_tree_decode=bool(case["tree"]))
+                        enable_tree_decode=bool(case["tree"]),
+                        spec_thresh=float(case["spec_thresh"]),
+                        tree_thresh=float(case["tree_thresh"]))
     return tok, prompts, texts, drafts, cfg
+
+
+def _graded(case):
+    return case["spec_thresh"] < 1.0 or case["tree_thresh"] < 1.0
+
+
+def _models(case, prompts, texts):
+    """``(model, logits_model)`` arguments of the oracle loop for the case."""
+    lm = SI.StandInLM(prompts, texts, graded=_graded(case))
+    if _graded(case):
+        return None, SI.oracle_logits_model(lm)
+    return SI.oracle_model(lm), None
 
 
 def _oracle_run(case):
     tok, prompts, texts, drafts, cfg = _setup(case)
-    lm = SI.StandInLM(prompts, texts)
+    model, logits_model = _models(case, prompts, texts)
     page = OP.OraclePage(tok, [OP.to_halfwidth_clean(d) for d in case["drafts"]], cfg)
-    gen, trace = OL.reference_loop(prompts, drafts + [[]], SI.oracle_model(lm), cfg,
+    gen, trace = OL.reference_loop(prompts, drafts + [[]], model, cfg,
                                    int(case["max_new_tokens"]),
                                    compact_period=int(case["compact_period"]),
-                                   max_iters=5000, page=page)
+                                   max_iters=5000, logits_model=logits_model, page=page)
     return gen, trace
 
 
@@ -90,7 +104,7 @@ def test_package_page_block_matches_oracle_page_block(case):
     from hsd_b200.page_block import PageBlock, halfwidth_clean
 
     tok, prompts, texts, drafts, cfg = _setup(case)
-    lm = SI.StandInLM(prompts, texts)
+    model, logits_model = _models(case, prompts, texts)
     page = OP.OraclePage(tok, [OP.to_halfwidth_clean(d) for d in case["drafts"]], cfg)
     mine = PageBlock(tok, max_tree_depth=15, tree_cap=256, min_input_length=128,
                      tight_pack=cfg.tight_pack, max_spec_len=cfg.max_spec_len,
@@ -113,9 +127,9 @@ def test_package_page_block_matches_oracle_page_block(case):
         return want
 
     page.next_input = both
-    OL.reference_loop(prompts, drafts + [[]], SI.oracle_model(lm), cfg,
+    OL.reference_loop(prompts, drafts + [[]], model, cfg,
                       int(case["max_new_tokens"]), compact_period=int(case["compact_period"]),
-                      max_iters=5000, page=page)
+                      max_iters=5000, logits_model=logits_model, page=page)
     assert len(calls) == case["decode_times"] - 1
     if case["tree"]:
         assert "tree" in calls and "spec" in calls
