@@ -15,7 +15,9 @@
 //               j: K_{j+1}, V_j
 //   warps 9, 11 MMA issuers (one thread each), slot 0 and slot 1: tcgen05
 //               with both operands in smem, S = Q K^T and O += P V
-//   warp 10     idle (the third warpgroup is whole for setmaxnreg)
+//   warp 10     publisher: copies a partial record staged by the softmax in
+//               shared memory out to the workspace and raises its flags, so
+//               the softmax goes on to its next piece at once
 //   warps 0-3   softmax + epilogue of head slot 0 (thread = query row)
 //   warps 4-7   softmax + epilogue of head slot 1
 //
@@ -39,7 +41,10 @@
 // its normalised rows with one flag per (CTA, slot, warp).  The owner merges
 // them into its own O in the epilogue; no second kernel.  Flags hold the
 // launch generation + 1 (the generation lives in the workspace and the last
-// CTA to exit advances it), so they never need clearing.
+// CTA to exit advances it), so they never need clearing.  Each role walks its
+// pieces from the previous one (the next head pair or tile) after one binary
+// search for the first.  The MMA thread releases Q after the piece's last S,
+// so the next piece's Q loads under the last block's softmax and PV.
 #include <atomic>
 
 #include "common.cuh"
@@ -89,6 +94,8 @@ struct __align__(1024) Smem {
   uint64_t bar_final[NSLOT];
   uint64_t bar_ostage[NSLOT];  // the slot's O rows are staged in its P buffer
   uint64_t bar_ofree[NSLOT];   // their bulk stores have read the buffer
+  uint64_t bar_pub[NSLOT];       // a partial record is staged in the slot's P buffer
+  uint64_t bar_pub_free[NSLOT];  // warp 10 has read it
   uint32_t tmem_base;
   int abort;
 };
@@ -118,33 +125,56 @@ struct Params {
 // A piece: blocks [b0, b1) of one item (query tile x head pair).
 struct Piece {
   int qt, kvh, h0, nslot, b0, b1, nblk, item, start;
+  int lo = -1, hp = 0;  // ordered tile index and head pair of the piece (lo < 0: none yet)
 };
 
 // Next piece of the work range [w, w1) (advances w).  Items are the query
 // tiles in tile_order, each split into hkv x pairs head-pair items of
-// blk_count[tile] blocks; W = sum of all items' blocks.
+// blk_count[tile] blocks; W = sum of all items' blocks.  pc holds the
+// previous piece of the walk (pc.lo < 0 before the first), which ended at an
+// item boundary unless the range is exhausted.
 __device__ __forceinline__ bool next_piece(const Params& p, int& w, int w1, Piece& pc) {
   if (w >= w1) return false;
   const int per_tile = p.hkv * p.pairs;
-  int lo = 0, hi = p.n_qtiles - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (p.blk_prefix[mid] * per_tile <= w)
-      lo = mid;
-    else
-      hi = mid - 1;
+  int lo, hp, c, b0;
+  if (pc.lo >= 0) {
+    // the walk continues where the previous piece ended (an item boundary):
+    // the next head pair of the same tile, or the next non-empty tile
+    b0 = 0;
+    lo = pc.lo;
+    c = pc.nblk;
+    hp = pc.hp + 1;
+    if (hp == per_tile) {
+      hp = 0;
+      do {
+        ++lo;
+        c = p.blk_prefix[lo + 1] - p.blk_prefix[lo];
+      } while (c == 0);
+      pc.qt = p.tile_order[lo];
+    }
+  } else {
+    lo = 0;
+    int hi = p.n_qtiles - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (p.blk_prefix[mid] * per_tile <= w)
+        lo = mid;
+      else
+        hi = mid - 1;
+    }
+    pc.qt = p.tile_order[lo];
+    c = p.blk_count[pc.qt];
+    const int off = w - p.blk_prefix[lo] * per_tile;
+    hp = off / c;
+    b0 = off - hp * c;
   }
-  const int qt = p.tile_order[lo];
-  const int c = p.blk_count[qt];
-  const int tile_start = p.blk_prefix[lo] * per_tile;
-  const int off = w - tile_start;
-  const int hp = off / c;
-  pc.qt = qt;
+  pc.lo = lo;
+  pc.hp = hp;
   pc.nblk = c;
-  pc.b0 = off - hp * c;
-  pc.b1 = min(c, pc.b0 + (w1 - w));
+  pc.b0 = b0;
+  pc.b1 = min(c, b0 + (w1 - w));
   pc.item = lo * per_tile + hp;
-  pc.start = tile_start + hp * c;
+  pc.start = w - b0;
   pc.kvh = hp / p.pairs;
   const int pair = hp - pc.kvh * p.pairs;
   pc.h0 = pc.kvh * p.group + 2 * pair;
@@ -220,6 +250,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.bar_final[i], 1);
       mbar_init(&sm.bar_ostage[i], 128);
       mbar_init(&sm.bar_ofree[i], 1);
+      mbar_init(&sm.bar_pub[i], 4);
+      mbar_init(&sm.bar_pub_free[i], 1);
     }
     sm.abort = 0;
     fence_barrier_init();
@@ -367,6 +399,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             issue_s(t_sl, qa, kv0 + st * TILE_BYTES);
             umma_commit(&sm.bar_s_full[s]);
             ++ns;
+            // the piece's last S: Q is free once it completes, so the next
+            // piece's Q loads under this block's softmax and PV
+            if (j == pc.b1 - 1)
+              for (int k = 0; k < rel; ++k) umma_commit(&sm.bar_q_free);
           } else {
             ok = mbar_wait(&sm.bar_p_full[s], uint32_t(gs) & 1u, abort, p.status, 0x206 + s);
             if (!ok) break;
@@ -385,7 +421,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < rel; ++k) umma_commit(&sm.bar_empty[st]);
         }
         if (!ok) break;
-        for (int k = 0; k < rel; ++k) umma_commit(&sm.bar_q_free);  // every S issued
         ++ps;
         ++pieces;
       }
@@ -393,6 +428,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (issued_any) {
         umma_commit(&sm.bar_final[s]);
         mbar_wait(&sm.bar_final[s], 0, abort, p.status, 0x20a + s, false);
+      }
+    } else if (warp == 10) {
+      // ---------------------------------------------------------- publisher
+      // When the CTA's first piece continues an item begun by an earlier CTA,
+      // copy each slot's staged rows (16 chunks x 128 rows of 16 bytes) to its
+      // record, release the buffer, then raise the slot's four flags.
+      Piece pc;
+      int wq = w0;
+      if (p.split && next_piece(p, wq, w1, pc) && !(pc.b0 == 0 && pc.b1 == pc.nblk) &&
+          pc.start < w0) {
+        for (int s = 0; s < pc.nslot; ++s) {
+          const bool ok = mbar_wait(&sm.bar_pub[s], 0, abort, p.status, 0x140 + s);
+          uint32_t* rec = p.partials + (size_t(blockIdx.x) * NSLOT + s) * kRecWords;
+          if (ok) {
+            const int4* src = reinterpret_cast<const int4*>(sm.pb[s]);
+            int4* dst = reinterpret_cast<int4*>(rec);
+#pragma unroll 1
+            for (int k0 = 0; k0 < 2048; k0 += 256) {
+              int4 v[8];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) v[u] = src[k0 + 32 * u + lane];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) dst[k0 + 32 * u + lane] = v[u];
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.bar_pub_free[s]);  // also after an abort
+          if (ok) {
+            // the rows above, and the softmax's (m, l) stores ordered before
+            // bar_pub, are visible before any flag
+            __threadfence();
+            __syncwarp();
+            if (lane < 4)
+              st_release_u32(p.flags + (size_t(blockIdx.x) * NSLOT + s) * 4 + lane, gen + 1u);
+          }
+        }
       }
     }
   } else {
@@ -408,6 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int fo = 0;  // final outputs this slot has stored (barrier parity)
     int hs = 0;  // blocks with both slots active (exponential-phase handshakes)
     bool ok = true;
+    bool pub_wait = false;  // the P buffer holds a staged record warp 10 may not have read
     int w = w0;
     Piece pc;
     while (ok && next_piece(p, w, w1, pc)) {
@@ -520,6 +592,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     p.status, 0x314 + s));
           if (!ok) break;
         }
+        if (pub_wait) {  // P is overwritten below: warp 10 has copied the staged record
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(&sm.bar_pub_free[s], 0, abort, p.status, 0x316 + s));
+          pub_wait = false;
+          if (!ok) break;
+        }
         // P = exp2(s * scale - m) -> bf16 pairs -> row r of the slot's P tile
         // (two 64-column sub-tiles, 128-byte rows, 16-byte chunk c stored at
         // chunk c ^ (r & 7): the TMA / MMA 128-byte swizzle).  The scale,
@@ -588,22 +666,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool whole = pc.b0 == 0 && pc.b1 == pc.nblk;
       if (!whole && pc.start < w0) {
         // a later piece of an item begun by an earlier CTA (this CTA's first
-        // piece): publish O / l in bf16 with its (m, l) for the item's owner;
-        // one flag per warp covers the warp's 32 rows.
+        // piece): O / l in bf16, in the record's layout, goes to the slot's P
+        // buffer (free: the last PV has completed) and (m, l) straight to the
+        // record; warp 10 copies the rows out and raises the flags.
         uint32_t* rec = p.partials + (size_t(blockIdx.x) * NSLOT + s) * kRecWords;
         const float invl = (l > 0.f) ? 1.f / l : 0.f;
-        int4* rec4 = reinterpret_cast<int4*>(rec);
+        const uint32_t stg = smem_u32(sm.pb[s]) + uint32_t(r) * 16u;
 #pragma unroll
         for (int c = 0; c < 16; ++c)
-          rec4[c * 128 + r] = make_int4(int(pack_bf16x2(o[8 * c] * invl, o[8 * c + 1] * invl)),
-                                        int(pack_bf16x2(o[8 * c + 2] * invl, o[8 * c + 3] * invl)),
-                                        int(pack_bf16x2(o[8 * c + 4] * invl, o[8 * c + 5] * invl)),
-                                        int(pack_bf16x2(o[8 * c + 6] * invl, o[8 * c + 7] * invl)));
+          st_shared_v4(stg + uint32_t(c) * 2048u, pack_bf16x2(o[8 * c] * invl, o[8 * c + 1] * invl),
+                       pack_bf16x2(o[8 * c + 2] * invl, o[8 * c + 3] * invl),
+                       pack_bf16x2(o[8 * c + 4] * invl, o[8 * c + 5] * invl),
+                       pack_bf16x2(o[8 * c + 6] * invl, o[8 * c + 7] * invl));
         reinterpret_cast<float2*>(rec + 128 * 64)[r] = make_float2(m, l);
-        __threadfence();
         __syncwarp();
-        if (lane == 0)
-          st_release_u32(p.flags + (size_t(blockIdx.x) * NSLOT + s) * 4 + quarter, gen + 1u);
+        if (lane == 0) mbar_arrive(&sm.bar_pub[s]);
+        pub_wait = true;
         continue;
       }
       if (!whole) {
@@ -652,6 +730,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // past q_len are not written).  The buffer is free again for the next
       // piece's P once the stores have read it.
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
+      if (pub_wait) {  // the output is staged in the P buffer below
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&sm.bar_pub_free[s], 0, abort, p.status, 0x318 + s));
+        pub_wait = false;
+        if (!ok) break;
+      }
       {
         const uint32_t orow = smem_u32(sm.pb[s]) + uint32_t(r) * 128u;
 #pragma unroll
