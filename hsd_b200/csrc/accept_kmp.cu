@@ -12,7 +12,7 @@
 // starts at once, which yields the same set (and so the same count and first
 // start).  The continuation tries for tree mode come packed as input
 // (hsd_continuation_trees builds them on the device).
-#include <atomic>
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 
@@ -138,26 +138,53 @@ __device__ __forceinline__ bool is_eos(const hsd_accept_config_t& c, int tok) {
 
 // Number of starts s (ascending) with text[s, s+m) == pat and s + m <= n - 1,
 // and the first such s (-1 if none) -- the matches find_all_matches_kmp keeps
-// (D:592-598).
+// (D:592-598).  Lane i tests start base + i.  For m <= 32 the pattern sits in
+// the lanes and each round of 32 starts needs one new coalesced load of the
+// text (lane i holds text[base + i] and text[base + 32 + i]; text[s + k] is
+// a shuffle), the next round's load issued before this round's compares.
 __device__ void count_matches(const int32_t* text, int n, const int32_t* pat, int m, int lane,
                               int& count, int& first) {
   count = 0;
   first = -1;
   const int last_start = n - 1 - m;  // inclusive
+  if (last_start < 0) return;
+  if (m > 32) {
+    for (int base = 0; base <= last_start; base += 32) {
+      const int s = base + lane;
+      bool hit = false;
+      if (s <= last_start) {
+        hit = true;
+        for (int k = 0; k < m; ++k)
+          if (text[s + k] != pat[k]) {
+            hit = false;
+            break;
+          }
+      }
+      const uint32_t bal = __ballot_sync(0xffffffffu, hit);
+      if (bal && first < 0) first = base + __ffs(bal) - 1;
+      count += __popc(bal);
+    }
+    return;
+  }
+  const int pk = lane < m ? pat[lane] : 0;
+  int t0 = lane < n ? text[lane] : 0;
+  int t1 = 32 + lane < n ? text[32 + lane] : 0;
   for (int base = 0; base <= last_start; base += 32) {
     const int s = base + lane;
-    bool hit = false;
-    if (s <= last_start) {
-      hit = true;
-      for (int k = 0; k < m; ++k)
-        if (text[s + k] != pat[k]) {
-          hit = false;
-          break;
-        }
+    const int t2 = s + 64 < n ? text[s + 64] : 0;  // the next round's second half
+    bool hit = s <= last_start;
+    for (int k = 0; k < m; ++k) {  // every lane takes part in every shuffle
+      const int src = (lane + k) & 31;
+      const int a0 = __shfl_sync(0xffffffffu, t0, src);
+      const int a1 = __shfl_sync(0xffffffffu, t1, src);
+      const int pv = __shfl_sync(0xffffffffu, pk, k);
+      hit &= (lane + k < 32 ? a0 : a1) == pv;
     }
     const uint32_t bal = __ballot_sync(0xffffffffu, hit);
     if (bal && first < 0) first = base + __ffs(bal) - 1;
     count += __popc(bal);
+    t0 = t1;
+    t1 = t2;
   }
 }
 
@@ -165,9 +192,8 @@ __device__ void count_matches(const int32_t* text, int n, const int32_t* pat, in
 // block sets its rejected columns (D:1196-1200), a tree block sets its walked
 // path and then inverts its column range (D:1266-1286), a finished block ORs
 // in its pointer row's visibility (D:1299-1319).  Setting bits commutes with
-// setting bits, so the rejected columns and tree paths go straight into a
-// shared-memory copy of the filter (atomics on masked words: neighbours may
-// share a word).  Only the inversions and the finished rows depend on the
+// setting bits, so the rejected columns and tree paths go straight into the
+// filter words (atomics on masked words: neighbours may share a word).  Only the inversions and the finished rows depend on the
 // block order (a row may reach another block's columns); each block records
 // those two as a FilterRec and one thread per filter word replays them in
 // block order at the end.
@@ -176,30 +202,34 @@ struct FilterRec {
   int32_t finished;  // OR the block's visibility row
 };
 
-__host__ __device__ __forceinline__ size_t filter_rec_offset(int nwords) {
-  return (size_t(nwords) * sizeof(uint64_t) + 15) & ~size_t(15);
-}
-
 __device__ __forceinline__ void filter_or(unsigned long long* f, int lo, int hi, int lane) {
   if (lo > hi) return;
   for (int w = (lo >> 6) + lane; w <= (hi >> 6); w += 32) atomicOr(f + w, word_range(w, lo, hi));
 }
 
-// One CTA; warp w handles blocks w, w + nwarps, ... in parallel.  Dynamic
-// shared memory: the filter words, then one FilterRec per block.
+// One thread-block cluster; warp w of the cluster (CTA rank x warps per CTA
+// + warp) handles blocks w, w + cluster warps, ... in parallel.  The blocks'
+// commuting filter updates are atomic ORs on the filter words in global
+// memory; one FilterRec per block lives in the first CTA's dynamic shared
+// memory, which the others reach through distributed shared memory (plain
+// stores), and the first CTA replays the order-dependent updates.
 __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ uint8_t smem_raw[];
-  unsigned long long* filt = reinterpret_cast<unsigned long long*>(smem_raw);
+  const bool leader = cluster.block_rank() == 0;
+  uint8_t* lead = cluster.map_shared_rank(smem_raw, 0);
+  unsigned long long* filt = reinterpret_cast<unsigned long long*>(p.filter_bits);
   const int lane = lane_id();
   const int nwarps = blockDim.x >> 5;
+  const int cwarps = nwarps * int(cluster.num_blocks());
   const hsd_accept_config_t& cfg = p.cfg;
   const int stride = cfg.kv_words_stride;
   const int nwords = (cfg.kv_len + 63) / 64;
   const int kvb = cfg.kv_base;
-  FilterRec* recs = reinterpret_cast<FilterRec*>(smem_raw + filter_rec_offset(nwords));
-  for (int w = threadIdx.x; w < nwords; w += blockDim.x) filt[w] = p.filter_bits[w];
-  __syncthreads();
-  for (int b = warp_id(); b < cfg.n_blocks; b += nwarps) {
+  FilterRec* recs = reinterpret_cast<FilterRec*>(lead);
+  cluster.sync();  // every CTA of the cluster runs before any reaches the first one's memory
+  for (int b = int(cluster.block_rank()) * nwarps + warp_id(); b < cfg.n_blocks; b += cwarps) {
     if (lane == 0) recs[b] = FilterRec{1, 0, 0};
     hsd_block_t blk = p.blocks[b];
     hsd_block_result_t res;
@@ -413,15 +443,17 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
       p.blocks[b] = blk;
     }
   }
-  __syncthreads();
+  cluster.sync();
+  if (!leader) return;
   // Order-dependent updates, per word in block order (the visibility rows
-  // are complete: every warp passed the barrier after writing its own).
+  // are complete: every warp of the cluster passed the barrier after writing
+  // its own).
   for (int w = threadIdx.x; w < nwords; w += blockDim.x) {
-    uint64_t v = filt[w];
+    uint64_t v = __ldcg(p.filter_bits + w);
     for (int b = 0; b < cfg.n_blocks; ++b) {
       const FilterRec r = recs[b];
       if (r.lo <= r.hi && (r.lo >> 6) <= w && w <= (r.hi >> 6)) v ^= word_range(w, r.lo, r.hi);
-      if (r.finished) v |= p.out_kv_bits[size_t(b) * stride + w];
+      if (r.finished) v |= __ldcg(p.out_kv_bits + size_t(b) * stride + w);  // other SMs wrote it
     }
     p.filter_bits[w] = v;
   }
@@ -433,12 +465,6 @@ __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
 using namespace hsd;
 
 static constexpr int kMaxBlocks = 1024;
-static constexpr size_t kMaxSmem = 200 * 1024;  // filter words + FilterRecs
-static constexpr int kMaxDevices = 64;
-// Set once per device; host threads driving different devices or streams may
-// race to set it, which is harmless (the attribute call is idempotent) and
-// atomic here.
-static std::atomic<bool> g_attr_set[kMaxDevices];
 
 static int accept_launch(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
                          hsd_block_result_t* results, const int32_t* next_ids,
@@ -514,32 +540,27 @@ static int accept_launch(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
     hsd_host::set_error("hsd_accept_kmp: %d blocks > %d", cfg->n_blocks, kMaxBlocks);
     return HSD_ERR_TOO_LARGE;
   }
-  const int warps = cfg->n_blocks < 32 ? cfg->n_blocks : 32;
-  const size_t smem = acc::filter_rec_offset((cfg->kv_len + 63) / 64) +
-                      size_t(cfg->n_blocks) * sizeof(acc::FilterRec);
-  if (smem > kMaxSmem) {
-    hsd_host::set_error("hsd_accept_kmp: %d blocks over %d KV columns need %zu bytes of "
-                        "shared memory (at most %zu)",
-                        cfg->n_blocks, cfg->kv_len, smem, kMaxSmem);
-    return HSD_ERR_TOO_LARGE;
-  }
-  int dev = 0;
-  int rc = hsd_host::cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
-  if (rc) return rc;
-  if (dev < 0 || dev >= kMaxDevices) {
-    hsd_host::set_error("hsd_accept_kmp: device ordinal %d >= %d", dev, kMaxDevices);
-    return HSD_ERR_UNSUPPORTED;
-  }
-  if (!g_attr_set[dev].load(std::memory_order_acquire)) {
-    rc = hsd_host::cuda_check(
-        cudaFuncSetAttribute(acc::accept_kmp_kernel,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxSmem)),
-        "cudaFuncSetAttribute(accept_kmp_kernel)");
-    if (rc) return rc;
-    g_attr_set[dev].store(true, std::memory_order_release);
-  }
-  acc::accept_kmp_kernel<<<1, warps * 32, smem, reinterpret_cast<cudaStream_t>(stream)>>>(p);
-  return hsd_host::cuda_check(cudaGetLastError(), "accept_kmp_kernel launch");
+  // up to 32 blocks per CTA, up to 8 CTAs in the cluster (beyond 256 blocks
+  // the warps take several blocks each)
+  const int ctas = (cfg->n_blocks + 31) / 32 < 8 ? (cfg->n_blocks + 31) / 32 : 8;
+  const int per_cta = (cfg->n_blocks + ctas - 1) / ctas;
+  const int warps = per_cta < 32 ? per_cta : 32;
+  // one FilterRec per block (at most 12 KB: within the default limit)
+  const size_t smem = size_t(cfg->n_blocks) * sizeof(acc::FilterRec);
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(unsigned(ctas));
+  lc.blockDim = dim3(unsigned(warps * 32));
+  lc.dynamicSmemBytes = smem;
+  lc.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(ctas);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  return hsd_host::cuda_check(cudaLaunchKernelEx(&lc, acc::accept_kmp_kernel, p),
+                              "accept_kmp_kernel launch");
 }
 
 extern "C" int hsd_accept_kmp(const hsd_accept_config_t* cfg, hsd_block_t* blocks,

@@ -37,7 +37,7 @@ struct Params {
   int64_t q_row_stride, kv_row_stride, cs_row_stride;
   int64_t kc_head_stride, vc_head_stride, cache_row_stride;
   int n_rows, hq, hkv, dst_row0;
-  int64_t n_q, n_k, n_v;  // work units of each kind
+  int n_q, n_k, n_v;  // work units of each kind
 };
 
 __device__ __forceinline__ uint4 ld16(const void* p) {
@@ -86,6 +86,65 @@ __device__ __forceinline__ void rotate8(uint4 a, uint4 b, uint4 c1, uint4 c2, ui
   }
 }
 
+// One work unit's operands: kind 0 = query / key (a, b = the two halves'
+// 8 lanes, c1..s2 = cos / sin), kind 1 = value (a = 16 bytes), kind 2 = none.
+struct Unit {
+  uint4 a, b, c1, c2, s1, s2;
+  __nv_bfloat16* dst;
+  int kind;
+};
+
+__device__ __forceinline__ void load_unit(const Params& p, int u, Unit& w) {
+  const int nqk = p.n_q + p.n_k;
+  if (u >= p.n_q + p.n_k + p.n_v) {
+    w.kind = 2;
+  } else if (u < nqk) {
+    const bool is_q = u < p.n_q;
+    const int t = is_q ? u : u - p.n_q;
+    const int heads = is_q ? p.hq : p.hkv;
+    const int c = t & 7;  // 8-lane group of the first half
+    const int rh = t >> 3;
+    const int row = rh / heads, head = rh - (rh / heads) * heads;
+    const __nv_bfloat16* cs = p.cos + size_t(row) * p.cs_row_stride + c * 8;
+    const __nv_bfloat16* sn = p.sin + size_t(row) * p.cs_row_stride + c * 8;
+    const __nv_bfloat16* src =
+        is_q ? p.q + size_t(row) * p.q_row_stride + head * 128 + c * 8
+             : p.k + size_t(row) * p.kv_row_stride + head * 128 + c * 8;
+    w.a = ld16(src);
+    w.b = ld16(src + 64);
+    w.c1 = ld16(cs);
+    w.c2 = ld16(cs + 64);
+    w.s1 = ld16(sn);
+    w.s2 = ld16(sn + 64);
+    w.dst = is_q ? p.q + size_t(row) * p.q_row_stride + head * 128 + c * 8
+                 : p.k_cache + size_t(head) * p.kc_head_stride +
+                       size_t(p.dst_row0 + row) * p.cache_row_stride + c * 8;
+    w.kind = 0;
+  } else {
+    const int t = u - nqk;
+    const int c = t & 15;  // 16-byte chunk of the row
+    const int rh = t >> 4;
+    const int row = rh / p.hkv, head = rh - (rh / p.hkv) * p.hkv;
+    w.a = ld16(p.v + size_t(row) * p.kv_row_stride + head * 128 + c * 8);
+    w.dst = p.v_cache + size_t(head) * p.vc_head_stride +
+            size_t(p.dst_row0 + row) * p.cache_row_stride + c * 8;
+    w.kind = 1;
+  }
+}
+
+__device__ __forceinline__ void store_unit(const Unit& w) {
+  if (w.kind == 0) {
+    uint4 y1, y2;
+    rotate8(w.a, w.b, w.c1, w.c2, w.s1, w.s2, y1, y2);
+    st16(w.dst, y1);
+    st16(w.dst + 64, y2);
+  } else if (w.kind == 1) {
+    st16(w.dst, w.a);
+  }
+}
+
+// One wave of CTAs (eight of 256 threads per SM) walks the units a grid
+// apart; more units per thread, or more CTAs than one wave, measured slower.
 __global__ void __launch_bounds__(kThreads) rope_append_kernel(const Params p) {
   // Launched with programmatic dependent launch: the CTAs are scheduled
   // while the previous kernel on the stream finishes, and nothing is read
@@ -93,41 +152,12 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(const Params p) {
   // waits for this one's completion in its own griddepcontrol.wait.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const int64_t total = p.n_q + p.n_k + p.n_v;
-  for (int64_t u = int64_t(blockIdx.x) * kThreads + threadIdx.x; u < total;
-       u += int64_t(gridDim.x) * kThreads) {
-    if (u < p.n_q + p.n_k) {
-      const bool is_q = u < p.n_q;
-      const int64_t t = is_q ? u : u - p.n_q;
-      const int heads = is_q ? p.hq : p.hkv;
-      const int c = int(t & 7);                    // 8-lane group of the first half
-      const int64_t rh = t >> 3;
-      const int row = int(rh / heads), head = int(rh % heads);
-      const __nv_bfloat16* cs = p.cos + size_t(row) * p.cs_row_stride + c * 8;
-      const __nv_bfloat16* sn = p.sin + size_t(row) * p.cs_row_stride + c * 8;
-      const uint4 c1 = ld16(cs), c2 = ld16(cs + 64), s1 = ld16(sn), s2 = ld16(sn + 64);
-      const __nv_bfloat16* src =
-          is_q ? p.q + size_t(row) * p.q_row_stride + size_t(head) * 128 + c * 8
-               : p.k + size_t(row) * p.kv_row_stride + size_t(head) * 128 + c * 8;
-      const uint4 a = ld16(src), b = ld16(src + 64);
-      uint4 y1, y2;
-      rotate8(a, b, c1, c2, s1, s2, y1, y2);
-      __nv_bfloat16* dst =
-          is_q ? p.q + size_t(row) * p.q_row_stride + size_t(head) * 128 + c * 8
-               : p.k_cache + size_t(head) * p.kc_head_stride +
-                     size_t(p.dst_row0 + row) * p.cache_row_stride + c * 8;
-      st16(dst, y1);
-      st16(dst + 64, y2);
-    } else {
-      const int64_t t = u - p.n_q - p.n_k;
-      const int c = int(t & 15);                   // 16-byte chunk of the row
-      const int64_t rh = t >> 4;
-      const int row = int(rh / p.hkv), head = int(rh % p.hkv);
-      const uint4 x = ld16(p.v + size_t(row) * p.kv_row_stride + size_t(head) * 128 + c * 8);
-      st16(p.v_cache + size_t(head) * p.vc_head_stride +
-               size_t(p.dst_row0 + row) * p.cache_row_stride + c * 8,
-           x);
-    }
+  const int total = p.n_q + p.n_k + p.n_v;
+  const int stride = int(gridDim.x) * kThreads;
+  for (int u = int(blockIdx.x) * kThreads + int(threadIdx.x); u < total; u += stride) {
+    Unit w;
+    load_unit(p, u, w);
+    store_unit(w);
   }
 }
 
@@ -179,12 +209,21 @@ extern "C" int hsd_rope_append(void* q, int64_t q_row_stride, const void* k, con
   p.hq = num_q_heads;
   p.hkv = num_kv_heads;
   p.dst_row0 = dst_row0;
-  p.n_q = int64_t(n_rows) * num_q_heads * 8;
-  p.n_k = int64_t(n_rows) * num_kv_heads * 8;
-  p.n_v = int64_t(n_rows) * num_kv_heads * 16;
-  const int64_t total = p.n_q + p.n_k + p.n_v;
+  const int64_t total = int64_t(n_rows) * (num_q_heads * 8 + num_kv_heads * 24);
+  if (total >= (int64_t(1) << 30)) {
+    hsd_host::set_error("hsd_rope_append: %d rows x %d heads exceed the launch's index range",
+                        n_rows, num_q_heads + num_kv_heads);
+    return HSD_ERR_TOO_LARGE;
+  }
+  p.n_q = n_rows * num_q_heads * 8;
+  p.n_k = n_rows * num_kv_heads * 8;
+  p.n_v = n_rows * num_kv_heads * 16;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    sms = 148;
   const int64_t blocks = (total + rope::kThreads - 1) / rope::kThreads;
-  const int grid = int(blocks < 148 * 16 ? blocks : 148 * 16);
+  const int grid = int(blocks < int64_t(sms) * 8 ? blocks : int64_t(sms) * 8);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3(rope::kThreads);

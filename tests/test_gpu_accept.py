@@ -99,6 +99,18 @@ def test_accept_kmp_matches_oracle(dev, seed, tight):
     compare(sc, seed, expect, filt, run_kernel(sc, dev, page_block=page))
 
 
+@pytest.mark.parametrize("n_blocks,seed", [(33, 0), (40, 1), (64, 2), (97, 3), (256, 4),
+                                           (300, 5)])
+def test_accept_kmp_many_blocks_matches_oracle(dev, n_blocks, seed):
+    """More blocks than one CTA's 32 warps: the launch becomes a cluster of
+    up to eight CTAs sharing the filter (and, past 256 blocks, warps take
+    several blocks each)."""
+    sc = AC.make_scenario(100 + seed, n_blocks=n_blocks, tight=bool(seed & 1))
+    page = n_blocks - 1 if seed % 2 == 0 else None
+    expect, filt = run_oracle_checked(sc, page)
+    compare(sc, seed, expect, filt, run_kernel(sc, dev, page_block=page))
+
+
 def compare(sc, seed, expect, filt, kernel_out):
     from hsd_b200 import accept as A
     res, blocks, gen, vis, kfilt = kernel_out
