@@ -88,3 +88,43 @@ def test_keys_and_values_only(dev):
     torch.cuda.synchronize()
     assert np.array_equal(d_kc.float().cpu().numpy(), want_kc)
     assert np.array_equal(d_vc.float().cpu().numpy(), want_vc)
+
+
+def test_special_values_bitwise_like_transformers(dev):
+    """Rounding edge cases: products and sums that overflow to infinity,
+    bf16 subnormals, signed zeros, ties between two bf16 neighbours and
+    infinite inputs, compared bit for bit (as int16) with transformers' ops
+    on the device."""
+    from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
+
+    from hsd_b200.rope import rope_append
+    g = torch.Generator().manual_seed(11)
+    n, hq, hkv = 256, 4, 2
+    w = (hq + 2 * hkv) * 128
+    special = torch.tensor([3.0e38, -3.0e38, 1.7e38, 2.0e-39, -5.0e-40, 1.0e-38, 0.0, -0.0,
+                            float("inf"), float("-inf"), 1.00390625, 65504.0, 1.5e-45, 7.0])
+    qkv = torch.randn(n, w, generator=g)
+    pick = torch.randint(0, len(special), (n, w), generator=g)
+    mask = torch.rand(n, w, generator=g) < 0.5
+    qkv = torch.where(mask, special[pick], qkv).to(torch.bfloat16)
+    cs_special = torch.tensor([1.0, -1.0, 0.5, 0.99609375, 1.0e-38, 2.0e-39, 0.75, 0.0])
+    cos = cs_special[torch.randint(0, len(cs_special), (n, 128), generator=g)]
+    sin = cs_special[torch.randint(0, len(cs_special), (n, 128), generator=g)]
+    cos, sin = cos.to(torch.bfloat16).to(dev), sin.to(torch.bfloat16).to(dev)
+    qd = qkv.to(dev)
+    kc = torch.zeros(hkv, n + 8, 128, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    q4 = qd[:, :hq * 128].reshape(1, n, hq, 128).transpose(1, 2)
+    k4 = qd[:, hq * 128:(hq + hkv) * 128].reshape(1, n, hkv, 128).transpose(1, 2)
+    qe, ke = apply_rotary_pos_emb(q4.clone(), k4.clone(), cos[None], sin[None])
+    qv = rope_append(qd[:, :hq * 128], qd[:, hq * 128:(hq + hkv) * 128],
+                     qd[:, (hq + hkv) * 128:], cos, sin, kc, vc, 4)
+    torch.cuda.synchronize()
+    nan_q, nan_k = torch.isnan(qe), torch.isnan(ke[0])
+    assert torch.equal(torch.isnan(qv), nan_q) and torch.equal(torch.isnan(kc[:, 4:4 + n]), nan_k)
+    bits = lambda t: t.contiguous().view(torch.int16)
+    assert torch.equal(bits(torch.where(nan_q, 0, qv)), bits(torch.where(nan_q, 0, qe)))
+    got_k = kc[:, 4:4 + n]
+    assert torch.equal(bits(torch.where(nan_k, 0, got_k)), bits(torch.where(nan_k, 0, ke[0])))
+    assert torch.equal(bits(vc[:, 4:4 + n]),
+                       bits(qd[:, (hq + hkv) * 128:].reshape(n, hkv, 128).transpose(0, 1)))
