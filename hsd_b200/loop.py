@@ -131,6 +131,7 @@ class VerifyLoop:
         self.compact_hook = compact_hook
         if self.page_block:
             self.drafts[-1] = []
+        self._drafts_np = [np.asarray(d, dtype=np.int64) for d in self.drafts]
         # host state of the current step
         self.input_ids = np.concatenate([np.asarray(p, dtype=np.int64) for p in prompts])
         if packed is not None:
@@ -205,34 +206,34 @@ class VerifyLoop:
         if self._mask is None:
             q = int(self.input_ids.size)
             segs = np.zeros((self.nb, 6), dtype=np.int32)
+            segs[:, 0], segs[:, 1], segs[:, 2] = self.q_start, self.q_len, self.kinds
             row_seg = np.full(q, -1, dtype=np.int32)
+            nrows = int(self.q_len.sum())
+            row_seg[:nrows] = np.repeat(np.arange(self.nb, dtype=np.int32), self.q_len)
             tree_rows, tree_off = [], 0
-            for b in range(self.nb):
+            for b in [b for b in range(self.nb) if self.kinds[b] == SEG_TREE]:
                 qs, ql = int(self.q_start[b]), int(self.q_len[b])
-                segs[b, :3] = (qs, ql, self.kinds[b])
-                row_seg[qs:qs + ql] = b
-                if self.kinds[b] == SEG_TREE:
-                    # node i sees itself and its ancestors (D:1506-1533), rows
-                    # from the tree kernel or the host tree; pad rows see nothing
-                    tw = (ql + 63) // 64
-                    n = int(self.valid[b])
-                    if self.host_tree[b] is not None:
-                        anc = np.zeros((ql, tw * 64), dtype=bool)
-                        par = self.host_tree[b][1]
-                        for j in range(n):
-                            a = j
-                            while a >= 0:
-                                anc[j, a] = True
-                                a = par[a]
-                        rows = torch.from_numpy(pack_bits(anc).view(np.int64)).to(self.device)
-                    else:
-                        i = self.tree_slot[b]
-                        rows = torch.zeros((ql, tw), dtype=torch.int64, device=self.device)
-                        w = min(tw, self.trees.anc.shape[2])
-                        rows[:n, :w] = self.trees.anc[i, :n, :w]
-                    tree_rows.append(rows.reshape(-1))
-                    segs[b, 3], segs[b, 4] = tree_off, tw
-                    tree_off += ql * tw
+                # node i sees itself and its ancestors (D:1506-1533), rows
+                # from the tree kernel or the host tree; pad rows see nothing
+                tw = (ql + 63) // 64
+                n = int(self.valid[b])
+                if self.host_tree[b] is not None:
+                    anc = np.zeros((ql, tw * 64), dtype=bool)
+                    par = self.host_tree[b][1]
+                    for j in range(n):
+                        a = j
+                        while a >= 0:
+                            anc[j, a] = True
+                            a = par[a]
+                    rows = torch.from_numpy(pack_bits(anc).view(np.int64)).to(self.device)
+                else:
+                    i = self.tree_slot[b]
+                    rows = torch.zeros((ql, tw), dtype=torch.int64, device=self.device)
+                    w = min(tw, self.trees.anc.shape[2])
+                    rows[:n, :w] = self.trees.anc[i, :n, :w]
+                tree_rows.append(rows.reshape(-1))
+                segs[b, 3], segs[b, 4] = tree_off, tw
+                tree_off += ql * tw
             kv_bits = self.seg_bits
             q_blocks = int(self.q_start[-1] + self.q_len[-1]) if self.nb else 0
             if self.pad_rows_inherit and q > q_blocks:
@@ -348,7 +349,8 @@ class VerifyLoop:
         self.blocks[:, self._upd_cols] = torch.from_numpy(cols).to(dev, non_blocking=True)
         pad_cols = np.zeros(self.stride * 64, dtype=bool)
         pad_cols[kv - q:kv] = self.input_ids == self.pad
-        pad_dev = torch.from_numpy(pack_bits(pad_cols).view(np.int64)).to(dev, non_blocking=True)
+        pad_words = np.packbits(pad_cols, bitorder="little").view(np.int64)  # 64 bits a word
+        pad_dev = torch.from_numpy(pad_words).to(dev, non_blocking=True)
         self.filter.zero_()
         self.out_bits.zero_()
         cfg = make_config(nb, kv, q, self.stride, self.eos, self.mws0, self.mws_ub,
@@ -387,9 +389,12 @@ class VerifyLoop:
         keep_bits, keep_idx, counts = keep_indices(self.out_bits, self.filter, kv,
                                                    out=self._keep_out)
         live = [b for b in range(nb) if self.modes[b] != N.HSD_MODE_FINISHED]
-        gidx = np.concatenate([b * self.gen_cap + len(self.gen_host[b])
-                               + np.arange(int(self.q_len[b])) for b in live]
-                              or [np.zeros(0, dtype=np.int64)]).astype(np.int64)
+        # gen-pool slots of every live block's rows, one run per block
+        lens = self.q_len[live].astype(np.int64)
+        first = np.asarray([b * self.gen_cap + len(self.gen_host[b]) for b in live],
+                           dtype=np.int64)
+        gidx = (np.arange(int(lens.sum()), dtype=np.int64)
+                + np.repeat(first - (np.cumsum(lens) - lens), lens))
         gidx = np.minimum(gidx, self.gen_pool.numel() - 1)
         parts = [self.results.reshape(-1), self.status, counts, self.blocks.reshape(-1)]
         if gidx.size:
@@ -529,36 +534,40 @@ class VerifyLoop:
                 continue
             base = int(self.position_ids[int(r[R["pointer"]])]) + 1
             if page_in is not None and b == nb - 1:
-                toks, pos = list(page_in.ids), list(page_in.pos)
+                toks = np.asarray(page_in.ids, dtype=np.int64)
+                pos = np.asarray(page_in.pos, dtype=np.int64)
                 if page_in.kind == "spec":
                     new_modes[b], new_kinds[b] = N.HSD_MODE_SPEC, SEG_CAUSAL
                 elif page_in.kind == "tree":
                     new_modes[b], new_kinds[b] = N.HSD_MODE_TREE, SEG_TREE
                     new_parents[b] = list(page_in.parents)
-                    new_host_tree[b] = (list(toks[:page_in.valid]), list(page_in.parents))
+                    new_host_tree[b] = (toks[:page_in.valid].tolist(), list(page_in.parents))
                 else:
                     new_modes[b], new_kinds[b] = N.HSD_MODE_NORMAL, SEG_SINGLE
                 new_valid[b] = int(page_in.valid)
             elif r[R["match_count"]] == 1:
-                toks = self.drafts[b][int(r[R["slice_begin"]]):int(r[R["slice_end"]])]
+                toks = self._drafts_np[b][int(r[R["slice_begin"]]):int(r[R["slice_end"]])]
                 n = len(toks)
                 if not self.tight:
-                    toks = toks + [self.pad] * (math.ceil(n / self.mil) * self.mil - n)
+                    pad_n = math.ceil(n / self.mil) * self.mil - n
+                    toks = np.concatenate([toks, np.full(pad_n, self.pad, dtype=np.int64)])
                 new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_SPEC, SEG_CAUSAL, n
-                pos = list(range(base, base + len(toks)))
+                pos = np.arange(base, base + len(toks), dtype=np.int64)
             else:
                 tree = host_tree_lists.get(b) if b in want else None
                 if tree is not None and len(tree[0]) > 1:    # D:1488-1543
                     tokens, depths, new_parents[b] = tree
                     n = len(tokens)
                     pad_n = 0 if self.tight else math.ceil(n / self.mil) * self.mil - n
-                    toks = list(tokens) + [self.pad] * pad_n
-                    pos = [d + base for d in depths] + [0] * pad_n
+                    toks = np.asarray(list(tokens) + [self.pad] * pad_n, dtype=np.int64)
+                    pos = np.asarray([d + base for d in depths] + [0] * pad_n, dtype=np.int64)
                     new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_TREE, SEG_TREE, n
                 else:                                        # D:1544-1565
                     fill = 0 if self.tight else self.mil - 1
-                    toks = [int(r[R["next_token"]])] + [self.pad] * fill
-                    pos = [base] + [0] * fill
+                    toks = np.full(1 + fill, self.pad, dtype=np.int64)
+                    toks[0] = int(r[R["next_token"]])
+                    pos = np.zeros(1 + fill, dtype=np.int64)
+                    pos[0] = base
                     new_modes[b], new_kinds[b], new_valid[b] = N.HSD_MODE_NORMAL, SEG_SINGLE, 1
             new_ids.append(toks)
             new_pos.append(pos)
@@ -571,10 +580,11 @@ class VerifyLoop:
         # pad filter drops their columns, so tokens and compaction are the same
         if self.tight and sum(new_lens) % Q_BLOCK:
             pad_n = Q_BLOCK - sum(new_lens) % Q_BLOCK
-            new_ids.append([self.pad] * pad_n)
-            new_pos.append([0] * pad_n)
-        self.input_ids = np.concatenate([np.asarray(t, dtype=np.int64) for t in new_ids])
-        self.position_ids = np.concatenate([np.asarray(t, dtype=np.int64) for t in new_pos])
+            new_ids.append(np.full(pad_n, self.pad, dtype=np.int64))
+            new_pos.append(np.zeros(pad_n, dtype=np.int64))
+        empty = np.zeros(0, dtype=np.int64)
+        self.input_ids = np.concatenate(new_ids or [empty])
+        self.position_ids = np.concatenate(new_pos or [empty])
         ends = np.cumsum(new_lens)
         self.q_len = np.asarray(new_lens, dtype=np.int64)
         self.q_start = ends - self.q_len
