@@ -99,8 +99,8 @@ def test_accept_kmp_matches_oracle(dev, seed, tight):
     compare(sc, seed, expect, filt, run_kernel(sc, dev, page_block=page))
 
 
-@pytest.mark.parametrize("n_blocks,seed", [(33, 0), (40, 1), (64, 2), (97, 3), (256, 4),
-                                           (300, 5)])
+@pytest.mark.parametrize("n_blocks,seed", [(17, 6), (33, 0), (40, 1), (64, 2), (97, 3),
+                                           (129, 7), (256, 4), (300, 5)])
 def test_accept_kmp_many_blocks_matches_oracle(dev, n_blocks, seed):
     """More blocks than one CTA's 32 warps: the launch becomes a cluster of
     up to eight CTAs sharing the filter (and, past 256 blocks, warps take
