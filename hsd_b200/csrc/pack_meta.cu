@@ -53,15 +53,33 @@ __device__ __forceinline__ uint64_t clip_word(uint64_t w, int t, int kv_len) {
   return w;
 }
 
-__device__ __forceinline__ uint64_t seg_row_word(const SegSource& S, int q, int t) {
-  if (q >= S.q_len) return 0;
+// A packed row's segment, looked up once per row (row_seg, then the
+// descriptor) so that the per-word loop has one load per word.
+struct RowSeg {
+  int s;  // segment, < 0: the row sees nothing
+  hsd_segment_t seg;
+};
+
+__device__ __forceinline__ RowSeg row_segment(const SegSource& S, int q) {
+  RowSeg r;
+  r.s = -1;
+  if (q >= S.q_len) return r;
   const int s = S.row_seg[q];
-  if (s < 0) return 0;
+  if (s < 0) return r;
   if (s >= S.n_segs) {
     report(S.status, HSD_DEV_BAD_INDEX | 1);
-    return 0;
+    return r;
   }
-  const hsd_segment_t seg = S.segs[s];
+  r.s = s;
+  r.seg = S.segs[s];
+  return r;
+}
+
+__device__ __forceinline__ uint64_t seg_row_word(const SegSource& S, const RowSeg& rs, int q,
+                                                 int t) {
+  if (rs.s < 0) return 0;
+  const int s = rs.s;
+  const hsd_segment_t& seg = rs.seg;
   uint64_t w = S.seg_kv_bits[size_t(s) * S.stride + t];
   const int i = q - seg.q_start;
   const int lo = S.kv_base + seg.q_start;
@@ -104,6 +122,12 @@ __global__ void __launch_bounds__(256) classify_kernel(SegSource S, hsd_plan_t P
   const int warp = warp_id(), lane = lane_id();
   const int n64 = P.n_kv64;
   uint64_t* words = P.mask_words + size_t(qt) * n64 * 128;
+  // lane's rows: lane + 32 k, their segments looked up once
+  RowSeg rs[4];
+  if (kFromSegments) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) rs[k] = row_segment(S, qt * 128 + lane + 32 * k);
+  }
   for (int t = warp; t < n64; t += 8) {
     uint64_t acc_and = ~0ull, acc_or = 0;
 #pragma unroll
@@ -112,7 +136,7 @@ __global__ void __launch_bounds__(256) classify_kernel(SegSource S, hsd_plan_t P
       const int q = qt * 128 + r;
       uint64_t w;
       if (kFromSegments) {
-        w = seg_row_word(S, q, t);
+        w = seg_row_word(S, rs[k], q, t);
         words[size_t(t) * 128 + r] = w;
       } else {
         w = (q < P.q_len) ? words[size_t(t) * 128 + r] : 0ull;
