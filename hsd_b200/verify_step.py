@@ -303,8 +303,10 @@ class VerifyStep:
         (set k is rewritten only after the step that last read it, two steps
         back, has finished).  The token ids (KBs) go on the compute stream.
         Inside a CUDA graph capture the copy stream forks from the capturing
-        stream when ``fork`` (the graph's first step) and otherwise queues
-        behind its own earlier copies: replays of a graph never overlap.
+        stream when ``fork`` (the graph's first step); a later step whose input
+        set an earlier step of the same capture read waits for that step's
+        kernels, the graph's second step only for its own earlier copies
+        (replays of a graph never overlap).
         """
         h = self.host_buffers()
         cs = stream if stream is not None else torch.cuda.current_stream()
@@ -316,9 +318,14 @@ class VerifyStep:
         xs = self._copy_stream
         q, nkv = (self.q, self.new_kv) if buffers == 0 else (
             self._second_input_set()["q"], self._second_input_set()["new_kv"])
-        if torch.cuda.is_current_stream_capturing():
+        capturing = torch.cuda.is_current_stream_capturing()
+        if capturing:
             if fork:
                 xs.wait_stream(cs)
+                self._cap_used = [False, False]
+                self._cap_free = [torch.cuda.Event(), torch.cuda.Event()]
+            elif self._cap_used[buffers]:
+                xs.wait_event(self._cap_free[buffers])  # recorded earlier in this capture
         elif self._set_used[buffers]:
             xs.wait_event(self._set_free[buffers])  # the step that last read this set is done
         else:
@@ -336,28 +343,34 @@ class VerifyStep:
             self.input_ids.copy_(h["input_ids"], non_blocking=True)
             self.next_ids.copy_(h["next_ids"], non_blocking=True)
         self.run(cs, layer_ready=self._ready[buffers], buffers=buffers)
-        if not torch.cuda.is_current_stream_capturing():
+        if capturing:
+            self._cap_free[buffers].record(cs)
+            self._cap_used[buffers] = True
+        else:
             self._set_free[buffers].record(cs)
             self._set_used[buffers] = True
         with torch.cuda.stream(cs):
             h["results"].copy_(self.results, non_blocking=True)
             h["counts"].copy_(self.counts, non_blocking=True)
 
-    def capture(self, from_host=False, attention_only=False):
-        """A CUDA graph of one whole step (``run`` or, ``from_host``, two
-        consecutive ``run_from_host`` steps on alternating input sets, or
-        only the step's attention launches): the launches replay with no
-        host work between them.  Call :meth:`run` (and, for ``from_host``,
-        :meth:`run_from_host` on both sets) once before capturing: first-call
-        setup must not happen inside a capture."""
+    def capture(self, from_host=False, attention_only=False, host_steps=2):
+        """A CUDA graph of one whole step (``run`` or, ``from_host``,
+        ``host_steps`` (even) consecutive ``run_from_host`` steps on
+        alternating input sets, or only the step's attention launches): the
+        launches replay with no host work between them.  Call :meth:`run`
+        (and, for ``from_host``, :meth:`run_from_host` on both sets) once
+        before capturing: first-call setup must not happen inside a
+        capture."""
+        if from_host and (host_steps < 2 or host_steps % 2):
+            raise ValueError("host_steps: an even number of steps, at least 2")
         torch.cuda.synchronize(self.device)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             if attention_only:
                 self.run_attention()
             elif from_host:
-                self.run_from_host(buffers=0, fork=True)
-                self.run_from_host(buffers=1, fork=False)
+                for i in range(host_steps):
+                    self.run_from_host(buffers=i % 2, fork=i == 0)
             else:
                 self.run()
         torch.cuda.synchronize(self.device)

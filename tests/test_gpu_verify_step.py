@@ -118,8 +118,9 @@ def _state(s):
 
 def test_from_host_and_graph_match_device_form(page):
     """The end-to-end form (rows copied layer by layer into alternating
-    device input sets, appended per layer) and its two-step CUDA graph give
-    the device-resident form's state after the same number of steps."""
+    device input sets, appended per layer) and its two- and four-step CUDA
+    graphs give the device-resident form's state after the same number of
+    steps."""
     a = _step(page)
     a.run()
     a.run()
@@ -127,6 +128,9 @@ def test_from_host_and_graph_match_device_form(page):
     a.run()
     a.run()
     want4 = _state(a)
+    a.run()
+    a.run()
+    want6 = _state(a)
 
     b = _step(page)
     b.run_from_host(buffers=0)
@@ -146,4 +150,14 @@ def test_from_host_and_graph_match_device_form(page):
     for x, y in zip(want4, _state(c)):
         assert torch.equal(x, y)
     assert int(c.status.item()) == 0
+    del g
+
+    d = _step(page)            # four steps per graph: set 0 reused inside the capture
+    d.run_from_host(buffers=0)
+    d.run_from_host(buffers=1)
+    g = d.capture(from_host=True, host_steps=4)
+    g.replay()
+    for x, y in zip(want6, _state(d)):
+        assert torch.equal(x, y)
+    assert int(d.status.item()) == 0
     del g
