@@ -193,10 +193,11 @@ __device__ void count_matches(const int32_t* text, int n, const int32_t* pat, in
 // path and then inverts its column range (D:1266-1286), a finished block ORs
 // in its pointer row's visibility (D:1299-1319).  Setting bits commutes with
 // setting bits, so the rejected columns and tree paths go straight into the
-// filter words (atomics on masked words: neighbours may share a word).  Only the inversions and the finished rows depend on the
-// block order (a row may reach another block's columns); each block records
-// those two as a FilterRec and one thread per filter word replays them in
-// block order at the end.
+// filter words (atomics on masked words: neighbours may share a word).  Only
+// the inversions and the finished rows depend on the block order (a row may
+// reach another block's columns); each block records those two as a
+// FilterRec and one thread per filter word replays them in block order at
+// the end.
 struct FilterRec {
   int32_t lo, hi;    // inverted columns [lo, hi] (none if lo > hi)
   int32_t finished;  // OR the block's visibility row
@@ -214,6 +215,7 @@ __device__ __forceinline__ void filter_or(unsigned long long* f, int lo, int hi,
 // memory, which the others reach through distributed shared memory (plain
 // stores), and the first CTA replays the order-dependent updates.
 __global__ void __launch_bounds__(1024) accept_kmp_kernel(Params p) {
+  pdl_wait_then_release();  // launched with launch_pdl
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ uint8_t smem_raw[];
@@ -547,20 +549,10 @@ static int accept_launch(const hsd_accept_config_t* cfg, hsd_block_t* blocks,
   const int warps = per_cta < 32 ? per_cta : 32;
   // one FilterRec per block (at most 12 KB: within the default limit)
   const size_t smem = size_t(cfg->n_blocks) * sizeof(acc::FilterRec);
-  cudaLaunchConfig_t lc = {};
-  lc.gridDim = dim3(unsigned(ctas));
-  lc.blockDim = dim3(unsigned(warps * 32));
-  lc.dynamicSmemBytes = smem;
-  lc.stream = reinterpret_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = unsigned(ctas);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  lc.attrs = attr;
-  lc.numAttrs = 1;
-  return hsd_host::cuda_check(cudaLaunchKernelEx(&lc, acc::accept_kmp_kernel, p),
-                              "accept_kmp_kernel launch");
+  return hsd_host::launch_pdl(acc::accept_kmp_kernel, dim3(unsigned(ctas)),
+                              dim3(unsigned(warps * 32)), smem,
+                              reinterpret_cast<cudaStream_t>(stream), "accept_kmp_kernel launch",
+                              unsigned(ctas), p);
 }
 
 extern "C" int hsd_accept_kmp(const hsd_accept_config_t* cfg, hsd_block_t* blocks,

@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "hsd_b200.h"
 
 namespace hsd {
@@ -401,6 +403,15 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t value,
   }
 }
 
+// Programmatic dependent launch, device side: wait until the previous kernel
+// on the stream has completed (its writes visible), then let the next kernel
+// be scheduled (it waits for this one in its own pdl_wait).  Called first
+// thing in a kernel launched with launch_pdl, before any global access.
+__device__ __forceinline__ void pdl_wait_then_release() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 }  // namespace hsd
 
 // Host-side helpers shared by the .cu files of the library.
@@ -417,4 +428,29 @@ EncodeTiledFn tensor_map_encoder();
 // launch counters that follow the partial records (they run to the end of
 // hsd_attention_workspace_bytes()).
 size_t attention_flags_offset(int32_t q_len, int32_t num_q_heads, int32_t num_kv_heads);
+
+// Launch with programmatic stream serialization (the kernel starts with
+// hsd::pdl_wait_then_release), optionally as a cluster of cluster_x CTAs.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+               cudaStream_t stream, const char* what, unsigned cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cluster_x > 0) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
+  return cuda_check(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), what);
+}
 }  // namespace hsd_host

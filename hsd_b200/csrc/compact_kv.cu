@@ -50,6 +50,7 @@ __global__ void __launch_bounds__(kThreads) compact_planes_kernel(
     const uint64_t* __restrict__ plane_ptrs, int n_planes, int row_bytes,
     const int32_t* __restrict__ keep_idx, int n_keep_host, const int32_t* counts,
     int32_t* status) {
+  pdl_wait_then_release();  // launched with launch_pdl
   const int cs = int(cluster_nrank());
   const int crank = int(cluster_rank());
   const int plane = blockIdx.x / cs;
@@ -141,6 +142,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) compact_plane_bulk_kernel(
     const uint64_t* __restrict__ plane_ptrs, int n_planes, int row_bytes,
     const int32_t* __restrict__ keep_idx, int n_keep_host, const int32_t* counts,
     int32_t* status) {
+  pdl_wait_then_release();  // launched with launch_pdl
   extern __shared__ __align__(128) unsigned char smem[];
   int32_t* s_idx = reinterpret_cast<int32_t*>(smem + kBulkNBuf * kBulkBuf);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kBulkNBuf * kBulkBuf + kIdxCache * 4);
@@ -249,6 +251,7 @@ __global__ void __launch_bounds__(1024) keep_kernel(const uint64_t* live, int n_
                                                     int live_stride, const uint64_t* filter,
                                                     int kv_len, uint64_t* keep_bits,
                                                     int32_t* keep_idx, int32_t* counts) {
+  pdl_wait_then_release();  // launched with launch_pdl
   __shared__ int warp_sums[32];
   __shared__ int carry;
   __shared__ int first_moved;
@@ -326,6 +329,7 @@ __global__ void __launch_bounds__(1024) keep_kernel(const uint64_t* live, int n_
 __global__ void compact_bits_kernel(const uint64_t* in, uint64_t* out, int n_rows, int stride,
                                     const int32_t* keep_idx, const int32_t* counts,
                                     int out_words) {
+  pdl_wait_then_release();  // launched with launch_pdl
   const int n_keep = counts[0];
   const int total = n_rows * out_words;
   const int lane = lane_id();
@@ -355,6 +359,7 @@ __global__ void __launch_bounds__(256) append_kernel(const uint64_t* __restrict_
                                                      const uint64_t* __restrict__ src_planes,
                                                      int n_planes, int row_bytes, int dst_row0,
                                                      int n_rows, int chunks) {
+  pdl_wait_then_release();  // launched with launch_pdl
   const int plane = blockIdx.x / chunks, chunk = blockIdx.x % chunks;
   if (plane >= n_planes) return;
   const size_t nvec = size_t(n_rows) * (row_bytes >> 4);
@@ -423,32 +428,22 @@ int hsd_compact_kv(const uint64_t* plane_ptrs, int32_t n_planes, int32_t row_byt
       if (rc) return rc;
       g_bulk_attr_set[dev].store(true, std::memory_order_release);
     }
-    compact::compact_plane_bulk_kernel<<<n_planes, compact::kBulkThreads, compact::kBulkSmem,
-                                         st>>>(plane_ptrs, n_planes, row_bytes, keep_idx, n_keep,
-                                               counts, status);
-    return hsd_host::cuda_check(cudaGetLastError(), "compact_plane_bulk_kernel launch");
+    return hsd_host::launch_pdl(compact::compact_plane_bulk_kernel, dim3(unsigned(n_planes)),
+                                dim3(compact::kBulkThreads), compact::kBulkSmem, st,
+                                "compact_plane_bulk_kernel launch", 0u, plane_ptrs,
+                                int(n_planes), int(row_bytes), keep_idx, int(n_keep), counts,
+                                status);
   }
 
   // Few planes: a cluster of CTAs per plane, enough to cover the SMs a few
   // times over, at most 8 (portable cluster size).
   int cs = 1;
   while (cs < 8 && n_planes * cs < 148 * 4) cs <<= 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(n_planes * cs));
-  cfg.blockDim = dim3(compact::kThreads);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cs;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return hsd_host::cuda_check(
-      cudaLaunchKernelEx(&cfg, compact::compact_planes_kernel, plane_ptrs, int(n_planes),
-                         int(row_bytes), keep_idx, int(n_keep), counts, status),
-      "compact_planes_kernel launch");
+  return hsd_host::launch_pdl(compact::compact_planes_kernel, dim3(unsigned(n_planes * cs)),
+                              dim3(compact::kThreads), 0, reinterpret_cast<cudaStream_t>(stream),
+                              "compact_planes_kernel launch", unsigned(cs), plane_ptrs,
+                              int(n_planes), int(row_bytes), keep_idx, int(n_keep), counts,
+                              status);
 }
 
 int hsd_kv_append(const uint64_t* dst_planes, const uint64_t* src_planes, int32_t n_planes,
@@ -463,9 +458,10 @@ int hsd_kv_append(const uint64_t* dst_planes, const uint64_t* src_planes, int32_
   const int64_t nvec = int64_t(n_rows) * (row_bytes >> 4);
   int chunks = int((nvec + 8191) / 8192);  // ~128 KB per CTA
   if (chunks < 1) chunks = 1;
-  compact::append_kernel<<<n_planes * chunks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      dst_planes, src_planes, n_planes, row_bytes, dst_row0, n_rows, chunks);
-  return hsd_host::cuda_check(cudaGetLastError(), "append_kernel launch");
+  return hsd_host::launch_pdl(compact::append_kernel, dim3(unsigned(n_planes * chunks)), dim3(256),
+                              0, reinterpret_cast<cudaStream_t>(stream), "append_kernel launch",
+                              0u, dst_planes, src_planes, int(n_planes), int(row_bytes),
+                              int(dst_row0), int(n_rows), chunks);
 }
 
 int hsd_keep_indices(const uint64_t* live_bits, int32_t n_live, int32_t live_stride,
@@ -476,9 +472,10 @@ int hsd_keep_indices(const uint64_t* live_bits, int32_t n_live, int32_t live_str
     hsd_host::set_error("hsd_keep_indices: bad arguments");
     return HSD_ERR_INVALID_ARG;
   }
-  compact::keep_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      live_bits, n_live, live_stride, filter_bits, kv_len, keep_bits, keep_idx, counts);
-  return hsd_host::cuda_check(cudaGetLastError(), "keep_kernel launch");
+  return hsd_host::launch_pdl(compact::keep_kernel, dim3(1), dim3(1024), 0,
+                              reinterpret_cast<cudaStream_t>(stream), "keep_kernel launch", 0u,
+                              live_bits, int(n_live), int(live_stride), filter_bits, int(kv_len),
+                              keep_bits, keep_idx, counts);
 }
 
 int hsd_compact_bits(const uint64_t* in_bits, uint64_t* out_bits, int32_t n_rows, int32_t stride,
@@ -491,10 +488,10 @@ int hsd_compact_bits(const uint64_t* in_bits, uint64_t* out_bits, int32_t n_rows
   }
   const int total = n_rows * out_words;  // one warp per output word
   const int grid = (total + 7) / 8 < 1184 ? (total + 7) / 8 : 1184;
-  compact::compact_bits_kernel<<<grid > 0 ? grid : 1, 256, 0,
-                                  reinterpret_cast<cudaStream_t>(stream)>>>(
-      in_bits, out_bits, n_rows, stride, keep_idx, counts, out_words);
-  return hsd_host::cuda_check(cudaGetLastError(), "compact_bits_kernel launch");
+  return hsd_host::launch_pdl(compact::compact_bits_kernel, dim3(unsigned(grid > 0 ? grid : 1)),
+                              dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                              "compact_bits_kernel launch", 0u, in_bits, out_bits, int(n_rows),
+                              int(stride), keep_idx, counts, int(out_words));
 }
 
 }  // extern "C"

@@ -117,6 +117,7 @@ __device__ __forceinline__ uint64_t warp_or64(uint64_t v) {
 // kernel stored.
 template <bool kFromSegments>
 __global__ void __launch_bounds__(256) classify_kernel(SegSource S, hsd_plan_t P) {
+  pdl_wait_then_release();  // launched with launch_pdl
   extern __shared__ uint8_t cls[];  // [n_kv64]
   const int qt = blockIdx.x;
   const int warp = warp_id(), lane = lane_id();
@@ -198,6 +199,7 @@ __global__ void __launch_bounds__(256) classify_kernel(SegSource S, hsd_plan_t P
 // the attention grid starts the longest tiles first, and the exclusive prefix
 // of block counts in that order (the work offsets of the stream-K schedule).
 __global__ void order_kernel(hsd_plan_t P) {
+  pdl_wait_then_release();  // launched with launch_pdl
   __shared__ int cnt_sorted[1024];
   const int n = P.n_qtiles;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -225,6 +227,7 @@ __global__ void order_kernel(hsd_plan_t P) {
 // 32-column halves are read as coalesced 128-byte lines.
 __global__ void __launch_bounds__(256) dense_words_kernel(const float* mask, int64_t row_stride,
                                                           hsd_plan_t P) {
+  pdl_wait_then_release();  // launched with launch_pdl
   const int n64 = P.n_kv64;
   const int64_t total = int64_t(P.n_qtiles) * 128 * n64;
   const int lane = lane_id();
@@ -273,17 +276,25 @@ static int launch_classify(bool from_segments, const meta::SegSource& S, const h
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(meta::classify_kernel<true>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    meta::classify_kernel<true><<<P.n_qtiles, 256, smem, st>>>(S, P);
+    {
+      int rc0 = hsd_host::launch_pdl(meta::classify_kernel<true>, dim3(unsigned(P.n_qtiles)),
+                                     dim3(256), smem, st, "classify_kernel launch", 0u, S, P);
+      if (rc0) return rc0;
+    }
   } else {
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(meta::classify_kernel<false>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    meta::classify_kernel<false><<<P.n_qtiles, 256, smem, st>>>(S, P);
+    {
+      int rc0 = hsd_host::launch_pdl(meta::classify_kernel<false>, dim3(unsigned(P.n_qtiles)),
+                                     dim3(256), smem, st, "classify_kernel launch", 0u, S, P);
+      if (rc0) return rc0;
+    }
   }
   int rc = hsd_host::cuda_check(cudaGetLastError(), "classify_kernel launch");
   if (rc) return rc;
-  meta::order_kernel<<<1, 1024, 0, st>>>(P);
-  return hsd_host::cuda_check(cudaGetLastError(), "order_kernel launch");
+  return hsd_host::launch_pdl(meta::order_kernel, dim3(1), dim3(1024), 0, st,
+                              "order_kernel launch", 0u, P);
 }
 
 extern "C" {
@@ -333,8 +344,8 @@ int hsd_build_plan_dense(const float* mask, int64_t row_stride, hsd_plan_t* plan
   const int64_t warps = int64_t(plan->n_qtiles) * 128 * plan->n_kv64;
   const int64_t blocks = (warps * 32 + 255) / 256;
   const int grid = int(blocks < 148 * 16 ? blocks : 148 * 16);
-  meta::dense_words_kernel<<<grid, 256, 0, st>>>(mask, row_stride, *plan);
-  rc = hsd_host::cuda_check(cudaGetLastError(), "dense_words_kernel launch");
+  rc = hsd_host::launch_pdl(meta::dense_words_kernel, dim3(unsigned(grid)), dim3(256), 0, st,
+                            "dense_words_kernel launch", 0u, mask, row_stride, *plan);
   if (rc) return rc;
   meta::SegSource S{};
   S.status = status;
