@@ -70,7 +70,7 @@ def profile_traffic(name):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 100 ms; ``stop()``
+    """nvidia-smi clocks / throttle reasons sampled every 20 ms; ``stop()``
     keeps the samples taken between ``mark_start()`` and ``mark_end()`` (the
     timed region), or all of them if the region was shorter than one
     sampling interval."""
@@ -97,7 +97,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
