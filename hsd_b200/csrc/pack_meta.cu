@@ -112,24 +112,26 @@ __device__ __forceinline__ uint64_t warp_or64(uint64_t v) {
   return (uint64_t(hi) << 32) | lo;
 }
 
-// One CTA (8 warps) per 128-row query tile.  kFromSegments: compute row words
-// from segment descriptors and store them; otherwise read the words the dense
-// kernel stored.
+// Row words and tile classes: CTA (qt, part) covers query tile qt's 64-column
+// tiles part, part + parts, ...; a warp per tile, each lane 4 rows.
+// kFromSegments: compute the row words from segment descriptors and store
+// them; otherwise read the words the dense kernel stored.
 template <bool kFromSegments>
 __global__ void __launch_bounds__(256) classify_kernel(SegSource S, hsd_plan_t P) {
   pdl_wait_then_release();  // launched with launch_pdl
-  extern __shared__ uint8_t cls[];  // [n_kv64]
   const int qt = blockIdx.x;
+  const int parts = gridDim.y;
   const int warp = warp_id(), lane = lane_id();
   const int n64 = P.n_kv64;
   uint64_t* words = P.mask_words + size_t(qt) * n64 * 128;
+  uint8_t* gcls = P.tile_class + size_t(qt) * n64;
   // lane's rows: lane + 32 k, their segments looked up once
   RowSeg rs[4];
   if (kFromSegments) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) rs[k] = row_segment(S, qt * 128 + lane + 32 * k);
   }
-  for (int t = warp; t < n64; t += 8) {
+  for (int t = int(blockIdx.y) + parts * warp; t < n64; t += parts * 8) {
     uint64_t acc_and = ~0ull, acc_or = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -147,13 +149,24 @@ __global__ void __launch_bounds__(256) classify_kernel(SegSource S, hsd_plan_t P
     }
     acc_and = warp_and64(acc_and);
     acc_or = warp_or64(acc_or);
-    if (lane == 0) cls[t] = acc_or == 0 ? 0 : (acc_and == ~0ull ? 2 : 1);
+    if (lane == 0) gcls[t] = acc_or == 0 ? 0 : (acc_and == ~0ull ? 2 : 1);
   }
-  __syncthreads();
-  uint8_t* gcls = P.tile_class + size_t(qt) * n64;
-  for (int t = threadIdx.x; t < n64; t += blockDim.x) gcls[t] = cls[t];
-  if (warp == 0) {
-    // FlexAttention-style ascending lists.
+}
+
+// One CTA: a warp per query tile turns its tile classes into the
+// FlexAttention-style ascending partial / full lists and the 128-column block
+// list; then the query tiles are ranked by descending block count (ties:
+// lower tile first), so the attention grid starts the longest tiles first,
+// with the exclusive prefix of block counts in that order (the work offsets
+// of the stream-K schedule).
+__global__ void __launch_bounds__(1024) order_kernel(hsd_plan_t P) {
+  pdl_wait_then_release();  // launched with launch_pdl
+  __shared__ int cnt_sorted[1024];
+  const int n = P.n_qtiles;
+  const int n64 = P.n_kv64;
+  const int warp = warp_id(), lane = lane_id(), nwarps = blockDim.x >> 5;
+  for (int qt = warp; qt < n; qt += nwarps) {
+    const uint8_t* cls = P.tile_class + size_t(qt) * n64;
     int n_part = 0, n_full = 0;
     int32_t* kvi = P.kv_indices + size_t(qt) * n64;
     int32_t* fvi = P.full_kv_indices + size_t(qt) * n64;
@@ -168,7 +181,6 @@ __global__ void __launch_bounds__(256) classify_kernel(SegSource S, hsd_plan_t P
       n_part += __popc(bp);
       n_full += __popc(bf);
     }
-    // 128-column blocks for the attention kernel.
     int n_blk = 0;
     uint32_t* bl = P.blk_list + size_t(qt) * P.n_kv128;
     for (int base = 0; base < P.n_kv128; base += 32) {
@@ -193,15 +205,7 @@ __global__ void __launch_bounds__(256) classify_kernel(SegSource S, hsd_plan_t P
       P.blk_count[qt] = n_blk;
     }
   }
-}
-
-// Query tiles ranked by descending block count (ties: lower tile first), so
-// the attention grid starts the longest tiles first, and the exclusive prefix
-// of block counts in that order (the work offsets of the stream-K schedule).
-__global__ void order_kernel(hsd_plan_t P) {
-  pdl_wait_then_release();  // launched with launch_pdl
-  __shared__ int cnt_sorted[1024];
-  const int n = P.n_qtiles;
+  __syncthreads();  // every tile's block count is written
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int ci = P.blk_count[i];
     int rank = 0;
@@ -267,31 +271,17 @@ static int check_plan(const hsd_plan_t* p) {
 
 static int launch_classify(bool from_segments, const meta::SegSource& S, const hsd_plan_t& P,
                            cudaStream_t st) {
-  const size_t smem = size_t(P.n_kv64);
-  if (smem > 200 * 1024) {
-    hsd_host::set_error("kv_len %d too large for the metadata kernel", P.kv_len);
-    return HSD_ERR_TOO_LARGE;
-  }
-  if (from_segments) {
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(meta::classify_kernel<true>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    {
-      int rc0 = hsd_host::launch_pdl(meta::classify_kernel<true>, dim3(unsigned(P.n_qtiles)),
-                                     dim3(256), smem, st, "classify_kernel launch", 0u, S, P);
-      if (rc0) return rc0;
-    }
-  } else {
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(meta::classify_kernel<false>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    {
-      int rc0 = hsd_host::launch_pdl(meta::classify_kernel<false>, dim3(unsigned(P.n_qtiles)),
-                                     dim3(256), smem, st, "classify_kernel launch", 0u, S, P);
-      if (rc0) return rc0;
-    }
-  }
-  int rc = hsd_host::cuda_check(cudaGetLastError(), "classify_kernel launch");
+  // enough CTAs to cover the SMs twice, at most one warp per 64-column tile
+  const int max_parts = (P.n_kv64 + 7) / 8;
+  int parts = (296 + P.n_qtiles - 1) / P.n_qtiles;
+  if (parts > max_parts) parts = max_parts;
+  if (parts < 1) parts = 1;
+  const dim3 grid(unsigned(P.n_qtiles), unsigned(parts));
+  int rc = from_segments
+               ? hsd_host::launch_pdl(meta::classify_kernel<true>, grid, dim3(256), 0, st,
+                                      "classify_kernel launch", 0u, S, P)
+               : hsd_host::launch_pdl(meta::classify_kernel<false>, grid, dim3(256), 0, st,
+                                      "classify_kernel launch", 0u, S, P);
   if (rc) return rc;
   return hsd_host::launch_pdl(meta::order_kernel, dim3(1), dim3(1024), 0, st,
                               "order_kernel launch", 0u, P);
