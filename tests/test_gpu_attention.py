@@ -136,6 +136,53 @@ def test_segment_plan_tree_single_none(dev):
     check_close(out, lse, q, k, v, allowed, None)
 
 
+@pytest.mark.parametrize("q_len,kv_old,seed", [(6000, 3000, 21), (4100, 9000, 22)])
+def test_segment_plan_many_tiles(dev, q_len, kv_old, seed):
+    """More query tiles than the ordering kernel has warps (each warp builds
+    several tiles' lists) and the classification spread over several parts
+    per tile: lists, classes, 128-column block list, tile order and prefix."""
+    from hsd_b200.plan import PackedMask
+    rng = np.random.default_rng(seed)
+    kv_len = kv_old + q_len
+    segs, qs = [], 0
+    while qs < q_len - 40:
+        ql = int(min(q_len - 40 - qs, rng.integers(1, 400)))
+        kind = [OM.CAUSAL, OM.SINGLE, OM.NONE][int(rng.integers(0, 3))] if ql > 1 else OM.SINGLE
+        kv = np.zeros(kv_len, bool)
+        kv[:int(rng.integers(0, kv_old))] = True
+        kv[rng.integers(0, kv_old + qs + 1, 20)] = True
+        segs.append(dict(q_start=qs, q_len=ql, kind=kind, kv=kv))
+        qs += ql
+    allowed = OM.segments_to_allowed(q_len, kv_len, segs)
+    pm = PackedMask(q_len, kv_len, segs, device=dev)
+    plan = pm.plan()
+    torch.cuda.synchronize()
+    plan.raise_on_device_error()
+    np.testing.assert_array_equal(plan.dense_allowed(), allowed)
+    cls = OB.tile_classes(allowed)
+    np.testing.assert_array_equal(plan.tile_class().cpu().numpy(), cls)
+    assert plan.block_mask_lists() == norm_lists(OB.block_mask_lists(allowed))
+    # 128-column blocks: present when either 64-column half is, flags per half
+    cnt, lst = (t.cpu().numpy() for t in plan.blocks())
+    nq, n64 = cls.shape
+    for t in range(nq):
+        want = []
+        for b in range((n64 + 1) // 2):
+            c0 = int(cls[t, 2 * b])
+            c1 = int(cls[t, 2 * b + 1]) if 2 * b + 1 < n64 else 0
+            if c0 or c1:
+                want.append(b | (int(c0 != 0) << 24) | (int(c0 == 1) << 25)
+                            | (int(c1 != 0) << 26) | (int(c1 == 1) << 27))
+        assert int(cnt[t]) == len(want), t
+        assert lst[t, :len(want)].astype(np.uint32).tolist() == want, t
+    # order: block count descending, ties by tile; prefix over that order
+    order = plan._view("tile_order", torch.int32, (nq,)).cpu().numpy()
+    prefix = plan._view("blk_prefix", torch.int32, (nq + 1,)).cpu().numpy()
+    want_order = sorted(range(nq), key=lambda t: (-int(cnt[t]), t))
+    assert order.tolist() == want_order
+    assert prefix.tolist() == np.concatenate([[0], np.cumsum(cnt[want_order])]).tolist()
+
+
 @pytest.mark.parametrize("name", ["cfg1", "step_gqa4", "masked_rows_mqa"])
 def test_attention_golden_cases(dev, name):
     q, k, v, mask, scale, _ = dict(C.attention_cases())[name]
