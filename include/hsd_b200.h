@@ -9,6 +9,14 @@
  * device memory (first error wins; NULL disables reporting); the host reads
  * it after its next synchronisation.  Every device pointer is caller-owned.
  *
+ * The kernels are launched with programmatic stream serialization: each
+ * waits for the previous work on the stream to complete before touching
+ * memory, then lets the next kernel be scheduled.  A caller's kernel that
+ * follows on the same stream with programmatic stream serialization of its
+ * own must wait for its predecessor (griddepcontrol.wait /
+ * cudaGridDependencySynchronize) before reading these kernels' outputs;
+ * ordinary launches, copies and events need nothing.
+ *
  * Reference interfaces replaced (paths inside whlscut/HSD):
  *   D  = hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py
  *   H  = hsd/hunyuan_ocr_pipeline/modeling_hunyuan_vl_hsd.py
