@@ -9,9 +9,11 @@
  * device memory (first error wins; NULL disables reporting); the host reads
  * it after its next synchronisation.  Every device pointer is caller-owned.
  *
- * The kernels are launched with programmatic stream serialization: each
- * waits for the previous work on the stream to complete before touching
- * memory, then lets the next kernel be scheduled.  A caller's kernel that
+ * The step's kernels (tile plan, attention, KV append, RoPE + cache update,
+ * acceptance + KMP, keep indices, compaction, bit remap) are launched with
+ * programmatic stream serialization: each waits for the previous work on the
+ * stream to complete before touching memory and lets the next kernel be
+ * scheduled early.  A caller's kernel that
  * follows on the same stream with programmatic stream serialization of its
  * own must wait for its predecessor (griddepcontrol.wait /
  * cudaGridDependencySynchronize) before reading these kernels' outputs;
