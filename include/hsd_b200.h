@@ -13,11 +13,10 @@
  * acceptance + KMP, keep indices, compaction, bit remap) are launched with
  * programmatic stream serialization: each waits for the previous work on the
  * stream to complete before touching memory and lets the next kernel be
- * scheduled early.  A caller's kernel that
- * follows on the same stream with programmatic stream serialization of its
- * own must wait for its predecessor (griddepcontrol.wait /
- * cudaGridDependencySynchronize) before reading these kernels' outputs;
- * ordinary launches, copies and events need nothing.
+ * scheduled early.  A caller's kernel that follows on the same stream with
+ * programmatic stream serialization of its own must wait for its predecessor
+ * (griddepcontrol.wait / cudaGridDependencySynchronize) before reading these
+ * kernels' outputs; ordinary launches, copies and events need nothing.
  *
  * Reference interfaces replaced (paths inside whlscut/HSD):
  *   D  = hsd/dots_ocr_pipeline/modeling_dots_ocr_hsd.py
